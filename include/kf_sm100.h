@@ -1,0 +1,133 @@
+/*
+ * kf_sm100.h -- C ABI of the B200 (sm_100a) layer-stack forward library.
+ *
+ * The library implements the hot path of the pre-norm Transformer stack of
+ * torch_transformer_benchmark.py (BaselineTransformer, :125-172) as four
+ * kernels: a fused residual-add + padding-mask + LayerNorm, a tcgen05 TF32
+ * GEMM with bias / bias+GELU(erf) epilogues, a key-padding bit packer and a
+ * tcgen05 TF32 FlashAttention forward with in-register causal and key-padding
+ * masks.
+ *
+ * Conventions shared by every entry point:
+ *   - all pointers are device pointers owned by the caller (the library never
+ *     allocates, frees or synchronises on the hot path; every call is
+ *     stream-ordered on `stream`, a cudaStream_t, and may be captured in a CUDA
+ *     graph);
+ *   - strides and leading dimensions are in ELEMENTS, not bytes;
+ *   - the return value is KF_OK (0) or a KF_E_* code; kf_last_error() gives the
+ *     message of the last failure on the calling thread;
+ *   - kernels that spin on barriers give up after a bounded time and record a
+ *     device status word, read back (with a device sync) by kf_device_status().
+ */
+#ifndef KF_SM100_H_
+#define KF_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KF_OK 0
+#define KF_E_INVALID 1     /* bad argument: null pointer, negative size, bad stride */
+#define KF_E_UNSUPPORTED 2 /* valid request outside what the kernels implement */
+#define KF_E_CUDA 3        /* a CUDA runtime / driver call failed */
+#define KF_E_NO_DEVICE 4   /* no sm_100 device is current */
+
+/* ----------------------------------------------------------- housekeeping */
+
+/* Library ABI version (major * 100 + minor). */
+int kf_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* kf_last_error(void);
+
+/* Reads the device-side status word of the current device (synchronises the
+ * device). 0 = no kernel has timed out on a barrier since the last reset;
+ * otherwise the code of the first failure. `reset` != 0 clears it. */
+int kf_device_status(int reset);
+
+/* ----------------------------------------------------------- LayerNorm */
+
+#define KF_LN_MASK_OUT 1   /* zero h on rows whose keep byte is 0 (final norm) */
+#define KF_LN_ROUND_TF32 2 /* round h to TF32 (it only feeds a TF32 GEMM) */
+
+/* Fused residual-add + row mask + LayerNorm over rows of width d:
+ *     s = keep[r] ? x[r] + y[r] : 0          (y optional, keep optional)
+ *     h = (s - mean(s)) / sqrt(var_biased(s) + eps) * w + b
+ *     h = (MASK_OUT && !keep[r]) ? 0 : h
+ * s_out is written when non-null. fp32 in and out.
+ * Replaces kernelforge/ops/layernorm.py:101-156 (add_mask_layernorm) and its
+ * Triton kernel _add_mask_ln_kernel (layernorm.py:40-86); semantics of
+ * torch_transformer_benchmark.py:128,140-144,169-171. */
+int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64_t ldy, const uint8_t* keep,
+                   const float* w, const float* b, float* s_out, int64_t lds, float* h_out,
+                   int64_t ldh, int64_t M, int64_t d, float eps, int flags, void* stream);
+
+/* ----------------------------------------------------------- GEMM */
+
+#define KF_EPI_BIAS 0      /* C = A W^T + bias */
+#define KF_EPI_BIAS_GELU 1 /* C = gelu_erf(A W^T + bias) */
+
+#define KF_GEMM_ROUND_TF32 1 /* round C to TF32 (it only feeds a TF32 MMA) */
+
+/* C[M,N] = epilogue(A[M,K] . W[N,K]^T + bias[N]) on tcgen05 TF32 tensor cores
+ * with an FP32 TMEM accumulator (nn.Linear layout: W row-major [N,K]).
+ * `bias` may be null. Requires K % 4 == 0, lda/ldw % 4 == 0 and 16-byte
+ * aligned A/W (TMA constraints). `bn` selects the N tile (0 = automatic,
+ * 64/128/256). When head_dim > 0, output column n is written to column
+ * (n / head_dim) * head_stride + n % head_dim of its row (used to zero-pad
+ * head_dim 8 to 16 for the attention MMA); columns never written keep their
+ * contents.
+ * Replaces the cuBLAS F.linear calls of kernelforge/optimized.py:441-446
+ * (FFN1 + F.gelu, FFN2), :483 (fused QKV) and :573 (out_proj). */
+int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t ldw, const float* bias,
+                 float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int flags,
+                 int bn, int head_dim, int head_stride, void* stream);
+
+/* ----------------------------------------------------------- attention */
+
+/* Words of the packed key-validity workspace for a [B, S] keep mask. */
+size_t kf_keep_bits_words(int64_t B, int64_t S);
+
+/* Pack a uint8 keep mask [B, S] (row stride ld_keep) into bits[B][ceil(S/32)]
+ * (bit k%32 of word k/32 = keep[b][k] != 0; bits past S are 0). This is the
+ * caller-owned workspace kf_flash_fwd_tf32 reads. */
+int kf_keep_bits(const uint8_t* keep, int64_t ld_keep, int64_t B, int64_t S, uint32_t* bits,
+                 void* stream);
+
+#define KF_ATTN_CAUSAL 1      /* mask keys after the query (triu(1) = -inf) */
+#define KF_ATTN_SKIP_EMPTY_Q 2 /* write 0 for query tiles with no valid query
+                                  (valid only when the caller masks those rows
+                                  afterwards, as the layer stack does) */
+#define KF_ATTN_ROUND_TF32 4  /* round O to TF32 (it only feeds a TF32 GEMM) */
+
+/* O = softmax(Q K^T * sm_scale + causal(-inf) + keypad(-inf)) V per (b, h),
+ * softmax in fp32, TF32 tensor-core contractions, FP32 accumulation in TMEM.
+ * Q/K/V/O are strided [B, H, S, Dh] views with unit stride on Dh and the
+ * other strides given as (batch, head, row) in elements (multiples of 4).
+ * `dh` is the stored head width of Q/K/V (16, 32, 64, 128 or 256), `dh_out`
+ * the number of O columns written (<= dh; dh_out < dh means Q/K/V carry
+ * zero padding up to dh). keep_bits may be null (no key mask) or a
+ * kf_keep_bits workspace. KV tiles without a valid key are skipped; a query
+ * row with no valid key yields 0, not NaN.
+ * Replaces kernelforge/ops/flash.py:363-422 (flash_attention) and its Triton
+ * kernel _flash_fwd_kernel (flash.py:41-249); semantics of
+ * torch_transformer_benchmark.py:97-112. */
+int kf_flash_fwd_tf32(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm, const float* k,
+                      int64_t k_sb, int64_t k_sh, int64_t k_sm, const float* v, int64_t v_sb,
+                      int64_t v_sh, int64_t v_sm, float* o, int64_t o_sb, int64_t o_sh,
+                      int64_t o_sm, const uint32_t* keep_bits, int64_t B, int64_t H, int64_t S,
+                      int dh, int dh_out, float sm_scale, int flags, void* stream);
+
+/* ----------------------------------------------------------- utilities */
+
+/* dst[i] = round_to_tf32(src[i]) for n fp32 values (weight preparation). */
+int kf_round_tf32(const float* src, float* dst, int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KF_SM100_H_ */

@@ -1,0 +1,566 @@
+// tcgen05 FlashAttention forward, TF32 contractions, causal + key-padding
+// masks applied in registers.
+//
+// One CTA = one (batch, head, 128-query tile). Warp roles:
+//   warp 0      TMA producer: Q once, then K and V tiles of BN keys through
+//               two independent smem rings (K released as soon as S = QK^T is
+//               done, V after O += PV);
+//   warp 1      MMA issuer and TMEM owner. TMEM holds two S buffers (BN fp32
+//               columns each) and the O accumulator (DH columns). S_j = Q K_j^T
+//               is issued one tile ahead of the softmax, and O += P_j V_j
+//               reads P straight from TMEM (tcgen05.mma A operand in TMEM), so
+//               P never touches shared memory;
+//   warps 2-5   softmax: one thread per query row (TMEM lane). Reads its S row,
+//               applies scale, causal and key-padding masks, updates the
+//               running max, writes P = exp2(S - m) back over S, and rescales
+//               its O row only when the max grew by more than 2^8 (the stale
+//               max cancels in O / l, so the result is unchanged). At the end
+//               it divides by l (0 for a row with no valid key) and stores O.
+//
+// KV tiles whose keys are all padding are skipped by every role (the three
+// roles walk the same list, derived from the packed key bits). With the
+// causal mask only tiles up to the diagonal are visited. V is consumed
+// MN-major straight from its [S, Dh] layout (no transpose copy), through the
+// 32-byte-atom swizzle that MN-major TF32 operands require.
+#include "kf_common.cuh"
+
+namespace kf {
+
+template <int DH, int BN, int KST, int VST>
+struct FlashCfg {
+  static constexpr int BM = 128;
+  static constexpr int RB = (DH * 4 < 128) ? DH * 4 : 128;  // bytes per swizzle row
+  static constexpr int CH = RB / 4;                          // fp32 elements per row chunk
+  static constexpr int NCH = DH / CH;                        // chunks along Dh
+  static constexpr uint32_t LAYOUT =
+      RB == 128 ? KF_SWIZZLE_128B : (RB == 64 ? KF_SWIZZLE_64B : KF_SWIZZLE_32B);
+  static constexpr int Q_BYTES = BM * DH * 4;
+  static constexpr int KV_BYTES = BN * DH * 4;  // one K tile
+  // V is read MN-major (Dh contiguous). For 32-bit elements the only MN-major
+  // shared-memory layout the tensor core accepts is 128-byte rows with a
+  // 32-byte-granule swizzle (descriptor layout SWIZZLE_128B_BASE32B, 4-row
+  // atoms), which TMA writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B. Rows
+  // are 32 elements wide; DH = 16 uses half a row (the rest is zero fill).
+  static constexpr int VCH = (DH + 31) / 32;
+  static constexpr int V_BYTES = BN * 128 * VCH;  // one V tile
+  static constexpr int K_OFF = Q_BYTES;
+  static constexpr int V_OFF = K_OFF + KST * KV_BYTES;
+  static constexpr int BAR_OFF = V_OFF + VST * V_BYTES;
+  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int O_COL = 2 * BN;
+  static_assert(DH >= 16 && DH <= 256 && (DH & (DH - 1)) == 0, "DH");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "BN");
+  static_assert(2 * BN + DH <= 512, "TMEM");
+  static_assert(SMEM_BYTES <= 232448, "smem");
+};
+
+// Does KV tile j (keys [j*BN, j*BN+BN)) hold at least one valid key?
+template <int BN>
+__device__ __forceinline__ bool kv_tile_live(const uint32_t* __restrict__ bits_b, int words, int j,
+                                             int S) {
+  const int k0 = j * BN;
+  if (k0 >= S) return false;
+  if (!bits_b) return true;
+  const int w0 = k0 >> 5;
+  uint32_t any = 0;
+#pragma unroll
+  for (int w = 0; w < BN / 32; ++w)
+    if (w0 + w < words) any |= __ldg(bits_b + w0 + w);
+  return any != 0;
+}
+
+template <int DH, int BN, int KST, int VST>
+__global__ void __launch_bounds__(192, 1)
+    flash_fwd_tf32_kernel(const __grid_constant__ CUtensorMap tmQ,
+                          const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, float* __restrict__ O,
+                          int64_t o_sb, int64_t o_sh, int64_t o_sm,
+                          const uint32_t* __restrict__ keep_bits, int H, int S, int dh_out,
+                          float scale_log2, int flags) {
+  using Cfg = FlashCfg<DH, BN, KST, VST>;
+  constexpr int BM = Cfg::BM;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + Cfg::K_OFF;
+  uint8_t* sV = smem + Cfg::V_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + KST;
+  uint64_t* v_full = k_empty + KST;
+  uint64_t* v_empty = v_full + VST;
+  uint64_t* s_full = v_empty + VST;  // [2]
+  uint64_t* p_full = s_full + 2;     // [2]
+  uint64_t* o_done = p_full + 2;
+  uint64_t* o_final = o_done + 1;
+  uint64_t* drain = o_final + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int b = bh / H;
+  const int h = bh % H;
+  const int n_qt = gridDim.y;
+  const int qt = n_qt - 1 - static_cast<int>(blockIdx.y);  // heaviest causal tiles first
+  const int q0 = qt * BM;
+  const bool causal = (flags & KF_ATTN_CAUSAL) != 0;
+  const int words = (S + 31) >> 5;
+  const uint32_t* bits_b = keep_bits ? keep_bits + static_cast<int64_t>(b) * words : nullptr;
+
+  // Optional skip of a query tile without any valid query (rows later masked).
+  if ((flags & KF_ATTN_SKIP_EMPTY_Q) && bits_b) {
+    uint32_t any = 0;
+    for (int w = q0 >> 5; w < ((q0 + BM) >> 5) && w < words; ++w) any |= __ldg(bits_b + w);
+    if (!any) {
+      if (warp >= 2) {
+        const int r = (warp & 3) * 32 + lane;
+        const int qi = q0 + r;
+        if (qi < S) {
+          float* orow = O + static_cast<int64_t>(b) * o_sb + static_cast<int64_t>(h) * o_sh +
+                        static_cast<int64_t>(qi) * o_sm;
+          for (int c = 0; c < dh_out; ++c) orow[c] = 0.f;
+        }
+      }
+      return;
+    }
+  }
+
+  const int n_kv_all = (S + BN - 1) / BN;
+  int kv_end = n_kv_all;
+  if (causal) {
+    const int last_q = (q0 + BM - 1 < S - 1) ? q0 + BM - 1 : S - 1;
+    const int lim = last_q / BN + 1;
+    kv_end = lim < kv_end ? lim : kv_end;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < KST; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < VST; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], 4);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(o_final, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      mbar_arrive_expect_tx(q_full, Cfg::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < Cfg::NCH; ++c)
+        tma_load_4d(sQ + c * BM * Cfg::RB, &tmQ, q_full, c * Cfg::CH, q0, h, b);
+      int ks = 0, vs = 0;
+      uint32_t kph = 0, vph = 0;
+      long long k_issued = 0, v_issued = 0;
+      bool ok = true;
+      for (int j = 0; j < kv_end && ok; ++j) {
+        if (!kv_tile_live<BN>(bits_b, words, j, S)) continue;
+        if (!mbar_wait(&k_empty[ks], kph ^ 1u, abort_flag, KF_DEV_WAIT_TIMEOUT_TMA)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[ks], Cfg::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < Cfg::NCH; ++c)
+          tma_load_4d(sK + ks * Cfg::KV_BYTES + c * BN * Cfg::RB, &tmK, &k_full[ks], c * Cfg::CH,
+                      j * BN, h, b);
+        ++k_issued;
+        if (++ks == KST) {
+          ks = 0;
+          kph ^= 1u;
+        }
+        if (!mbar_wait(&v_empty[vs], vph ^ 1u, abort_flag, KF_DEV_WAIT_TIMEOUT_TMA)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[vs], Cfg::V_BYTES);
+#pragma unroll
+        for (int c = 0; c < Cfg::VCH; ++c)
+          tma_load_4d(sV + vs * Cfg::V_BYTES + c * BN * 128, &tmV, &v_full[vs], c * 32, j * BN, h,
+                      b);
+        ++v_issued;
+        if (++vs == VST) {
+          vs = 0;
+          vph ^= 1u;
+        }
+      }
+      if (!ok) {
+        mbar_wait_drain(q_full, 0, KF_DEV_WAIT_TIMEOUT_TMA);
+        for (long long i = (k_issued > KST ? k_issued - KST : 0); i < k_issued; ++i)
+          mbar_wait_drain(&k_full[i % KST], static_cast<uint32_t>((i / KST) & 1),
+                            KF_DEV_WAIT_TIMEOUT_TMA);
+        for (long long i = (v_issued > VST ? v_issued - VST : 0); i < v_issued; ++i)
+          mbar_wait_drain(&v_full[i % VST], static_cast<uint32_t>((i / VST) & 1),
+                            KF_DEV_WAIT_TIMEOUT_TMA);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc_s = make_idesc_tf32(BM, BN, 0, 0);
+      constexpr uint32_t idesc_o = make_idesc_tf32(BM, DH, 0, 1);
+      const uint32_t sQa = smem_u32(sQ);
+      const uint32_t sKa = smem_u32(sK);
+      const uint32_t sVa = smem_u32(sV);
+      int ks = 0, vs = 0;
+      uint32_t kph = 0, vph = 0;
+      bool ok = mbar_wait(q_full, 0, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA);
+      int it = 0;
+      auto issue_pv = [&](int i) -> bool {
+        const int sb = i & 1;
+        if (!mbar_wait(&p_full[sb], static_cast<uint32_t>((i >> 1) & 1), abort_flag,
+                       KF_DEV_WAIT_TIMEOUT_MMA))
+          return false;
+        if (!mbar_wait(&v_full[vs], vph, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA)) return false;
+        tc_fence_after();
+        const uint32_t vbase = sVa + vs * Cfg::V_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BN / 8; ++kk) {
+          // 8 keys = 8 rows of 128 bytes; LBO = next 32-wide Dh chunk,
+          // SBO = next 4-row swizzle atom.
+          const uint64_t bd =
+              make_smem_desc(vbase + kk * 8 * 128, BN * 128, 4 * 128, KF_SWIZZLE_128B_BASE32B);
+          mma_tf32_ts(tmem_base + Cfg::O_COL, tmem_base + sb * BN + kk * 8, bd, idesc_o,
+                      (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&v_empty[vs]);
+        mma_commit(o_done);
+        if (++vs == VST) {
+          vs = 0;
+          vph ^= 1u;
+        }
+        return true;
+      };
+      for (int j = 0; j < kv_end && ok; ++j) {
+        if (!kv_tile_live<BN>(bits_b, words, j, S)) continue;
+        if (!mbar_wait(&k_full[ks], kph, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int sb = it & 1;
+        const uint32_t kbase = sKa + ks * Cfg::KV_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < DH / 8; ++kk) {
+          const int chunk = kk / (Cfg::CH / 8);
+          const int within = kk % (Cfg::CH / 8);
+          const uint64_t ad = make_smem_desc(sQa + chunk * BM * Cfg::RB + within * 32, 16,
+                                             8 * Cfg::RB, Cfg::LAYOUT);
+          const uint64_t bd = make_smem_desc(kbase + chunk * BN * Cfg::RB + within * 32, 16,
+                                             8 * Cfg::RB, Cfg::LAYOUT);
+          mma_tf32_ss(tmem_base + sb * BN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&k_empty[ks]);
+        mma_commit(&s_full[sb]);
+        if (++ks == KST) {
+          ks = 0;
+          kph ^= 1u;
+        }
+        if (it > 0 && !issue_pv(it - 1)) {
+          ok = false;
+          break;
+        }
+        ++it;
+      }
+      if (ok && it > 0 && issue_pv(it - 1)) mma_commit(o_final);
+      mma_commit(drain);
+      mbar_wait_drain(drain, 0, KF_DEV_WAIT_TIMEOUT_MMA);
+    }
+  } else {
+    // -------------------------------------------------- softmax (warps 2..5)
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int qi = q0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t t_row = tmem_base + lane_off;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    int it = 0;
+    bool ok = true;
+    for (int j = 0; j < kv_end; ++j) {
+      if (!kv_tile_live<BN>(bits_b, words, j, S)) continue;
+      const int sb = it & 1;
+      if (!mbar_wait(&s_full[sb], static_cast<uint32_t>((it >> 1) & 1), abort_flag,
+                     KF_DEV_WAIT_TIMEOUT_SOFTMAX)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+        tmem_ld32(t_row + sb * BN + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+
+      const int k0 = j * BN;
+      uint32_t kw[BN / 32];
+      bool all_keys = (k0 + BN <= S);
+#pragma unroll
+      for (int w = 0; w < BN / 32; ++w) {
+        const int wi = (k0 >> 5) + w;
+        kw[w] = bits_b ? (wi < words ? __ldg(bits_b + wi) : 0u) : 0xffffffffu;
+        all_keys = all_keys && (kw[w] == 0xffffffffu);
+      }
+      const bool diag = causal && (k0 + BN - 1 > q0);
+      float mx = -INFINITY;
+      if (all_keys && !diag) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          s[c] *= scale_log2;
+          mx = fmaxf(mx, s[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          const int kidx = k0 + c;
+          const bool valid = ((kw[c >> 5] >> (c & 31)) & 1u) && (kidx < S) && (!causal || kidx <= qi);
+          s[c] = valid ? s[c] * scale_log2 : -INFINITY;
+          mx = fmaxf(mx, s[c]);
+        }
+      }
+      // Running max with lazy rescale: keep the old reference unless the new
+      // max exceeds it by more than 8 (P stays <= 256 in fp32).
+      float alpha = 1.f;
+      bool rescale_o = false;
+      if (mx > m_run + 8.f) {
+        if (m_run != -INFINITY) {
+          alpha = fast_exp2(m_run - mx);
+          l_run *= alpha;
+          rescale_o = (it > 0);
+        }
+        m_run = mx;
+      }
+      const float m_ref = (m_run == -INFINITY) ? 0.f : m_run;
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        const float p = round_tf32(fast_exp2(s[c] - m_ref));
+        s[c] = p;
+        sum += p;
+      }
+      l_run += sum;
+      if (__any_sync(0xffffffffu, rescale_o)) {
+        // O += P_{it-1} V_{it-1} must have landed before this row is rescaled.
+        // The s_full arrival just observed implies PV_{it-2} is complete (the
+        // MMA pipe completes in issue order and S_it was issued after it), so
+        // o_done is at most one phase behind and the parity wait is exact.
+        if (!mbar_wait(o_done, static_cast<uint32_t>((it - 1) & 1), abort_flag,
+                       KF_DEV_WAIT_TIMEOUT_SOFTMAX)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // DH == 16 uses one 32-column access: the 16 columns past O are
+        // unused TMEM, so scaling them is harmless.
+#pragma unroll
+        for (int c = 0; c < (DH + 31) / 32; ++c) {
+          float o[32];
+          tmem_ld32(t_row + Cfg::O_COL + c * 32, o);
+#pragma unroll
+          for (int t = 0; t < 32; ++t) o[t] *= alpha;
+          tmem_st32(t_row + Cfg::O_COL + c * 32, o);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+        tmem_st32(t_row + sb * BN + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[sb]);
+      ++it;
+    }
+    if (ok) {
+      float* orow = O + static_cast<int64_t>(b) * o_sb + static_cast<int64_t>(h) * o_sh +
+                    static_cast<int64_t>(qi) * o_sm;
+      const bool rnd = (flags & KF_ATTN_ROUND_TF32) != 0;
+      if (it > 0) {
+        // o_final (one phase) rather than o_done: by now o_done may be two
+        // phases behind, where a parity wait cannot tell the phases apart.
+        if (mbar_wait(o_final, 0, abort_flag, KF_DEV_WAIT_TIMEOUT_SOFTMAX)) {
+          tc_fence_after();
+          const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll 1
+          for (int c = 0; c < (DH + 31) / 32; ++c) {
+            float o[32];
+            tmem_ld32(t_row + Cfg::O_COL + c * 32, o);
+            if (qi < S) {
+#pragma unroll
+              for (int t = 0; t < 32; t += 4) {
+                const int col = c * 32 + t;
+                if (col < dh_out) {
+                  float4 v4 = make_float4(o[t] * inv_l, o[t + 1] * inv_l, o[t + 2] * inv_l,
+                                          o[t + 3] * inv_l);
+                  if (rnd) {
+                    v4.x = round_tf32(v4.x);
+                    v4.y = round_tf32(v4.y);
+                    v4.z = round_tf32(v4.z);
+                    v4.w = round_tf32(v4.w);
+                  }
+                  if (col + 3 < dh_out && (flags & (1 << 8))) {
+                    *reinterpret_cast<float4*>(orow + col) = v4;
+                  } else {
+                    const float tmp[4] = {v4.x, v4.y, v4.z, v4.w};
+                    for (int u = 0; u < 4 && col + u < dh_out; ++u) orow[col + u] = tmp[u];
+                  }
+                }
+              }
+            }
+          }
+        }
+      } else if (qi < S) {
+        for (int c = 0; c < dh_out; ++c) orow[c] = 0.f;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+template <int DH, int BN, int KST, int VST>
+static int launch_flash(const float* q, const int64_t* qs, const float* k, const int64_t* ks,
+                        const float* v, const int64_t* vs, float* o, const int64_t* os,
+                        const uint32_t* bits, int B, int H, int S, int dh_stored, int dh_out,
+                        float scale_log2, int flags, cudaStream_t st) {
+  using Cfg = FlashCfg<DH, BN, KST, VST>;
+  CUtensorMap tq, tk, tv;
+  const uint64_t dims[4] = {static_cast<uint64_t>(dh_stored), static_cast<uint64_t>(S),
+                            static_cast<uint64_t>(H), static_cast<uint64_t>(B)};
+  auto enc = [&](CUtensorMap* m, const float* base, const int64_t* s, uint32_t rows) {
+    // strides (in bytes) of dims 1..3 = row, head, batch
+    const uint64_t str[3] = {static_cast<uint64_t>(s[2]) * 4, static_cast<uint64_t>(s[1]) * 4,
+                             static_cast<uint64_t>(s[0]) * 4};
+    const uint32_t box[4] = {static_cast<uint32_t>(Cfg::CH), rows, 1, 1};
+    const CUtensorMapSwizzle sw = Cfg::RB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : Cfg::RB == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                  : CU_TENSOR_MAP_SWIZZLE_32B;
+    return encode_tensor_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, str, box, sw);
+  };
+  int rc = enc(&tq, q, qs, Cfg::BM);
+  if (!rc) rc = enc(&tk, k, ks, BN);
+  if (!rc) {
+    const uint64_t str[3] = {static_cast<uint64_t>(vs[2]) * 4, static_cast<uint64_t>(vs[1]) * 4,
+                             static_cast<uint64_t>(vs[0]) * 4};
+    const uint32_t box[4] = {32, static_cast<uint32_t>(BN), 1, 1};
+    rc = encode_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, v, dims, str, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  }
+  if (rc) return rc;
+
+  auto kern = flash_fwd_tf32_kernel<DH, BN, KST, VST>;
+  static int attr_set[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!attr_set[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_status(e, "kf_flash_fwd_tf32: set smem attribute");
+    attr_set[dev] = 1;
+  }
+  const int n_qt = (S + Cfg::BM - 1) / Cfg::BM;
+  dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>(n_qt));
+  kern<<<grid, 192, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, o, os[0], os[1], os[2], bits, H, S,
+                                             dh_out, scale_log2, flags);
+  return cuda_status(cudaGetLastError(), "kf_flash_fwd_tf32 launch");
+}
+
+}  // namespace kf
+
+using namespace kf;
+
+extern "C" int kf_flash_fwd_tf32(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
+                                 const float* k, int64_t k_sb, int64_t k_sh, int64_t k_sm,
+                                 const float* v, int64_t v_sb, int64_t v_sh, int64_t v_sm,
+                                 float* o, int64_t o_sb, int64_t o_sh, int64_t o_sm,
+                                 const uint32_t* keep_bits, int64_t B, int64_t H, int64_t S,
+                                 int dh, int dh_out, float sm_scale, int flags, void* stream) {
+  if (!q || !k || !v || !o || B < 0 || H < 0 || S < 0) {
+    set_last_error("kf_flash_fwd_tf32: invalid arguments");
+    return KF_E_INVALID;
+  }
+  if (B == 0 || H == 0 || S == 0) return KF_OK;
+  if (dh != 16 && dh != 32 && dh != 64 && dh != 128 && dh != 256) {
+    set_last_error("kf_flash_fwd_tf32: stored head_dim %d not in {16,32,64,128,256}", dh);
+    return KF_E_UNSUPPORTED;
+  }
+  if (dh_out <= 0 || dh_out > dh) {
+    set_last_error("kf_flash_fwd_tf32: dh_out %d must be in [1, %d]", dh_out, dh);
+    return KF_E_INVALID;
+  }
+  const int64_t strides[9] = {q_sb, q_sh, q_sm, k_sb, k_sh, k_sm, v_sb, v_sh, v_sm};
+  for (int i = 0; i < 9; ++i) {
+    if (strides[i] <= 0 || strides[i] % 4) {
+      set_last_error("kf_flash_fwd_tf32: Q/K/V strides must be positive multiples of 4");
+      return KF_E_UNSUPPORTED;
+    }
+  }
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+       reinterpret_cast<uintptr_t>(v)) &
+      15u) {
+    set_last_error("kf_flash_fwd_tf32: Q/K/V must be 16-byte aligned");
+    return KF_E_UNSUPPORTED;
+  }
+  if (B * H > INT32_MAX || S > (int64_t)65535 * 128 || S > INT32_MAX) {
+    set_last_error("kf_flash_fwd_tf32: B*H or S too large");
+    return KF_E_UNSUPPORTED;
+  }
+  int f = flags & (KF_ATTN_CAUSAL | KF_ATTN_SKIP_EMPTY_Q | KF_ATTN_ROUND_TF32);
+  if ((o_sm % 4 == 0) && !(reinterpret_cast<uintptr_t>(o) & 15u) && o_sb % 4 == 0 &&
+      o_sh % 4 == 0)
+    f |= (1 << 8);
+  const float scale_log2 = sm_scale * 1.4426950408889634f;
+  const int64_t qs[3] = {q_sb, q_sh, q_sm}, ks[3] = {k_sb, k_sh, k_sm},
+                vs[3] = {v_sb, v_sh, v_sm}, os[3] = {o_sb, o_sh, o_sm};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int Bi = static_cast<int>(B), Hi = static_cast<int>(H), Si = static_cast<int>(S);
+  switch (dh) {
+    case 16:
+      return launch_flash<16, 128, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+                                         dh_out, scale_log2, f, st);
+    case 32:
+      return launch_flash<32, 128, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+                                         dh_out, scale_log2, f, st);
+    case 64:
+      return launch_flash<64, 128, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+                                         dh_out, scale_log2, f, st);
+    case 128:
+      return launch_flash<128, 64, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+                                         dh_out, scale_log2, f, st);
+    default:
+      return launch_flash<256, 32, 2, 1>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+                                         dh_out, scale_log2, f, st);
+  }
+}

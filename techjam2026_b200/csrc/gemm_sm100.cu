@@ -1,0 +1,383 @@
+// tcgen05 TF32 GEMM with fused epilogues:  C = epi(A . W^T + bias)
+//
+// A [M,K] and W [N,K] are both K-major (nn.Linear layout), fp32 in HBM, fed to
+// the tensor core as TF32. The kernel is persistent (one CTA per SM, static
+// round-robin over 128 x BN output tiles, N-fastest so the CTAs running at one
+// time share the same A rows in L2) and warp-specialised:
+//
+//   warp 0      TMA producer: one elected thread streams 128x32 A and BNx32 W
+//               boxes (128-byte rows, 128B swizzle) into a STAGES-deep smem
+//               ring, completion tracked by mbarrier transaction counts;
+//   warp 1      MMA issuer: allocates TMEM (two BN-column accumulators), one
+//               thread issues 4 tcgen05.mma (K = 8 each) per 32-wide k block
+//               and releases the smem stage with tcgen05.commit;
+//   warps 2-5   epilogue: tcgen05.ld the accumulator of a finished tile (warp w
+//               owns TMEM lanes 32*(w%4)..+31 = 32 output rows), add bias,
+//               optionally GELU(erf) and TF32 rounding, store fp32 to HBM,
+//               then hand the accumulator back to the MMA warp. Double
+//               buffering lets the epilogue of tile i overlap the main loop of
+//               tile i+1.
+#include "kf_common.cuh"
+
+namespace kf {
+
+enum : int { KF_GEMM_VEC_OK = 1 << 8 };
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 32;  // 32 fp32 = 128 bytes = one swizzle row
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(SMEM_BYTES <= 232448, "smem");
+};
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.f + erff(x * 0.70710678118654752440f));
+}
+
+template <int EPI>
+__device__ __forceinline__ void gemm_store_chunk(const float (&v)[32], float* __restrict__ crow,
+                                                 const float* __restrict__ bias, int col0, int N,
+                                                 int flags, int hd, int hs) {
+  const bool rnd = (flags & KF_GEMM_ROUND_TF32) != 0;
+  const bool vec = (flags & KF_GEMM_VEC_OK) != 0;
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const int col = col0 + j;
+    if (col >= N) break;
+    if (vec && col + 3 < N) {
+      float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (bias) bb = __ldg(reinterpret_cast<const float4*>(bias + col));
+      float4 o = make_float4(v[j] + bb.x, v[j + 1] + bb.y, v[j + 2] + bb.z, v[j + 3] + bb.w);
+      if (EPI == KF_EPI_BIAS_GELU) {
+        o.x = gelu_erf(o.x);
+        o.y = gelu_erf(o.y);
+        o.z = gelu_erf(o.z);
+        o.w = gelu_erf(o.w);
+      }
+      if (rnd) {
+        o.x = round_tf32(o.x);
+        o.y = round_tf32(o.y);
+        o.z = round_tf32(o.z);
+        o.w = round_tf32(o.w);
+      }
+      const int dst = hd ? (col / hd) * hs + (col % hd) : col;
+      *reinterpret_cast<float4*>(crow + dst) = o;
+    } else {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int cc = col + t;
+        if (cc < N) {
+          float o = v[j + t] + (bias ? __ldg(bias + cc) : 0.f);
+          if (EPI == KF_EPI_BIAS_GELU) o = gelu_erf(o);
+          if (rnd) o = round_tf32(o);
+          const int dst = hd ? (cc / hd) * hs + (cc % hd) : cc;
+          crow[dst] = o;
+        }
+      }
+    }
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int M,
+                     int N, int K, int flags, int head_dim, int head_stride) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / num_n) * BM;
+        const int n0 = (tile % num_n) * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, KF_DEV_WAIT_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
+          tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full[stage], kb * BK, n0);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: wait for the loads still in flight (the last <= STAGES).
+        const long long first = issued > STAGES ? issued - STAGES : 0;
+        for (long long i = first; i < issued; ++i)
+          mbar_wait_drain(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1),
+                          KF_DEV_WAIT_TIMEOUT_TMA);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = make_idesc_tf32(BM, BN, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            const uint64_t ad = make_smem_desc(a_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+            const uint64_t bd = make_smem_desc(b_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+            mma_tf32_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Every MMA this thread issued completes before TMEM is released.
+      mma_commit(drain);
+      mbar_wait_drain(drain, 0, KF_DEV_WAIT_TIMEOUT_MMA);
+    }
+  } else {
+    // -------------------------------------------------- epilogue (warps 2..5)
+    const int quarter = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m0 = (tile / num_n) * BM;
+      const int n0 = (tile % num_n) * BN;
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, KF_DEV_WAIT_TIMEOUT_EPI)) break;
+      tc_fence_after();
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      float* crow = C + static_cast<int64_t>(row) * ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        if (n0 + c >= N) break;  // warp-uniform
+        float v[32];
+        tmem_ld32(tbase + static_cast<uint32_t>(c), v);
+        if (row < M) gemm_store_chunk<EPI>(v, crow, bias, n0 + c, N, flags, head_dim, head_stride);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+template <int BN, int EPI>
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, float* C, int64_t ldc,
+                       const float* bias, int M, int N, int K, int flags, int hd, int hs,
+                       cudaStream_t st) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tf32_kernel<BN, EPI>;
+  static int attr_set[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!attr_set[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_status(e, "kf_gemm_tf32: set smem attribute");
+    attr_set[dev] = 1;
+  }
+  const int tiles = ((M + Cfg::BM - 1) / Cfg::BM) * ((N + BN - 1) / BN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kern<<<grid, 192, Cfg::SMEM_BYTES, st>>>(ta, tb, C, ldc, bias, M, N, K, flags, hd, hs);
+  return cuda_status(cudaGetLastError(), "kf_gemm_tf32 launch");
+}
+
+// Pick the N tile that minimises (waves x per-tile cost) on this GPU.
+static int choose_bn(int64_t M, int64_t N) {
+  const int sms = sm_count();
+  const int64_t mt = (M + 127) / 128;
+  int best = 128;
+  double best_cost = 1e30;
+  const int cands[3] = {256, 128, 64};
+  for (int i = 0; i < 3; ++i) {
+    const int bn = cands[i];
+    const int64_t tiles = mt * ((N + bn - 1) / bn);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const double cost = static_cast<double>(waves) * (bn + 32);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+}  // namespace kf
+
+using namespace kf;
+
+extern "C" int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t ldw,
+                            const float* bias, float* C, int64_t ldc, int64_t M, int64_t N,
+                            int64_t K, int epilogue, int flags, int bn, int head_dim,
+                            int head_stride, void* stream) {
+  if (!A || !W || !C || M < 0 || N < 0 || K < 0) {
+    set_last_error("kf_gemm_tf32: invalid arguments");
+    return KF_E_INVALID;
+  }
+  if (M == 0 || N == 0) return KF_OK;
+  if (K == 0 || K % 4 || lda % 4 || ldw % 4 || lda < K || ldw < K ||
+      (reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(W) & 15u)) {
+    set_last_error(
+        "kf_gemm_tf32: TMA needs K %% 4 == 0, lda/ldw %% 4 == 0, lda/ldw >= K and 16-byte "
+        "aligned A/W (K=%lld lda=%lld ldw=%lld)",
+        (long long)K, (long long)lda, (long long)ldw);
+    return KF_E_UNSUPPORTED;
+  }
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) {
+    set_last_error("kf_gemm_tf32: dimensions beyond 2^31");
+    return KF_E_UNSUPPORTED;
+  }
+  if (epilogue != KF_EPI_BIAS && epilogue != KF_EPI_BIAS_GELU) {
+    set_last_error("kf_gemm_tf32: unknown epilogue %d", epilogue);
+    return KF_E_INVALID;
+  }
+  if (head_dim < 0 || (head_dim > 0 && head_stride < head_dim)) {
+    set_last_error("kf_gemm_tf32: head_stride must be >= head_dim");
+    return KF_E_INVALID;
+  }
+  const int64_t out_cols = head_dim > 0 ? ((N + head_dim - 1) / head_dim) * head_stride : N;
+  if (ldc < out_cols && M > 1) {
+    set_last_error("kf_gemm_tf32: ldc %lld smaller than the output row", (long long)ldc);
+    return KF_E_INVALID;
+  }
+  if (bn == 0) bn = choose_bn(M, N);
+  if (bn != 64 && bn != 128 && bn != 256) {
+    set_last_error("kf_gemm_tf32: bn must be 0, 64, 128 or 256");
+    return KF_E_INVALID;
+  }
+
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 4};
+    const uint32_t box[2] = {32, 128};
+    int rc = encode_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, A, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldw) * 4};
+    const uint32_t box[2] = {32, static_cast<uint32_t>(bn)};
+    int rc = encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, W, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+
+  int f = flags & KF_GEMM_ROUND_TF32;
+  const bool vec = (ldc % 4 == 0) && !(reinterpret_cast<uintptr_t>(C) & 15u) &&
+                   !(reinterpret_cast<uintptr_t>(bias) & 15u) &&
+                   (head_dim == 0 || (head_dim % 4 == 0 && head_stride % 4 == 0));
+  if (vec) f |= KF_GEMM_VEC_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
+#define KF_GEMM_CASE(BNV)                                                                   \
+  if (bn == BNV) {                                                                          \
+    if (epilogue == KF_EPI_BIAS)                                                            \
+      return launch_gemm<BNV, KF_EPI_BIAS>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,      \
+                                           head_stride, st);                                \
+    return launch_gemm<BNV, KF_EPI_BIAS_GELU>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,   \
+                                              head_stride, st);                             \
+  }
+  KF_GEMM_CASE(64)
+  KF_GEMM_CASE(128)
+  KF_GEMM_CASE(256)
+#undef KF_GEMM_CASE
+  return KF_E_INVALID;
+}

@@ -1,0 +1,161 @@
+// Host runtime of the C ABI: error reporting, device status word, tensor-map
+// encoding through the driver entry point, and two small utility kernels
+// (key-padding bit packing, TF32 rounding).
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "kf_common.cuh"
+
+namespace kf {
+
+static thread_local char t_last_error[512] = {0};
+
+void set_last_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int cuda_status(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return KF_OK;
+  set_last_error("%s: %s (%s)", where, cudaGetErrorString(e), cudaGetErrorName(e));
+  return KF_E_CUDA;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,
+                      const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                      CUtensorMapSwizzle swizzle) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode) {
+    set_last_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return KF_E_CUDA;
+  }
+  cuuint64_t gdim[5];
+  cuuint64_t gstride[4];
+  cuuint32_t bdim[5];
+  cuuint32_t estride[5];
+  for (uint32_t i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bdim[i] = box[i];
+    estride[i] = 1;
+    if (i + 1 < rank) gstride[i] = strides_bytes[i];
+  }
+  CUresult r = g_encode(map, dtype, rank, const_cast<void*>(base), gdim, gstride, bdim, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("cuTensorMapEncodeTiled failed (CUresult %d, rank %u)", static_cast<int>(r),
+                   rank);
+    return KF_E_CUDA;
+  }
+  return KF_OK;
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+// ---------------------------------------------------------------- kernels
+
+// One warp per 32 keys: ballot of keep != 0 (and k < S).
+__global__ void keep_bits_kernel(const uint8_t* __restrict__ keep, int64_t ld_keep, int64_t B,
+                                 int64_t S, uint32_t* __restrict__ bits) {
+  const int64_t words = (S + 31) / 32;
+  const int64_t warp_global = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (warp_global >= B * words) return;
+  const int64_t b = warp_global / words;
+  const int64_t w = warp_global % words;
+  const int64_t k = w * 32 + lane;
+  const bool valid = (k < S) && keep[b * ld_keep + k] != 0;
+  const uint32_t m = __ballot_sync(0xffffffffu, valid);
+  if (lane == 0) bits[warp_global] = m;
+}
+
+__global__ void round_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst,
+                                  int64_t n) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += stride)
+    dst[i] = round_tf32(src[i]);
+}
+
+}  // namespace kf
+
+using namespace kf;
+
+extern "C" int kf_version(void) { return 100; }
+
+extern "C" const char* kf_last_error(void) { return t_last_error; }
+
+extern "C" int kf_device_status(int reset) {
+  int v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return -cuda_status(e, "kf_device_status: synchronize");
+  e = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int));
+  if (e != cudaSuccess) return -cuda_status(e, "kf_device_status: read");
+  if (reset) {
+    int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return -cuda_status(e, "kf_device_status: reset");
+  }
+  return v;
+}
+
+extern "C" size_t kf_keep_bits_words(int64_t B, int64_t S) {
+  if (B <= 0 || S <= 0) return 0;
+  return static_cast<size_t>(B) * static_cast<size_t>((S + 31) / 32);
+}
+
+extern "C" int kf_keep_bits(const uint8_t* keep, int64_t ld_keep, int64_t B, int64_t S,
+                            uint32_t* bits, void* stream) {
+  if (!keep || !bits || B <= 0 || S <= 0 || ld_keep < S) {
+    set_last_error("kf_keep_bits: invalid arguments (B=%lld S=%lld ld=%lld)", (long long)B,
+                   (long long)S, (long long)ld_keep);
+    return KF_E_INVALID;
+  }
+  const int64_t warps = B * ((S + 31) / 32);
+  const int threads = 256;
+  const int64_t blocks = (warps * 32 + threads - 1) / threads;
+  keep_bits_kernel<<<static_cast<unsigned>(blocks), threads, 0,
+                     static_cast<cudaStream_t>(stream)>>>(keep, ld_keep, B, S, bits);
+  return cuda_status(cudaGetLastError(), "kf_keep_bits launch");
+}
+
+extern "C" int kf_round_tf32(const float* src, float* dst, int64_t n, void* stream) {
+  if (!src || !dst || n < 0) {
+    set_last_error("kf_round_tf32: invalid arguments");
+    return KF_E_INVALID;
+  }
+  if (n == 0) return KF_OK;
+  const int threads = 256;
+  int64_t blocks = (n + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  round_tf32_kernel<<<static_cast<unsigned>(blocks), threads, 0,
+                      static_cast<cudaStream_t>(stream)>>>(src, dst, n);
+  return cuda_status(cudaGetLastError(), "kf_round_tf32 launch");
+}

@@ -1,0 +1,193 @@
+// Fused residual-add + padding-mask + LayerNorm (one pass over HBM).
+//
+//   s = keep[r] ? x[r] + y[r] : 0
+//   h = (s - mean) * rsqrt(var_biased + eps) * w + b      (LN of a zero row = b)
+//   h = (MASK_OUT && !keep[r]) ? 0 : h
+//
+// The row mask is a select, not a multiply, so a padded row is exactly 0 even
+// if its inputs hold non-finite values (masked_fill semantics of
+// torch_transformer_benchmark.py:120-121, 143-144, 170-171).
+//
+// x and s_out may alias (the residual stream is updated in place): every
+// element is read by the thread that later writes it, so no restrict/ldg on
+// those two operands.
+//
+// Work split: one warp per row, each lane owning every 32nd float4 of the row,
+// so a warp's loads are fully coalesced 512-byte transactions and the two
+// reductions (mean, then centred variance, as nn.LayerNorm computes them) are
+// warp shuffles over values already in registers. The row is read once (x and
+// y) and written once (s and h): 16*d bytes per row, the HBM floor.
+#include "kf_common.cuh"
+
+namespace kf {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256) ln_add_mask_vec_kernel(
+    const float* x, int64_t ldx, const float* y, int64_t ldy, const uint8_t* __restrict__ keep,
+    const float* __restrict__ w, const float* __restrict__ b, float* s_out, int64_t lds,
+    float* __restrict__ h_out, int64_t ldh, int64_t M,
+    int d, float eps, int flags) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const int nv4 = d >> 2;
+  const bool kept = keep ? (keep[row] != 0) : true;
+
+  float4 v[NV];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < nv4 && kept) {
+      float4 a = reinterpret_cast<const float4*>(x + row * ldx)[c];
+      if (y) {
+        const float4 t = reinterpret_cast<const float4*>(y + row * ldy)[c];
+        a.x += t.x;
+        a.y += t.y;
+        a.z += t.z;
+        a.w += t.w;
+      }
+      v[i] = a;
+      sum += (a.x + a.y) + (a.z + a.w);
+    }
+  }
+  const float inv_d = 1.f / static_cast<float>(d);
+  const float mean = warp_sum(sum) * inv_d;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nv4) {
+      const float a = v[i].x - mean, bb = v[i].y - mean, cc = v[i].z - mean, dd = v[i].w - mean;
+      sq += (a * a + bb * bb) + (cc * cc + dd * dd);
+    }
+  }
+  const float var = warp_sum(sq) * inv_d;
+  const float rstd = 1.f / sqrtf(var + eps);
+  const bool zero_h = (flags & KF_LN_MASK_OUT) && !kept;
+  const bool rnd = (flags & KF_LN_ROUND_TF32) != 0;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nv4) {
+      if (s_out) reinterpret_cast<float4*>(s_out + row * lds)[c] = v[i];
+      float4 h;
+      if (zero_h) {
+        h = make_float4(0.f, 0.f, 0.f, 0.f);
+      } else {
+        const float4 ww = __ldg(reinterpret_cast<const float4*>(w) + c);
+        const float4 bb = __ldg(reinterpret_cast<const float4*>(b) + c);
+        h.x = (v[i].x - mean) * rstd * ww.x + bb.x;
+        h.y = (v[i].y - mean) * rstd * ww.y + bb.y;
+        h.z = (v[i].z - mean) * rstd * ww.z + bb.z;
+        h.w = (v[i].w - mean) * rstd * ww.w + bb.w;
+        if (rnd) {
+          h.x = round_tf32(h.x);
+          h.y = round_tf32(h.y);
+          h.z = round_tf32(h.z);
+          h.w = round_tf32(h.w);
+        }
+      }
+      reinterpret_cast<float4*>(h_out + row * ldh)[c] = h;
+    }
+  }
+}
+
+// Generic path (any d, any alignment): three strided passes over the row.
+__global__ void __launch_bounds__(256) ln_add_mask_scalar_kernel(
+    const float* x, int64_t ldx, const float* y, int64_t ldy, const uint8_t* __restrict__ keep,
+    const float* __restrict__ w, const float* __restrict__ b, float* s_out, int64_t lds,
+    float* __restrict__ h_out, int64_t ldh, int64_t M,
+    int d, float eps, int flags) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const bool kept = keep ? (keep[row] != 0) : true;
+  auto val = [&](int c) -> float {
+    if (!kept) return 0.f;
+    float a = x[row * ldx + c];
+    if (y) a += y[row * ldy + c];
+    return a;
+  };
+  float sum = 0.f;
+  for (int c = lane; c < d; c += 32) sum += val(c);
+  const float inv_d = 1.f / static_cast<float>(d);
+  const float mean = warp_sum(sum) * inv_d;
+  float sq = 0.f;
+  for (int c = lane; c < d; c += 32) {
+    const float t = val(c) - mean;
+    sq += t * t;
+  }
+  const float rstd = 1.f / sqrtf(warp_sum(sq) * inv_d + eps);
+  const bool zero_h = (flags & KF_LN_MASK_OUT) && !kept;
+  const bool rnd = (flags & KF_LN_ROUND_TF32) != 0;
+  for (int c = lane; c < d; c += 32) {
+    const float s = val(c);
+    if (s_out) s_out[row * lds + c] = s;
+    float h = zero_h ? 0.f : (s - mean) * rstd * w[c] + b[c];
+    if (rnd && !zero_h) h = round_tf32(h);
+    h_out[row * ldh + c] = h;
+  }
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace kf
+
+using namespace kf;
+
+extern "C" int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64_t ldy,
+                              const uint8_t* keep, const float* w, const float* b, float* s_out,
+                              int64_t lds, float* h_out, int64_t ldh, int64_t M, int64_t d,
+                              float eps, int flags, void* stream) {
+  if (!x || !w || !b || !h_out || M < 0 || d <= 0 || ldx < d || ldh < d ||
+      (y && ldy < d) || (s_out && lds < d) || d > (1 << 24)) {
+    set_last_error("kf_ln_add_mask: invalid arguments (M=%lld d=%lld)", (long long)M,
+                   (long long)d);
+    return KF_E_INVALID;
+  }
+  if (M == 0) return KF_OK;
+  const int threads = 256;
+  const int rows_per_block = threads / 32;
+  const unsigned blocks = static_cast<unsigned>((M + rows_per_block - 1) / rows_per_block);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int di = static_cast<int>(d);
+
+  bool vec = (d % 4 == 0) && aligned16(x) && aligned16(w) && aligned16(b) && aligned16(h_out) &&
+             ldx % 4 == 0 && ldh % 4 == 0 && d <= 4096;
+  if (y) vec = vec && aligned16(y) && ldy % 4 == 0;
+  if (s_out) vec = vec && aligned16(s_out) && lds % 4 == 0;
+
+  if (vec) {
+    const int nv = (di / 4 + 31) / 32;
+#define KF_LN_LAUNCH(NV)                                                                      \
+  ln_add_mask_vec_kernel<NV><<<blocks, threads, 0, st>>>(x, ldx, y, ldy, keep, w, b, s_out, lds, \
+                                                         h_out, ldh, M, di, eps, flags)
+    if (nv <= 1)
+      KF_LN_LAUNCH(1);
+    else if (nv <= 2)
+      KF_LN_LAUNCH(2);
+    else if (nv <= 4)
+      KF_LN_LAUNCH(4);
+    else if (nv <= 6)
+      KF_LN_LAUNCH(6);
+    else if (nv <= 8)
+      KF_LN_LAUNCH(8);
+    else if (nv <= 16)
+      KF_LN_LAUNCH(16);
+    else
+      KF_LN_LAUNCH(32);
+#undef KF_LN_LAUNCH
+  } else {
+    ln_add_mask_scalar_kernel<<<blocks, threads, 0, st>>>(x, ldx, y, ldy, keep, w, b, s_out, lds,
+                                                          h_out, ldh, M, di, eps, flags);
+  }
+  return cuda_status(cudaGetLastError(), "kf_ln_add_mask launch");
+}

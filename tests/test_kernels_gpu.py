@@ -1,0 +1,239 @@
+"""The CUDA kernels through the C ABI against exact torch references.
+
+Traps targeted, as the reference's own kernel tests do
+(kernelforge tests/test_kernels.py): all-zero rows and mask ordering around
+the norm, row counts and sequence lengths that are not tile multiples, causal
+crossed with padding, fully masked softmax rows, strided QKV views, head_dim
+8 (zero-padded) through 256.
+
+Operands are pre-rounded to TF32 so the GEMM can be checked against a float64
+product to fp32-accumulation accuracy: any descriptor, swizzle or tiling error
+shows up as an O(1) difference, not as noise inside a loose tolerance.
+"""
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import tf32_round
+from techjam2026_b200.numerics import check
+from techjam2026_b200.ops import add_mask_layernorm, flash_attention, linear
+
+pytestmark = pytest.mark.gpu
+
+
+# --------------------------------------------------------------- layernorm
+
+@pytest.mark.parametrize("d", [128, 256, 512, 768, 1024, 100])
+@pytest.mark.parametrize("mask_out", [False, True])
+def test_fused_add_mask_layernorm(d, mask_out):
+    torch.manual_seed(0)
+    M = 517
+    x = torch.randn(M, d, device="cuda")
+    y = torch.randn(M, d, device="cuda")
+    keep = (torch.rand(M, device="cuda") > 0.3).float()
+    w = torch.randn(d, device="cuda")
+    b = torch.randn(d, device="cuda")
+    s, h = add_mask_layernorm(x, y, keep, w, b, 1e-5, mask_out=mask_out)
+    ref_s = (x + y) * keep[:, None]                     # fp32 add: bit-exact target
+    ref_h = F.layer_norm(ref_s.double(), (d,), w.double(), b.double(), 1e-5)
+    if mask_out:
+        ref_h = ref_h * keep[:, None].double()
+    assert torch.equal(s, ref_s)
+    assert (h.double() - ref_h).abs().max().item() < 2e-5
+    # padded rows: residual exactly 0; h exactly 0 under mask_out
+    dead = keep == 0
+    assert torch.count_nonzero(s[dead]) == 0
+    if mask_out:
+        assert torch.count_nonzero(h[dead]) == 0
+
+
+def test_layernorm_of_an_all_zero_row_returns_bias():
+    d = 256
+    x = torch.zeros(8, d, device="cuda")
+    w = torch.randn(d, device="cuda")
+    b = torch.randn(d, device="cuda")
+    _, h = add_mask_layernorm(x, None, None, w, b, 1e-5, mask_out=False)
+    assert torch.equal(h, b.expand_as(h))
+    keep = torch.zeros(8, device="cuda")
+    _, h_masked = add_mask_layernorm(x, None, keep, w, b, 1e-5, mask_out=True)
+    assert torch.count_nonzero(h_masked) == 0
+
+
+def test_layernorm_mask_is_a_select_not_a_multiply():
+    """A padded row holding NaN/Inf still comes out exactly 0 (masked_fill)."""
+    d = 128
+    x = torch.randn(4, d, device="cuda")
+    x[1] = float("nan")
+    x[2] = float("inf")
+    keep = torch.tensor([1, 0, 0, 1], device="cuda", dtype=torch.bool)
+    w, b = torch.ones(d, device="cuda"), torch.zeros(d, device="cuda")
+    s, h = add_mask_layernorm(x, None, keep, w, b, mask_out=True)
+    assert torch.count_nonzero(s[1:3]) == 0 and torch.count_nonzero(h[1:3]) == 0
+    assert torch.isfinite(h).all()
+
+
+def test_layernorm_in_place_residual():
+    """The stack updates its residual stream in place (x is s_out)."""
+    from techjam2026_b200 import _lib
+    torch.manual_seed(1)
+    M, d = 300, 512
+    x = torch.randn(M, d, device="cuda")
+    y = torch.randn(M, d, device="cuda")
+    w, b = torch.randn(d, device="cuda"), torch.randn(d, device="cuda")
+    ref_s = x + y
+    ref_h = F.layer_norm(ref_s, (d,), w, b, 1e-5)
+    h = torch.empty_like(x)
+    rc = _lib.lib().kf_ln_add_mask(x.data_ptr(), d, y.data_ptr(), d, None, w.data_ptr(),
+                                   b.data_ptr(), x.data_ptr(), d, h.data_ptr(), d, M, d, 1e-5,
+                                   0, _lib.stream_ptr())
+    _lib.check(rc, "kf_ln_add_mask")
+    assert torch.equal(x, ref_s)
+    assert (h - ref_h).abs().max().item() < 2e-5
+
+
+# --------------------------------------------------------------- GEMM
+
+@pytest.mark.parametrize("M,N,K", [(128, 64, 32), (517, 384, 512), (4096, 1536, 512),
+                                   (300, 200, 132), (1, 2304, 768), (2048, 512, 2048)])
+@pytest.mark.parametrize("bn", [0, 64, 128, 256])
+def test_gemm_exact_on_tf32_operands(M, N, K, bn):
+    torch.manual_seed(M + N + K)
+    a = tf32_round(torch.randn(M, K, device="cuda"))
+    w = tf32_round(torch.randn(N, K, device="cuda") / math.sqrt(K))
+    bias = torch.randn(N, device="cuda")
+    out = linear(a, w, bias, bn=bn)
+    ref = a.double() @ w.double().t() + bias.double()
+    err = (out.double() - ref).abs().max().item()
+    assert err < 1e-4, f"max abs err {err}"
+
+
+@pytest.mark.parametrize("M,N,K", [(517, 2048, 512), (128, 512, 128)])
+def test_gemm_gelu_epilogue(M, N, K):
+    torch.manual_seed(3)
+    a = tf32_round(torch.randn(M, K, device="cuda"))
+    w = tf32_round(torch.randn(N, K, device="cuda") / math.sqrt(K))
+    bias = torch.randn(N, device="cuda")
+    out = linear(a, w, bias, gelu=True)
+    ref = F.gelu(a.double() @ w.double().t() + bias.double(), approximate="none")
+    assert (out.double() - ref).abs().max().item() < 1e-4
+
+
+def test_gemm_unrounded_operands_within_tf32_error():
+    torch.manual_seed(4)
+    M, N, K = 1000, 768, 768
+    a = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / math.sqrt(K)
+    out = linear(a, w, None)
+    ref = a.double() @ w.double().t()
+    # TF32 keeps 10 explicit mantissa bits: |err| ~ 2^-11 * sqrt(K) * |a||w|
+    assert (out.double() - ref).abs().max().item() < 1e-2
+
+
+def test_gemm_head_padded_output():
+    """head_dim 8 columns land in 16-wide slots; pad columns stay untouched."""
+    from techjam2026_b200 import _lib
+    torch.manual_seed(5)
+    M, N, K = 256, 3 * 128, 128        # 3 x (16 heads x 8)
+    a = tf32_round(torch.randn(M, K, device="cuda"))
+    w = tf32_round(torch.randn(N, K, device="cuda") / math.sqrt(K))
+    out = torch.full((M, 3 * 16 * 16), 7.0, device="cuda")
+    rc = _lib.lib().kf_gemm_tf32(a.data_ptr(), K, w.data_ptr(), K, None, out.data_ptr(),
+                                 out.stride(0), M, N, K, 0, 0, 0, 8, 16, _lib.stream_ptr())
+    _lib.check(rc, "kf_gemm_tf32")
+    ref = (a.double() @ w.double().t()).view(M, 48, 8)
+    got = out.view(M, 48, 16)
+    assert (got[..., :8].double() - ref).abs().max().item() < 1e-4
+    assert torch.all(got[..., 8:] == 7.0)
+
+
+# --------------------------------------------------------------- attention
+
+def reference_attention(q, k, v, keep, causal, scale=None):
+    """float64 transcription of BaselineSelfAttention's core (softmax(QK^T)V)."""
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    scores = torch.matmul(q.double(), k.double().transpose(-2, -1)) * scale
+    S = q.shape[2]
+    if causal:
+        cm = torch.ones((S, S), device=q.device, dtype=torch.bool).triu(1)
+        scores = scores.masked_fill(cm, float("-inf"))
+    if keep is not None:
+        scores = scores.masked_fill(~keep.bool()[:, None, None, :], float("-inf"))
+    p = torch.softmax(scores, dim=-1)
+    p = torch.nan_to_num(p, nan=0.0)     # fully masked rows -> 0 (kernel contract)
+    return torch.matmul(p, v.double())
+
+
+@pytest.mark.parametrize("shape", [
+    (2, 8, 128, 64), (1, 4, 1, 64), (2, 8, 333, 64), (1, 8, 2048, 64),
+    (1, 4, 100, 128), (2, 4, 64, 32), (2, 4, 200, 16), (1, 2, 300, 256), (2, 16, 257, 8),
+])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("pad", [0.0, 0.4])
+def test_flash_attention_matches_reference(shape, causal, pad):
+    torch.manual_seed(0)
+    B, H, S, Dh = shape
+    q, k, v = (torch.randn(B, H, S, Dh, device="cuda") for _ in range(3))
+    keep = None
+    if pad > 0:
+        lens = torch.randint(1, S + 1, (B,), device="cuda")
+        keep = (torch.arange(S, device="cuda")[None, :] < lens[:, None]).to(torch.uint8)
+    out = flash_attention(q, k, v, keep=keep, causal=causal)
+    ref = reference_attention(q, k, v, keep, causal)
+    res = check(ref.float(), out)
+    assert res.passed, str(res)
+    assert (out.double() - ref).abs().max().item() < 5e-3
+
+
+def test_flash_fully_masked_row_yields_zero_not_nan():
+    torch.manual_seed(1)
+    B, H, S, Dh = 1, 2, 64, 32
+    q, k, v = (torch.randn(B, H, S, Dh, device="cuda") for _ in range(3))
+    keep = torch.zeros(B, S, dtype=torch.uint8, device="cuda")
+    keep[0, 40:] = 1      # rows < 40 see no valid key under the causal mask
+    out = flash_attention(q, k, v, keep=keep, causal=True)
+    assert torch.isfinite(out).all()
+    assert torch.count_nonzero(out[:, :, :40]) == 0
+
+
+def test_flash_random_non_prefix_mask():
+    torch.manual_seed(2)
+    B, H, S, Dh = 2, 4, 400, 64
+    q, k, v = (torch.randn(B, H, S, Dh, device="cuda") for _ in range(3))
+    keep = (torch.rand(B, S, device="cuda") > 0.5).to(torch.uint8)
+    keep[:, 0] = 1
+    keep[0, 128:256] = 0           # one fully masked KV tile in the middle
+    for causal in (False, True):
+        out = flash_attention(q, k, v, keep=keep, causal=causal)
+        ref = reference_attention(q, k, v, keep, causal)
+        assert (out.double() - ref).abs().max().item() < 5e-3
+
+
+def test_flash_on_strided_qkv_views():
+    """Q/K/V as views of one fused [B, S, 3, H, Dh] buffer, output into [B, S, H, Dh]."""
+    torch.manual_seed(3)
+    B, S, H, Dh = 2, 300, 8, 64
+    qkv = torch.randn(B, S, 3, H, Dh, device="cuda")
+    q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+    ctx = torch.empty(B, S, H, Dh, device="cuda")
+    flash_attention(q, k, v, causal=True, out=ctx.permute(0, 2, 1, 3))
+    ref = reference_attention(q.contiguous(), k.contiguous(), v.contiguous(), None, True)
+    assert (ctx.permute(0, 2, 1, 3).double() - ref).abs().max().item() < 5e-3
+
+
+def test_flash_long_sequence_causal_padded():
+    torch.manual_seed(4)
+    B, H, S, Dh = 1, 2, 4096, 64
+    q, k, v = (torch.randn(B, H, S, Dh, device="cuda") for _ in range(3))
+    keep = (torch.arange(S, device="cuda")[None, :] < 3000).to(torch.uint8)
+    out = flash_attention(q, k, v, keep=keep, causal=True)
+    ref = reference_attention(q, k, v, keep, True)
+    assert (out.double() - ref).abs().max().item() < 5e-3
+
+
+def test_device_status_clean_after_kernels():
+    from techjam2026_b200 import _lib
+    assert _lib.lib().kf_device_status(0) == 0
