@@ -1,0 +1,424 @@
+#!/usr/bin/env python3
+"""Benchmark of the layer-stack forward (BASELINE.json metric) on 1..8 B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2]
+                    [--impl ours|reference]
+
+A step is one forward of the stack over one batch of the workload (default
+c2: 6 layers, B=8, S=512, d=512, H=8, F=2048, causal + key padding). Under
+torchrun each rank runs its own batch (seed = rank) on its own GPU with no
+collective in the data path (weak scaling); the time is the max over ranks.
+
+Rank 0 prints one JSON line:
+  value        useful TFLOP/s of all ranks (valid tokens, valid causal pairs)
+               with inputs resident in HBM: CUDA-graph replays timed with
+               CUDA events, L2 flushed (256 MiB write) between steps;
+  e2e          the same metric through the public API (submission's
+               UserOptimizedTransformer): pinned host x/mask -> device ->
+               forward -> pinned host output, all inside the timed region;
+  roofline     the dominant kernel (largest share of forward time, measured
+               live with CUDA events around each launch of an eager forward);
+  cpu_baseline the CPU oracle (reference layer restated in PyTorch) on a
+               bounded sample, rank 0 at N=1;
+  clocks       nvidia-smi samples taken during the timed region.
+
+`--impl reference` times the reference's own CPU implementation of the path
+(the oracle port; the Python reference cannot be installed on the GPU box)
+on the host cores, same metric and config; only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+from techjam2026_b200.configs import WORKLOADS, generate_case, make_state_dict  # noqa: E402
+from techjam2026_b200.roofline import (lengths_of, measured_peaks, useful_flops,  # noqa: E402
+                                       dense_causal_flops)
+
+METRIC = "layer-stack fwd latency ms & TFLOP/s (% tcgen05 peak) at 1/2/4/8 B200 vs CPU ref"
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--config", default="c2", choices=sorted(WORKLOADS))
+    p.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    p.add_argument("--cpu-seconds", type=float, default=12.0,
+                   help="budget of the CPU-baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+# ----------------------------------------------------------------- CPU legs
+
+def cpu_sample(w, seconds: float, seed: int = 0):
+    """Time the CPU oracle on single sequences of the workload until `seconds`
+    elapse (at least one). Returns (useful TFLOP/s, sample description, threads)."""
+    import oracle
+    threads = max(1, os.cpu_count() or 1)
+    torch.set_num_threads(threads)
+    cfg = w.cfg
+    sd = make_state_dict(cfg, 0)
+    x, mask = generate_case(cfg, seed, w.padding_ratio, w.input_scale)
+    qc = 1024 if cfg.seq_len > 4096 else None
+    one = lambda b: oracle.forward(sd, cfg.num_layers, cfg.num_heads, x[b:b + 1],  # noqa: E731
+                                   mask[b:b + 1], causal=cfg.causal, query_chunk=qc)
+    if cfg.seq_len > 8192:
+        # c5-sized sequences: one prefix of 8192 tokens is the bounded unit.
+        P = 8192
+        one = lambda b: oracle.forward(sd, cfg.num_layers, cfg.num_heads,  # noqa: E731
+                                       x[b:b + 1, :P], mask[b:b + 1, :P], causal=cfg.causal,
+                                       query_chunk=1024)
+    one(0)  # warm-up
+    flops, t_total, n, b = 0.0, 0.0, 0, 0
+    t_end = time.perf_counter() + seconds
+    while n == 0 or time.perf_counter() < t_end:
+        t0 = time.perf_counter_ns()
+        one(b)
+        t_total += (time.perf_counter_ns() - t0) / 1e9
+        L = mask[b]
+        if cfg.seq_len > 8192:
+            L = L[:8192]
+        flops += useful_flops(cfg, [int(L.sum())])
+        n += 1
+        b = (b + 1) % cfg.batch_size
+    desc = (f"oracle fp32 on {n} single sequence(s) of {w.name} "
+            f"({'prefix 8192 of ' if cfg.seq_len > 8192 else ''}S={cfg.seq_len}), "
+            f"{t_total:.1f} s, torch threads={threads}")
+    return flops / t_total / 1e12, desc, threads, t_total / n * 1e3
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    w = WORKLOADS[args.config]
+    for _ in range(max(0, args.warmup)):
+        pass  # the sample itself includes a warm-up forward
+    per_step = max(2.0, min(20.0, 120.0 / max(1, args.steps)))
+    vals, descs = [], []
+    threads = 1
+    for _ in range(args.steps):
+        v, desc, threads, ms = cpu_sample(w, per_step, seed=0)
+        vals.append(v)
+        descs.append(desc)
+    value = statistics.median(vals)
+    line = {
+        "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "impl": "reference",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded generate_random_case draws, Xavier weights)",
+        "config": {"workload": w.name, "signature": sig(w.cfg)},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port", "sample": descs[-1]},
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def sig(cfg):
+    from techjam2026_b200.configs import signature
+    return signature(cfg)
+
+
+# ----------------------------------------------------------------- clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="kf_clocks_", suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sms, maxes, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sms.append(float(parts[1]))
+                    maxes.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(name)
+        os.unlink(self.path)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
+                "samples": len(sms), "reasons": sorted(reasons)}
+
+
+# ----------------------------------------------------------------- GPU legs
+
+class LaunchTimer:
+    """Brackets each C-ABI launch of an eager forward with CUDA events."""
+
+    def __init__(self):
+        self.records = []
+
+    def __call__(self, kind: str):
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        self.records.append((kind, start, end))
+        return start, end
+
+
+def kernel_breakdown(model, x, keep, ws, weights, repeats: int = 5):
+    """Per-kind average launch time (ms) from events around every launch."""
+    out = torch.empty_like(x)
+    totals, counts = {}, {}
+    for _ in range(repeats):
+        timer = LaunchTimer()
+        model.launch(x, keep, out, ws, weights, timer=timer)
+        torch.cuda.synchronize()
+        for kind, s, e in timer.records:
+            totals[kind] = totals.get(kind, 0.0) + s.elapsed_time(e)
+            counts[kind] = counts.get(kind, 0) + 1
+    return {k: (totals[k] / counts[k], counts[k] // repeats) for k in totals}
+
+
+def kernel_work(kind: str, cfg, B: int, S: int, lengths) -> tuple:
+    """Algorithmic work of ONE launch of `kind`: (amount, unit, bound)."""
+    d, F, H = cfg.d_model, cfg.ffn_dim, cfg.num_heads
+    M = B * S
+    if kind == "qkv":
+        return 2.0 * M * 3 * d * d, "flop", "tensor"
+    if kind == "out_proj":
+        return 2.0 * M * d * d, "flop", "tensor"
+    if kind == "ffn1":
+        return 2.0 * M * F * d, "flop", "tensor"
+    if kind == "ffn2":
+        return 2.0 * M * d * F, "flop", "tensor"
+    if kind == "attention":
+        pairs = sum(n * (n + 1) // 2 for n in lengths) if cfg.causal else sum(n * n for n in lengths)
+        return 4.0 * d * pairs, "flop", "tensor"
+    if kind == "ln":
+        return 16.0 * d * M, "byte", "hbm"
+    if kind == "keep_bits":
+        return float(M + 4 * B * ((S + 31) // 32)), "byte", "hbm"
+    return 0.0, "flop", "tensor"
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        args.gpus = world if world > 1 else args.gpus
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch.distributed as dist
+    from techjam2026_b200 import _lib
+    from techjam2026_b200.dispatch import DispatchTable, probe
+    from techjam2026_b200.fused import FusedTransformer
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+
+    w = WORKLOADS[args.config]
+    cfg = w.cfg
+    spec = probe(local)
+    plan, source = DispatchTable.load_for(spec).lookup(spec.arch, torch.float32, cfg)
+    model = FusedTransformer(cfg, plan)
+    model.load_state_dict(make_state_dict(cfg, 0), strict=True)
+    model.eval()
+
+    seed = w.seeds[rank % len(w.seeds)] if world == 1 else rank
+    x_cpu, mask_cpu = generate_case(cfg, seed, w.padding_ratio, w.input_scale)
+    lengths = lengths_of(mask_cpu, cfg.batch_size, cfg.seq_len)
+    flops_rank = useful_flops(cfg, lengths)
+    x = x_cpu.to(dev)
+    mask = mask_cpu.to(dev)
+
+    runner = model.graph_runner(x, mask)
+    runner.load_inputs(x, mask)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    for _ in range(max(3, args.warmup)):
+        runner.replay()
+    torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        time.sleep(0.3)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for k in range(args.steps):
+            flush.zero_()                       # evict L2 between steps (untimed)
+            starts[k].record()
+            runner.replay()
+            ends[k].record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms_total = sum(step_ms)
+    t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
+    f = torch.tensor([flops_rank], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(f, op=dist.ReduceOp.SUM)
+    ms_total_max = float(t.item())
+    flops_all = float(f.item())
+    ms_per_step = ms_total_max / args.steps
+    value = flops_all / (ms_per_step / 1e3) / 1e12
+    status = _lib.lib().kf_device_status(0)
+
+    # ---- e2e through the public API (pinned host buffers, copies timed)
+    e2e = None
+    if not args.no_e2e:
+        import submission
+        api = submission.UserOptimizedTransformer(cfg)
+        api.load_state_dict(model.state_dict(), strict=True)
+        api = api.to(dev).eval()
+        xh = x_cpu.pin_memory()
+        mh = mask_cpu.pin_memory()
+        oh = torch.empty_like(x_cpu).pin_memory()
+        with torch.inference_mode():
+            for _ in range(max(3, args.warmup)):
+                oh.copy_(api(xh.to(dev, non_blocking=True), mh.to(dev, non_blocking=True)),
+                         non_blocking=True)
+            torch.cuda.synchronize()
+            e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+            e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+            if world > 1:
+                dist.barrier()
+            for k in range(args.steps):
+                flush.zero_()
+                e_s[k].record()
+                xd = xh.to(dev, non_blocking=True)
+                md = mh.to(dev, non_blocking=True)
+                oh.copy_(api(xd, md), non_blocking=True)
+                e_e[k].record()
+            torch.cuda.synchronize()
+        assert api._impl is not None, "public API fell back: e2e would not measure the GPU path"
+        e_ms = torch.tensor([sum(s.elapsed_time(e) for s, e in zip(e_s, e_e))],
+                            dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e_step = float(e_ms.item()) / args.steps
+        e2e = {"value": round(flops_all / (e_step / 1e3) / 1e12, 3), "unit": "TFLOP/s",
+               "ms_per_step": round(e_step, 4),
+               "h2d_bytes_per_step": int(xh.numel() * 4 + mh.numel()),
+               "d2h_bytes_per_step": int(oh.numel() * 4)}
+
+    # ---- live per-kernel breakdown (eager forward, events around each launch)
+    ws = runner.ws
+    bd = kernel_breakdown(model, runner.static_x, runner.static_keep, ws, runner.weights)
+    shares = {k: ms * n for k, (ms, n) in bd.items()}
+    total = sum(shares.values())
+    dom = max(shares, key=shares.get)
+    amount, unit, bound = kernel_work(dom, cfg, cfg.batch_size, cfg.seq_len, lengths)
+    peaks = measured_peaks()
+    dom_ms = bd[dom][0]
+    if bound == "tensor":
+        achieved = amount / (dom_ms / 1e3) / 1e12
+        peak = peaks["tf32_tflops"]
+        r_unit = "TFLOP/s"
+    else:
+        achieved = amount / (dom_ms / 1e3) / 1e9
+        peak = peaks["hbm_gbs"]
+        r_unit = "GB/s"
+    roofline = {"kernel": dom, "bound": bound, "achieved": round(achieved, 2),
+                "peak": round(peak, 1), "unit": r_unit, "frac": round(achieved / peak, 4),
+                "traffic": None,
+                "peak_source": f"{peaks['source']} (TF32 = measured dense BF16 / 2)"
+                if bound == "tensor" else peaks["source"],
+                "launch_ms": round(dom_ms, 5),
+                "share": {k: round(v / total, 4) for k, v in sorted(shares.items())}}
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            v, desc, threads, ms = cpu_sample(w, args.cpu_seconds)
+            cpu = {"value": round(v, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                   "sample": desc, "ms_per_sequence": round(ms, 2)}
+        clk = clocks.summary()
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded generate_random_case draws, Xavier weights)",
+            "config": {"workload": w.name, "signature": sig(cfg),
+                       "global_batch": cfg.batch_size * world, "seq_len": cfg.seq_len,
+                       "parallelism": f"batch-sharded x{world}, no collective",
+                       "plan": plan.describe(), "plan_source": source,
+                       "l2": "flushed between steps (256 MiB write)",
+                       "valid_tokens_per_rank": int(sum(lengths)),
+                       "dense_causal_tflop_per_rank": round(dense_causal_flops(cfg) / 1e12, 4),
+                       "useful_tflop_per_rank": round(flops_rank / 1e12, 4)},
+            "tc_frac_of_tf32_peak": round(value / world / peaks["tf32_tflops"], 4),
+            "gpu_launches": int(runner.launches * args.steps),
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    runner = None
+    model.release_buffers()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -42,11 +42,16 @@ SIGNATURES = {
 
 # C-ABI constants (include/kf_sm100.h)
 KF_OK = 0
+KF_E_INVALID = 1
+KF_E_UNSUPPORTED = 2
+KF_E_CUDA = 3
+KF_E_NO_DEVICE = 4
 KF_LN_MASK_OUT = 1
 KF_LN_ROUND_TF32 = 2
 KF_EPI_BIAS = 0
 KF_EPI_BIAS_GELU = 1
 KF_GEMM_ROUND_TF32 = 1
+KF_GEMM_SPLIT3 = 2
 KF_ATTN_CAUSAL = 1
 KF_ATTN_SKIP_EMPTY_Q = 2
 KF_ATTN_ROUND_TF32 = 4

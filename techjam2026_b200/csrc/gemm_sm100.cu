@@ -16,27 +16,50 @@
 //               optionally GELU(erf) and TF32 rounding, store fp32 to HBM,
 //               then hand the accumulator back to the MMA warp. Double
 //               buffering lets the epilogue of tile i overlap the main loop of
-//               tile i+1.
+//               tile i+1;
+//   warps 6-9   (split mode only) converters: once a stage has landed they
+//               write lo = x - trunc_tf32(x) of both tiles next to them in
+//               shared memory, so the MMA warp can issue the error-compensated
+//               product  A.B ~= hi(A).hi(B) + hi(A).lo(B) + lo(A).hi(B)
+//               (three kind::tf32 MMAs per k step; the tensor core itself
+//               drops the low mantissa bits, so the staged fp32 tile serves
+//               as hi). Error ~2^-20 relative instead of TF32's 2^-11, with no
+//               extra HBM or L2 traffic.
 #include "kf_common.cuh"
 
 namespace kf {
 
 enum : int { KF_GEMM_VEC_OK = 1 << 8 };
 
-template <int BN>
+template <int BN, int SPLIT>
 struct GemmCfg {
   static constexpr int BM = 128;
   static constexpr int BK = 32;  // 32 fp32 = 128 bytes = one swizzle row
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+  // stage layout: A | B [| lo(A) | lo(B)]
+  static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (SPLIT ? 2 : 1);
+  static constexpr int STAGES_FIT = 196608 / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int THREADS = SPLIT ? 320 : 192;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(STAGES >= 2, "stages");
   static_assert(SMEM_BYTES <= 232448, "smem");
 };
+
+// Low part of a TF32 split: x - trunc_tf32(x), exact in fp32.
+__device__ __forceinline__ uint32_t tf32_lo_bits(uint32_t x) {
+  const float f = __uint_as_float(x);
+  const float hi = __uint_as_float(x & 0xFFFFE000u);
+  return __float_as_uint(f - hi);
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.f + erff(x * 0.70710678118654752440f));
@@ -86,19 +109,20 @@ __device__ __forceinline__ void gemm_store_chunk(const float (&v)[32], float* __
   }
 }
 
-template <int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+template <int BN, int EPI, int SPLIT>
+__global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int M,
                      int N, int K, int flags, int head_dim, int head_stride) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, SPLIT>;
   constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* acc_full = empty + STAGES;
+  uint64_t* conv = empty + STAGES;  // split mode: lo tiles written
+  uint64_t* acc_full = conv + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -115,6 +139,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 4);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
@@ -151,7 +176,7 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::B_BYTES);
           tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
           tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full[stage], kb * BK, n0);
           ++issued;
@@ -186,18 +211,27 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA)) {
+          if (!mbar_wait(SPLIT ? &conv[stage] : &full[stage], phase, abort_flag,
+                         KF_DEV_WAIT_TIMEOUT_MMA)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_BYTES);
           const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+          const uint32_t alo_addr = b_addr + Cfg::B_BYTES;
+          const uint32_t blo_addr = alo_addr + Cfg::A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 8; ++k) {
             const uint64_t ad = make_smem_desc(a_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
             const uint64_t bd = make_smem_desc(b_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
-            mma_tf32_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            if (SPLIT) {
+              const uint64_t ald = make_smem_desc(alo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+              const uint64_t bld = make_smem_desc(blo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+              mma_tf32_ss(d_tmem, ald, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+              mma_tf32_ss(d_tmem, ad, bld, idesc, 1u);
+            }
+            mma_tf32_ss(d_tmem, ad, bd, idesc, (SPLIT || (kb | k) != 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -215,6 +249,39 @@ __global__ void __launch_bounds__(192, 1)
       // Every MMA this thread issued completes before TMEM is released.
       mma_commit(drain);
       mbar_wait_drain(drain, 0, KF_DEV_WAIT_TIMEOUT_MMA);
+    }
+  } else if (SPLIT && warp >= 6) {
+    // -------------------------------------------------- converters (warps 6..9)
+    const int ct = threadIdx.x - 192;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        const uint4* src = reinterpret_cast<const uint4*>(smem + stage * Cfg::STAGE_BYTES);
+        uint4* dst = reinterpret_cast<uint4*>(smem + stage * Cfg::STAGE_BYTES + Cfg::A_BYTES +
+                                              Cfg::B_BYTES);
+#pragma unroll 4
+        for (int i = ct; i < (Cfg::A_BYTES + Cfg::B_BYTES) / 16; i += 128) {
+          uint4 v = src[i];
+          v.x = tf32_lo_bits(v.x);
+          v.y = tf32_lo_bits(v.y);
+          v.z = tf32_lo_bits(v.z);
+          v.w = tf32_lo_bits(v.w);
+          dst[i] = v;
+        }
+        fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
     }
   } else {
     // -------------------------------------------------- epilogue (warps 2..5)
@@ -256,12 +323,12 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int SPLIT>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, float* C, int64_t ldc,
                        const float* bias, int M, int N, int K, int flags, int hd, int hs,
                        cudaStream_t st) {
-  using Cfg = GemmCfg<BN>;
-  auto kern = gemm_tf32_kernel<BN, EPI>;
+  using Cfg = GemmCfg<BN, SPLIT>;
+  auto kern = gemm_tf32_kernel<BN, EPI, SPLIT>;
   static int attr_set[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -274,7 +341,8 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, float* C, i
   }
   const int tiles = ((M + Cfg::BM - 1) / Cfg::BM) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, 192, Cfg::SMEM_BYTES, st>>>(ta, tb, C, ldc, bias, M, N, K, flags, hd, hs);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, C, ldc, bias, M, N, K, flags, hd,
+                                                     hs);
   return cuda_status(cudaGetLastError(), "kf_gemm_tf32 launch");
 }
 
@@ -367,13 +435,21 @@ extern "C" int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t
   if (vec) f |= KF_GEMM_VEC_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
-#define KF_GEMM_CASE(BNV)                                                                   \
-  if (bn == BNV) {                                                                          \
-    if (epilogue == KF_EPI_BIAS)                                                            \
-      return launch_gemm<BNV, KF_EPI_BIAS>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,      \
-                                           head_stride, st);                                \
-    return launch_gemm<BNV, KF_EPI_BIAS_GELU>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,   \
-                                              head_stride, st);                             \
+  const bool split = (flags & KF_GEMM_SPLIT3) != 0;
+#define KF_GEMM_CASE(BNV)                                                                     \
+  if (bn == BNV) {                                                                            \
+    if (split) {                                                                              \
+      if (epilogue == KF_EPI_BIAS)                                                            \
+        return launch_gemm<BNV, KF_EPI_BIAS, 1>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,   \
+                                                head_stride, st);                             \
+      return launch_gemm<BNV, KF_EPI_BIAS_GELU, 1>(ta, tb, C, ldc, bias, m, n, k, f,          \
+                                                   head_dim, head_stride, st);                \
+    }                                                                                         \
+    if (epilogue == KF_EPI_BIAS)                                                              \
+      return launch_gemm<BNV, KF_EPI_BIAS, 0>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,     \
+                                              head_stride, st);                               \
+    return launch_gemm<BNV, KF_EPI_BIAS_GELU, 0>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,  \
+                                                 head_stride, st);                            \
   }
   KF_GEMM_CASE(64)
   KF_GEMM_CASE(128)

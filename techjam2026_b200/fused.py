@@ -1,0 +1,316 @@
+"""The layer-stack forward on sm_100a: every op is a call into libkf_sm100.
+
+Per forward (fp32 I/O, residual stream fp32 throughout):
+
+  keep bits  <- kf_keep_bits(valid_token_mask)                  (once)
+  res, h     <- kf_ln_add_mask(x, -, keep, LN1[0])              (entry norm)
+  per layer i:
+    qkv      <- kf_gemm_tf32(h, [Wq;Wk;Wv], b)                  fused QKV
+    ctx      <- kf_flash_fwd_tf32(q, k, v views of qkv, keep bits, causal)
+    y        <- kf_gemm_tf32(ctx, Wo, bo)                       out_proj
+    res, h   <- kf_ln_add_mask(res, y, keep, LN2[i])            in place
+    ffn      <- kf_gemm_tf32(h, W1, b1, GELU(erf))
+    y        <- kf_gemm_tf32(ffn, W2, b2)
+    res, h   <- kf_ln_add_mask(res, y, keep, LN1[i+1])          (last layer:
+                final_norm with mask_out, written to the output)
+
+That is the reference's fused structure (kernelforge/optimized.py:397-458),
+with cuBLAS replaced by the tcgen05 GEMM and the GELU fused into FFN1's
+epilogue. Masking the residual at the entry norm and inside every norm is
+exact: padded rows never feed a valid row (keys are masked in attention, all
+other ops are per row) and the reference zeroes them at every block end.
+
+The whole forward is captured once per (shape, mask presence) into one CUDA
+graph (kernelforge/optimized.py:588-625 pattern): static input buffers, one
+replay, output cloned for the caller. There is no fallback: a failing
+kernel raises.
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import _lib
+from .dispatch import DEFAULT_PLAN, Plan
+from .model import LayerStack
+
+SUPPORTED_HEAD_DIMS = (8, 16, 32, 64, 128, 256)
+
+
+class _Weights:
+    """Device copies laid out for the kernels: fused [Wq;Wk;Wv]; weights of a
+    GEMM that runs plain TF32 are rounded to the nearest TF32 value once
+    (weights of a 3xTF32 GEMM keep all their bits)."""
+
+    def __init__(self, model: LayerStack, device: torch.device, plan: Plan):
+        from .ops.gemm import round_tf32 as rnd
+
+        def prep_w(w: torch.Tensor, split: bool = False) -> torch.Tensor:
+            w = w.detach().to(device=device, dtype=torch.float32).contiguous()
+            return rnd(w) if (plan.round_tf32 and not split) else w.clone()
+
+        def prep_b(b: torch.Tensor) -> torch.Tensor:
+            return b.detach().to(device=device, dtype=torch.float32).contiguous().clone()
+
+        self.layers = []
+        for layer in model.layers:
+            a = layer.attention
+            self.layers.append(dict(
+                wqkv=prep_w(torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0),
+                            plan.split_qkv),
+                bqkv=prep_b(torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias], 0)),
+                wo=prep_w(a.out_proj.weight, plan.split_out), bo=prep_b(a.out_proj.bias),
+                w1=prep_w(layer.ffn_in.weight, plan.split_ffn1), b1=prep_b(layer.ffn_in.bias),
+                w2=prep_w(layer.ffn_out.weight, plan.split_ffn2), b2=prep_b(layer.ffn_out.bias),
+                ln1w=prep_b(layer.norm1.weight), ln1b=prep_b(layer.norm1.bias),
+                ln2w=prep_b(layer.norm2.weight), ln2b=prep_b(layer.norm2.bias),
+                eps1=float(layer.norm1.eps), eps2=float(layer.norm2.eps)))
+        self.finw = prep_b(model.final_norm.weight)
+        self.finb = prep_b(model.final_norm.bias)
+        self.fin_eps = float(model.final_norm.eps)
+
+
+class _Workspace:
+    """Activation buffers for one (B, S): allocated once, reused every call.
+    The QKV buffer is zeroed once so head-padding columns (head_dim 8 stored
+    as 16) stay exactly zero."""
+
+    def __init__(self, cfg, B: int, S: int, device: torch.device):
+        d, F, H = cfg.d_model, cfg.ffn_dim, cfg.num_heads
+        self.dh = d // H
+        self.dh_store = max(16, self.dh)
+        M = B * S
+        f32 = dict(dtype=torch.float32, device=device)
+        self.res = torch.empty(M, d, **f32)
+        self.h = torch.empty(M, d, **f32)
+        self.qkv = torch.zeros(M, 3 * H * self.dh_store, **f32)
+        self.ctx = torch.empty(M, d, **f32)
+        self.y = torch.empty(M, d, **f32)
+        self.ffn = torch.empty(M, F, **f32)
+        words = (S + 31) // 32
+        self.bits = torch.empty(B * words, dtype=torch.int32, device=device)
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size()
+                   for t in (self.res, self.h, self.qkv, self.ctx, self.y, self.ffn, self.bits))
+
+
+class FusedTransformer(LayerStack):
+    """Drop-in for BaselineTransformer (identical state_dict keys).
+
+    `forward(x, valid_token_mask=None) -> Tensor[B, S, d]` with x fp32 on an
+    sm_100 GPU and valid_token_mask bool [B, S] (True = real token).
+    """
+
+    def __init__(self, config, plan: Optional[Plan] = None):
+        super().__init__(config)
+        self.plan = plan or DEFAULT_PLAN
+        self._weights: Optional[_Weights] = None
+        self._weights_key = None
+        self._workspaces: Dict[Tuple, _Workspace] = {}
+        self._graphs: Dict[Tuple, "GraphRunner"] = {}
+        self.launches_per_forward = 0
+
+    # ------------------------------------------------------------ preparation
+
+    def _param_key(self, device) -> tuple:
+        # Parameter storage identity; call invalidate() after editing weights
+        # in place (inference tensors carry no version counter to watch).
+        return (str(device),) + tuple(p.data_ptr() for p in self.parameters())
+
+    def invalidate(self) -> None:
+        """Drop prepared weights and captured graphs (after in-place edits)."""
+        self._weights = None
+        self._weights_key = None
+        self._graphs.clear()
+
+    def prepare(self, device: torch.device) -> _Weights:
+        key = self._param_key(device)
+        if self._weights is None or self._weights_key != key:
+            self._weights = _Weights(self, device, self.plan)
+            self._weights_key = key
+            self._graphs.clear()
+        return self._weights
+
+    def workspace(self, B: int, S: int, device: torch.device) -> _Workspace:
+        key = (B, S, str(device))
+        ws = self._workspaces.get(key)
+        if ws is None:
+            ws = _Workspace(self.config, B, S, device)
+            self._workspaces[key] = ws
+        return ws
+
+    def release_buffers(self) -> None:
+        self._graphs.clear()
+        self._workspaces.clear()
+
+    # ------------------------------------------------------------ the forward
+
+    def _check_inputs(self, x: torch.Tensor, mask: Optional[torch.Tensor]) -> None:
+        cfg = self.config
+        if x.dim() != 3 or x.shape[-1] != cfg.d_model:
+            raise ValueError(f"x must be [B, S, {cfg.d_model}], got {tuple(x.shape)}")
+        if x.dtype != torch.float32:
+            raise TypeError("only float32 I/O is implemented")
+        if not x.is_cuda:
+            raise RuntimeError("FusedTransformer runs on an sm_100 GPU only (no CPU path)")
+        if mask is not None and tuple(mask.shape) != tuple(x.shape[:2]):
+            raise ValueError("valid_token_mask must be [B, S]")
+        if cfg.d_model // cfg.num_heads not in SUPPORTED_HEAD_DIMS:
+            raise RuntimeError(f"head_dim {cfg.d_model // cfg.num_heads} unsupported")
+
+    def launch(self, x: torch.Tensor, keep_u8: Optional[torch.Tensor], out: torch.Tensor,
+               ws: _Workspace, w: _Weights, timer=None) -> int:
+        """Issue the whole forward on the current stream; returns launches.
+
+        `timer(kind) -> (start_event, end_event)`, when given, brackets every
+        launch with CUDA events (used for the live per-kernel breakdown)."""
+        cfg, plan = self.config, self.plan
+        B, S, d = x.shape
+        M, H, F = B * S, cfg.num_heads, cfg.ffn_dim
+        dh, dhs = ws.dh, ws.dh_store
+        L = _lib.lib()
+        st = _lib.stream_ptr()
+        R = plan.round_tf32
+        # Round a producer's output only when its consumer is a plain TF32 MMA.
+        rnd_h1 = _lib.KF_LN_ROUND_TF32 if (R and not plan.split_qkv) else 0
+        rnd_h2 = _lib.KF_LN_ROUND_TF32 if (R and not plan.split_ffn1) else 0
+        rnd_qkv = _lib.KF_GEMM_ROUND_TF32 if R else 0          # feeds attention
+        rnd_gelu = _lib.KF_GEMM_ROUND_TF32 if (R and not plan.split_ffn2) else 0
+        sp = _lib.KF_GEMM_SPLIT3
+        f_qkv = rnd_qkv | (sp if plan.split_qkv else 0)
+        f_out = sp if plan.split_out else 0
+        f_ffn1 = rnd_gelu | (sp if plan.split_ffn1 else 0)
+        f_ffn2 = sp if plan.split_ffn2 else 0
+        attn_flags = (_lib.KF_ATTN_CAUSAL if cfg.causal else 0) | (
+            _lib.KF_ATTN_ROUND_TF32 if (R and not plan.split_out) else 0)
+        keep = keep_u8.data_ptr() if keep_u8 is not None else None
+        bits = ws.bits.data_ptr() if keep_u8 is not None else None
+        if keep_u8 is not None and plan.skip_empty_queries:
+            attn_flags |= _lib.KF_ATTN_SKIP_EMPTY_Q
+        res, h, y, ctx, ffn, qkv = (ws.res.data_ptr(), ws.h.data_ptr(), ws.y.data_ptr(),
+                                    ws.ctx.data_ptr(), ws.ffn.data_ptr(), ws.qkv.data_ptr())
+        ldq = 3 * H * dhs
+        hd, hs = (dh, dhs) if dhs != dh else (0, 0)
+        n = 0
+
+        def run(kind, fn, *a):
+            nonlocal n
+            if timer is not None:
+                ev0, ev1 = timer(kind)
+                ev0.record()
+            _lib.check(fn(*a), fn.__name__)
+            if timer is not None:
+                ev1.record()
+            n += 1
+
+        if keep is not None:
+            run("keep_bits", L.kf_keep_bits, keep, S, B, S, bits, st)
+        l0 = w.layers[0]
+        run("ln", L.kf_ln_add_mask, x.data_ptr(), d, None, 0, keep, l0["ln1w"].data_ptr(),
+            l0["ln1b"].data_ptr(), res, d, h, d, M, d, l0["eps1"], rnd_h1, st)
+        nl = len(w.layers)
+        for i, lw in enumerate(w.layers):
+            run("qkv", L.kf_gemm_tf32, h, d, lw["wqkv"].data_ptr(), d, lw["bqkv"].data_ptr(),
+                qkv, ldq, M, 3 * d, d, _lib.KF_EPI_BIAS, f_qkv, plan.bn_qkv, hd, hs, st)
+            run("attention", L.kf_flash_fwd_tf32, qkv, S * ldq, dhs, ldq,
+                qkv + 4 * H * dhs, S * ldq, dhs, ldq, qkv + 8 * H * dhs, S * ldq, dhs, ldq,
+                ctx, S * d, dh, d, bits, B, H, S, dhs, dh, dh ** -0.5, attn_flags, st)
+            run("out_proj", L.kf_gemm_tf32, ctx, d, lw["wo"].data_ptr(), d, lw["bo"].data_ptr(),
+                y, d, M, d, d, _lib.KF_EPI_BIAS, f_out, plan.bn_out, 0, 0, st)
+            run("ln", L.kf_ln_add_mask, res, d, y, d, keep, lw["ln2w"].data_ptr(),
+                lw["ln2b"].data_ptr(), res, d, h, d, M, d, lw["eps2"], rnd_h2, st)
+            run("ffn1", L.kf_gemm_tf32, h, d, lw["w1"].data_ptr(), d, lw["b1"].data_ptr(), ffn,
+                F, M, F, d, _lib.KF_EPI_BIAS_GELU, f_ffn1, plan.bn_ffn1, 0, 0, st)
+            run("ffn2", L.kf_gemm_tf32, ffn, F, lw["w2"].data_ptr(), F, lw["b2"].data_ptr(), y,
+                d, M, d, F, _lib.KF_EPI_BIAS, f_ffn2, plan.bn_ffn2, 0, 0, st)
+            if i == nl - 1:
+                run("ln", L.kf_ln_add_mask, res, d, y, d, keep, w.finw.data_ptr(),
+                    w.finb.data_ptr(), None, 0, out.data_ptr(), d, M, d, w.fin_eps,
+                    _lib.KF_LN_MASK_OUT, st)
+            else:
+                nx = w.layers[i + 1]
+                run("ln", L.kf_ln_add_mask, res, d, y, d, keep, nx["ln1w"].data_ptr(),
+                    nx["ln1b"].data_ptr(), res, d, h, d, M, d, nx["eps1"], rnd_h1, st)
+        self.launches_per_forward = n
+        return n
+
+    @staticmethod
+    def _keep_u8(mask: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+        if mask is None:
+            return None
+        if mask.dtype == torch.bool:
+            return mask.contiguous().view(torch.uint8)
+        return (mask != 0).to(torch.uint8).contiguous()
+
+    def eager_forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
+                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        self._check_inputs(x, valid_token_mask)
+        x = x.contiguous()
+        w = self.prepare(x.device)
+        B, S, d = x.shape
+        ws = self.workspace(B, S, x.device)
+        out = torch.empty_like(x) if out is None else out
+        self.launch(x, self._keep_u8(valid_token_mask), out, ws, w)
+        return out
+
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None
+                ) -> torch.Tensor:
+        if self.plan.cuda_graph and not torch.cuda.is_current_stream_capturing():
+            self._check_inputs(x, valid_token_mask)
+            return self.graph_runner(x, valid_token_mask)(x, valid_token_mask)
+        return self.eager_forward(x, valid_token_mask)
+
+    def graph_runner(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]
+                     ) -> "GraphRunner":
+        key = (tuple(x.shape), str(x.device), valid_token_mask is None)
+        runner = self._graphs.get(key)
+        if runner is None:
+            runner = GraphRunner(self, x, valid_token_mask)
+            self._graphs[key] = runner
+        return runner
+
+
+class GraphRunner:
+    """One CUDA graph holding the whole multi-layer forward for a fixed shape.
+
+    Inputs are copied into static device buffers, the graph is replayed, and
+    the output is cloned (the next replay overwrites the static output, and
+    callers legitimately hold results)."""
+
+    def __init__(self, model: FusedTransformer, x: torch.Tensor,
+                 mask: Optional[torch.Tensor]):
+        self.model = model
+        B, S, d = x.shape
+        self.static_x = x.detach().clone().contiguous()
+        self.static_keep = None if mask is None else model._keep_u8(mask).clone()
+        self.static_out = torch.empty_like(self.static_x)
+        self.weights = model.prepare(x.device)
+        # A workspace of its own: eager calls of other shapes never alias it.
+        self.ws = _Workspace(model.config, B, S, x.device)
+        side = torch.cuda.Stream(device=x.device)
+        side.wait_stream(torch.cuda.current_stream(x.device))
+        with torch.cuda.stream(side):
+            # Warm-up outside capture: sets kernel attributes, checks arguments.
+            self.launches = model.launch(self.static_x, self.static_keep, self.static_out,
+                                         self.ws, self.weights)
+        torch.cuda.current_stream(x.device).wait_stream(side)
+        torch.cuda.synchronize(x.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            model.launch(self.static_x, self.static_keep, self.static_out, self.ws,
+                         self.weights)
+
+    def load_inputs(self, x: torch.Tensor, mask: Optional[torch.Tensor]) -> None:
+        self.static_x.copy_(x, non_blocking=True)
+        if self.static_keep is not None and mask is not None:
+            self.static_keep.copy_(FusedTransformer._keep_u8(mask), non_blocking=True)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.static_out
+
+    def __call__(self, x: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
+        self.load_inputs(x, mask)
+        return self.replay().clone()

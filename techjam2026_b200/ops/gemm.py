@@ -16,8 +16,14 @@ from .. import _lib
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
            gelu: bool = False, out: Optional[torch.Tensor] = None, round_tf32: bool = False,
-           bn: int = 0) -> torch.Tensor:
-    """x [M, K] fp32 (unit inner stride), weight [N, K] fp32 -> [M, N] fp32."""
+           bn: int = 0, precision: str = "3xtf32") -> torch.Tensor:
+    """x [M, K] fp32 (unit inner stride), weight [N, K] fp32 -> [M, N] fp32.
+
+    precision "3xtf32": error-compensated hi*hi + hi*lo + lo*hi on the TF32
+    tensor core (~fp32 accuracy); "tf32": one TF32 MMA per k step (the
+    tensor core drops the low 13 mantissa bits of each operand)."""
+    if precision not in ("tf32", "3xtf32"):
+        raise ValueError(f"precision must be 'tf32' or '3xtf32', got {precision!r}")
     if x.dtype != torch.float32 or weight.dtype != torch.float32:
         raise TypeError("linear: only float32 operands are implemented")
     if not x.is_cuda:
@@ -40,7 +46,8 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
         bias.data_ptr() if bias is not None else None,
         out.data_ptr(), out.stride(0), M, N, K,
         _lib.KF_EPI_BIAS_GELU if gelu else _lib.KF_EPI_BIAS,
-        _lib.KF_GEMM_ROUND_TF32 if round_tf32 else 0, bn, 0, 0, _lib.stream_ptr())
+        (_lib.KF_GEMM_ROUND_TF32 if round_tf32 else 0)
+        | (_lib.KF_GEMM_SPLIT3 if precision == "3xtf32" else 0), bn, 0, 0, _lib.stream_ptr())
     _lib.check(rc, "kf_gemm_tf32")
     return out.reshape(*lead, N)
 

@@ -1,0 +1,91 @@
+"""Work and traffic formulas used for roofline fractions.
+
+Useful FLOPs of one forward (the figure `roofline.achieved` uses):
+
+    sum over layers of  2*T*(4d^2 + 2dF)  +  4*d*sum_b L_b(L_b+1)/2
+
+T = sum_b L_b valid tokens; the attention term counts only valid causal
+(query, key) pairs of valid queries, 2*Dh FLOPs each for QK^T and PV over
+all heads. Padded rows, skipped tiles and head-dim padding are not counted,
+so skipping them raises the achieved rate and cannot push it past 100%.
+The dense-causal count (all M = B*S rows, S(S+1)/2 pairs per sequence) is
+the reference's roofline.stack_flops convention (kernelforge/roofline.py:
+96-116, attention halved for causal).
+
+LayerNorm traffic: 16*d bytes per row per add+mask+LN call (read x and y,
+write s and h, fp32), 2L+1 calls per forward (an upper bound: the entry call
+reads no y, the final call writes no s).
+"""
+from __future__ import annotations
+
+import json
+import os
+from typing import Iterable, List, Optional
+
+import torch
+
+
+def lengths_of(mask: Optional[torch.Tensor], B: int, S: int) -> List[int]:
+    if mask is None:
+        return [S] * B
+    return [int(v) for v in mask.to(torch.int64).sum(dim=1).tolist()]
+
+
+def gemm_flops_per_token(cfg) -> float:
+    d, F = cfg.d_model, cfg.ffn_dim
+    return 2.0 * (4 * d * d + 2 * d * F)
+
+
+def attn_pairs(lengths: Iterable[int], causal: bool = True, S: Optional[int] = None) -> float:
+    if causal:
+        return float(sum(n * (n + 1) // 2 for n in lengths))
+    return float(sum(n * n for n in lengths))
+
+
+def useful_flops(cfg, lengths: Iterable[int]) -> float:
+    lengths = list(lengths)
+    T = float(sum(lengths))
+    return cfg.num_layers * (T * gemm_flops_per_token(cfg)
+                             + 4.0 * cfg.d_model * attn_pairs(lengths, cfg.causal))
+
+
+def useful_attention_flops(cfg, lengths: Iterable[int]) -> float:
+    return cfg.num_layers * 4.0 * cfg.d_model * attn_pairs(list(lengths), cfg.causal)
+
+
+def dense_causal_flops(cfg) -> float:
+    B, S = cfg.batch_size, cfg.seq_len
+    M = B * S
+    pairs = B * S * (S + 1) / 2 if cfg.causal else B * S * S
+    return cfg.num_layers * (M * gemm_flops_per_token(cfg) + 4.0 * cfg.d_model * pairs)
+
+
+def norm_bytes(cfg) -> float:
+    M = cfg.batch_size * cfg.seq_len
+    return 16.0 * cfg.d_model * M * (2 * cfg.num_layers + 1)
+
+
+def ln_call_bytes(M: int, d: int, has_y: bool = True, writes_s: bool = True) -> float:
+    return 4.0 * d * M * (1 + int(has_y) + int(writes_s) + 1)
+
+
+def measured_peaks(path: Optional[str] = None) -> dict:
+    """MEASURED_PEAKS.json (driver-written) or the pool's stated fallback.
+    TF32 tensor peak = half the measured dense BF16 GEMM rate (tcgen05 TF32
+    issues at half the BF16 rate)."""
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    path = path or os.path.join(here, "MEASURED_PEAKS.json")
+    out = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+           "source": "fallback"}
+    try:
+        with open(path, encoding="utf-8") as f:
+            blob = json.load(f)
+        for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained"):
+            if k in blob:
+                out[k] = float(blob[k])
+        out["source"] = "measured"
+    except Exception:
+        pass
+    out["tf32_tflops"] = out["bf16_tflops"] / 2.0
+    out["tf32_tflops_sustained"] = out["bf16_tflops_sustained"] / 2.0
+    return out

@@ -1,0 +1,79 @@
+"""The C-ABI library: it builds for sm_100a, loads without a GPU, exports
+every symbol include/kf_sm100.h declares, and rejects bad arguments before
+touching the device. No kernel is launched here. CPU only."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from techjam2026_b200 import _lib, build
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "kf_sm100.h")
+
+
+def declared_symbols():
+    src = open(HEADER, encoding="utf-8").read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(kf_[a-z0-9_]+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def test_header_and_binding_agree():
+    assert declared_symbols() == sorted(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    raw = ctypes.CDLL(build.LIB_PATH)
+    for name in declared_symbols():
+        assert hasattr(raw, name), name
+
+
+def test_library_has_no_libcuda_link_dependency():
+    import subprocess
+    out = subprocess.run(["ldd", build.LIB_PATH], capture_output=True, text=True).stdout
+    assert "libcuda.so" not in out
+
+
+def test_version_and_workspace_size(lib):
+    assert lib.kf_version() == 100
+    assert lib.kf_keep_bits_words(2, 33) == 4
+    assert lib.kf_keep_bits_words(0, 33) == 0
+
+
+def test_invalid_arguments_are_rejected_without_a_device(lib):
+    assert lib.kf_gemm_tf32(None, 4, None, 4, None, None, 4, 4, 4, 4, 0, 0, 0, 0, 0, None) == \
+        _lib.KF_E_INVALID
+    assert b"invalid" in lib.kf_last_error()
+    assert lib.kf_ln_add_mask(None, 8, None, 0, None, None, None, None, 0, None, 8, 4, 8, 1e-5,
+                              0, None) == _lib.KF_E_INVALID
+    assert lib.kf_keep_bits(None, 8, 1, 8, None, None) == _lib.KF_E_INVALID
+    assert lib.kf_flash_fwd_tf32(None, 1, 1, 1, None, 1, 1, 1, None, 1, 1, 1, None, 1, 1, 1,
+                                 None, 1, 1, 1, 64, 64, 0.125, 0, None) == _lib.KF_E_INVALID
+    assert lib.kf_round_tf32(None, None, 4, None) == _lib.KF_E_INVALID
+
+
+def test_unsupported_shapes_are_reported(lib):
+    fake = ctypes.c_void_p(0x1000)   # never dereferenced: rejected by the shape checks
+    rc = lib.kf_gemm_tf32(fake, 6, fake, 6, None, fake, 8, 8, 8, 6, 0, 0, 0, 0, 0, None)
+    assert rc == _lib.KF_E_UNSUPPORTED and b"K % 4" in lib.kf_last_error()
+    rc = lib.kf_flash_fwd_tf32(fake, 64, 64, 64, fake, 64, 64, 64, fake, 64, 64, 64,
+                               fake, 64, 64, 64, None, 1, 1, 8, 48, 48, 0.1, 0, None)
+    assert rc == _lib.KF_E_UNSUPPORTED
+    rc = lib.kf_gemm_tf32(fake, 8, fake, 8, None, fake, 8, 8, 8, 8, 7, 0, 0, 0, 0, None)
+    assert rc == _lib.KF_E_INVALID
+
+
+def test_empty_problems_are_no_ops(lib):
+    fake = ctypes.c_void_p(0x1000)
+    assert lib.kf_gemm_tf32(fake, 8, fake, 8, None, fake, 8, 0, 8, 8, 0, 0, 0, 0, 0, None) == 0
+    assert lib.kf_ln_add_mask(fake, 8, None, 0, None, fake, fake, None, 0, fake, 8, 0, 8, 1e-5,
+                              0, None) == 0

@@ -1,0 +1,53 @@
+"""Dispatch table: sm_100 keys, reference signature format, lookup order
+exact -> nearest -> default (kernelforge/dispatch.py:254-288). CPU only."""
+from __future__ import annotations
+
+import dataclasses
+
+import pytest
+import torch
+
+from techjam2026_b200.configs import WORKLOADS, TransformerConfig, signature
+from techjam2026_b200.dispatch import (CONSERVATIVE_PLAN, DEFAULT_PLAN, DispatchTable, Entry,
+                                       Plan)
+
+
+def test_signature_format_matches_reference():
+    cfg = TransformerConfig(8, 512, 512, 8, 2048, 6, True)
+    assert signature(cfg) == "B8-S512-d512-H8-F2048-L6-causal"
+    assert signature(dataclasses.replace(cfg, causal=False)) == "B8-S512-d512-H8-F2048-L6"
+
+
+def test_shipped_table_covers_every_baseline_config():
+    table = DispatchTable.load("sm_100")
+    for w in WORKLOADS.values():
+        plan, src = table.lookup("sm_100", torch.float32, w.cfg)
+        assert src == "exact", w.name
+
+
+def test_lookup_order():
+    cfg = TransformerConfig(2, 64, 128, 4, 512, 1, True)
+    special = Plan(name="special", bn_qkv=64)
+    t = DispatchTable([Entry(signature(cfg), "float32", "sm_100", special)])
+    assert t.lookup("sm_100a", torch.float32, cfg) == (special, "exact")
+    other = TransformerConfig(2, 64, 128, 4, 512, 2, True)
+    assert t.lookup("sm_100", torch.float32, other) == (CONSERVATIVE_PLAN, "nearest")
+    assert DispatchTable([]).lookup("sm_100", torch.float32, other) == (DEFAULT_PLAN, "default")
+
+
+def test_other_arches_and_dtypes_are_refused():
+    cfg = TransformerConfig(2, 64, 128, 4, 512, 1, True)
+    with pytest.raises(RuntimeError):
+        DispatchTable([]).lookup("sm_90", torch.float32, cfg)
+    with pytest.raises(RuntimeError):
+        DispatchTable([]).lookup("sm_100", torch.float16, cfg)
+
+
+def test_table_round_trips(tmp_path, monkeypatch):
+    import techjam2026_b200.dispatch as D
+    monkeypatch.setattr(D, "TABLE_DIR", str(tmp_path))
+    cfg = TransformerConfig(2, 64, 128, 4, 512, 1, True)
+    t = DispatchTable([Entry(signature(cfg), "float32", "sm_100", Plan(name="x", bn_out=128))])
+    t.save("sm_100")
+    back = DispatchTable.load("sm_100")
+    assert back.lookup("sm_100", torch.float32, cfg)[0] == Plan(name="x", bn_out=128)

@@ -105,10 +105,40 @@ def test_gemm_exact_on_tf32_operands(M, N, K, bn):
     a = tf32_round(torch.randn(M, K, device="cuda"))
     w = tf32_round(torch.randn(N, K, device="cuda") / math.sqrt(K))
     bias = torch.randn(N, device="cuda")
-    out = linear(a, w, bias, bn=bn)
+    out = linear(a, w, bias, bn=bn, precision="tf32")
     ref = a.double() @ w.double().t() + bias.double()
     err = (out.double() - ref).abs().max().item()
     assert err < 1e-4, f"max abs err {err}"
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 64, 32), (517, 384, 512), (4096, 1536, 512),
+                                   (300, 200, 132), (2048, 512, 2048)])
+@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("gelu", [False, True])
+def test_gemm_split3_has_fp32_accuracy(M, N, K, bn, gelu):
+    """3xTF32 on unrounded operands: error at fp32-accumulation level."""
+    torch.manual_seed(M + 7 * N + K)
+    a = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / math.sqrt(K)
+    bias = torch.randn(N, device="cuda")
+    out = linear(a, w, bias, gelu=gelu, bn=bn, precision="3xtf32")
+    ref = a.double() @ w.double().t() + bias.double()
+    if gelu:
+        ref = F.gelu(ref, approximate="none")
+    err = (out.double() - ref).abs().max().item()
+    assert err < 3e-5, f"max abs err {err}"
+
+
+def test_gemm_plain_tf32_is_tf32_level():
+    torch.manual_seed(9)
+    a = torch.randn(1000, 768, device="cuda")
+    w = torch.randn(768, 768, device="cuda") / math.sqrt(768)
+    one = linear(a, w, None, precision="tf32")
+    three = linear(a, w, None, precision="3xtf32")
+    ref = a.double() @ w.double().t()
+    e1 = (one.double() - ref).abs().max().item()
+    e3 = (three.double() - ref).abs().max().item()
+    assert 1e-4 < e1 < 1e-2 and e3 < 3e-5 and e3 < e1 / 50
 
 
 @pytest.mark.parametrize("M,N,K", [(517, 2048, 512), (128, 512, 128)])
@@ -127,7 +157,7 @@ def test_gemm_unrounded_operands_within_tf32_error():
     M, N, K = 1000, 768, 768
     a = torch.randn(M, K, device="cuda")
     w = torch.randn(N, K, device="cuda") / math.sqrt(K)
-    out = linear(a, w, None)
+    out = linear(a, w, None, precision="tf32")
     ref = a.double() @ w.double().t()
     # TF32 keeps 10 explicit mantissa bits: |err| ~ 2^-11 * sqrt(K) * |a||w|
     assert (out.double() - ref).abs().max().item() < 1e-2
