@@ -72,11 +72,15 @@ int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64_t ldy, con
 
 #define KF_GEMM_ROUND_TF32 1 /* round C to TF32 (it only feeds a TF32 MMA) */
 #define KF_GEMM_SPLIT3 2     /* error-compensated 3xTF32: hi*hi + hi*lo + lo*hi
-                                (~fp32 accuracy, 3 MMAs per k step) */
+                                (~2^-20 relative, 3 TF32 MMAs per k step) */
+#define KF_GEMM_BF16X3 4     /* error-compensated BF16x3: bf16 hi/lo split of the
+                                fp32 operands, hi*hi + hi*lo + lo*hi on the BF16
+                                tensor path (~2^-17 relative, 1.5x one TF32
+                                pass); exclusive with KF_GEMM_SPLIT3 */
 
 /* C[M,N] = epilogue(A[M,K] . W[N,K]^T + bias[N]) on tcgen05 TF32 tensor cores
  * with an FP32 TMEM accumulator (nn.Linear layout: W row-major [N,K]).
- * flags: KF_GEMM_ROUND_TF32 | KF_GEMM_SPLIT3.
+ * flags: KF_GEMM_ROUND_TF32 | (KF_GEMM_SPLIT3 or KF_GEMM_BF16X3).
  * `bias` may be null. Requires K % 4 == 0, lda/ldw % 4 == 0 and 16-byte
  * aligned A/W (TMA constraints). `bn` selects the N tile (0 = automatic,
  * 64/128/256). When head_dim > 0, output column n is written to column

@@ -52,6 +52,9 @@ KF_EPI_BIAS = 0
 KF_EPI_BIAS_GELU = 1
 KF_GEMM_ROUND_TF32 = 1
 KF_GEMM_SPLIT3 = 2
+KF_GEMM_BF16X3 = 4
+
+GEMM_PRECISION_FLAGS = {"tf32": 0, "3xtf32": KF_GEMM_SPLIT3, "bf16x3": KF_GEMM_BF16X3}
 KF_ATTN_CAUSAL = 1
 KF_ATTN_SKIP_EMPTY_Q = 2
 KF_ATTN_ROUND_TF32 = 4

@@ -17,19 +17,26 @@
 //               then hand the accumulator back to the MMA warp. Double
 //               buffering lets the epilogue of tile i overlap the main loop of
 //               tile i+1;
-//   warps 6-9   (split mode only) converters: once a stage has landed they
-//               write lo = x - trunc_tf32(x) of both tiles next to them in
-//               shared memory, so the MMA warp can issue the error-compensated
+//   warps 6-9   (split modes only) converters: once a stage has landed they
+//               write a hi/lo split of both fp32 tiles next to them in shared
+//               memory, so the MMA warp can issue the error-compensated
 //               product  A.B ~= hi(A).hi(B) + hi(A).lo(B) + lo(A).hi(B)
-//               (three kind::tf32 MMAs per k step; the tensor core itself
-//               drops the low mantissa bits, so the staged fp32 tile serves
-//               as hi). Error ~2^-20 relative instead of TF32's 2^-11, with no
-//               extra HBM or L2 traffic.
+//               with no extra HBM or L2 traffic:
+//                 3xTF32: lo = x - trunc_tf32(x) (fp32); hi is the staged tile
+//                         itself (the tensor core drops its low 13 bits);
+//                         three kind::tf32 MMAs per 8-wide k step, ~2^-20;
+//                 BF16x3: hi = bf16_rn(x), lo = bf16_rn(x - hi), written as
+//                         64-byte swizzled bf16 rows; three kind::f16 MMAs per
+//                         16-wide k step (BF16 issues at twice the TF32 rate,
+//                         so 1.5x the cost of one TF32 pass), ~2^-17.
+#include <cuda_bf16.h>
+
 #include "kf_common.cuh"
 
 namespace kf {
 
 enum : int { KF_GEMM_VEC_OK = 1 << 8 };
+enum : int { SPLIT_NONE = 0, SPLIT_TF32X3 = 1, SPLIT_BF16X3 = 2 };
 
 template <int BN, int SPLIT>
 struct GemmCfg {
@@ -55,6 +62,53 @@ __device__ __forceinline__ uint32_t tf32_lo_bits(uint32_t x) {
   const float f = __uint_as_float(x);
   const float hi = __uint_as_float(x & 0xFFFFE000u);
   return __float_as_uint(f - hi);
+}
+
+// Instruction descriptor for kind::f16 with BF16 A/B and an FP32 accumulator.
+__host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(__nv_bfloat16 lo_k, __nv_bfloat16 hi_k) {
+  return static_cast<uint32_t>(__bfloat16_as_ushort(lo_k)) |
+         (static_cast<uint32_t>(__bfloat16_as_ushort(hi_k)) << 16);
+}
+
+// Split 8 consecutive k-values of one row of a staged fp32 tile (128-byte
+// rows, 128B swizzle: 16-byte chunk c of row r sits at chunk c ^ (r & 7)) into
+// bf16 hi and lo rows (64-byte rows, 64B swizzle: chunk m of row r sits at
+// chunk m ^ ((r >> 1) & 3)).
+__device__ __forceinline__ void split_bf16_chunk(const uint8_t* f32_tile, uint8_t* hi_tile,
+                                                 uint8_t* lo_tile, int r, int m) {
+  const float4 v0 =
+      *reinterpret_cast<const float4*>(f32_tile + r * 128 + (((2 * m) ^ (r & 7)) << 4));
+  const float4 v1 =
+      *reinterpret_cast<const float4*>(f32_tile + r * 128 + (((2 * m + 1) ^ (r & 7)) << 4));
+  const float x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  __nv_bfloat16 h[8], l[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    h[t] = __float2bfloat16_rn(x[t]);
+    l[t] = __float2bfloat16_rn(x[t] - __bfloat162float(h[t]));
+  }
+  const int dst = r * 64 + ((m ^ ((r >> 1) & 3)) << 4);
+  *reinterpret_cast<uint4*>(hi_tile + dst) =
+      make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]), pack_bf16x2(h[4], h[5]),
+                 pack_bf16x2(h[6], h[7]));
+  *reinterpret_cast<uint4*>(lo_tile + dst) =
+      make_uint4(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]), pack_bf16x2(l[4], l[5]),
+                 pack_bf16x2(l[6], l[7]));
+}
+
+__device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -198,6 +252,7 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
     if (lane == 0) {
       // ------------------------------------------------ MMA issuer
       constexpr uint32_t idesc = make_idesc_tf32(BM, BN, 0, 0);
+      constexpr uint32_t idesc_bf = make_idesc_bf16(BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -221,6 +276,21 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
           const uint32_t b_addr = a_addr + Cfg::A_BYTES;
           const uint32_t alo_addr = b_addr + Cfg::B_BYTES;
           const uint32_t blo_addr = alo_addr + Cfg::A_BYTES;
+          if (SPLIT == SPLIT_BF16X3) {
+            // bf16 tiles: A_hi | A_lo | B_hi | B_lo, 64-byte rows (SW64).
+            const uint32_t ahi = alo_addr, alo = ahi + Cfg::A_BYTES / 2;
+            const uint32_t bhi = alo + Cfg::A_BYTES / 2, blo = bhi + Cfg::B_BYTES / 2;
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint64_t ah = make_smem_desc(ahi + k * 32, 16, 512, KF_SWIZZLE_64B);
+              const uint64_t al = make_smem_desc(alo + k * 32, 16, 512, KF_SWIZZLE_64B);
+              const uint64_t bh = make_smem_desc(bhi + k * 32, 16, 512, KF_SWIZZLE_64B);
+              const uint64_t bl = make_smem_desc(blo + k * 32, 16, 512, KF_SWIZZLE_64B);
+              mma_bf16_ss(d_tmem, al, bh, idesc_bf, (kb | k) != 0 ? 1u : 0u);
+              mma_bf16_ss(d_tmem, ah, bl, idesc_bf, 1u);
+              mma_bf16_ss(d_tmem, ah, bh, idesc_bf, 1u);
+            }
+          } else
 #pragma unroll
           for (int k = 0; k < BK / 8; ++k) {
             const uint64_t ad = make_smem_desc(a_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
@@ -232,6 +302,7 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
               mma_tf32_ss(d_tmem, ad, bld, idesc, 1u);
             }
             mma_tf32_ss(d_tmem, ad, bd, idesc, (SPLIT || (kb | k) != 0) ? 1u : 0u);
+            (void)idesc_bf;
           }
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -262,17 +333,29 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
           ok = false;
           break;
         }
-        const uint4* src = reinterpret_cast<const uint4*>(smem + stage * Cfg::STAGE_BYTES);
-        uint4* dst = reinterpret_cast<uint4*>(smem + stage * Cfg::STAGE_BYTES + Cfg::A_BYTES +
-                                              Cfg::B_BYTES);
+        uint8_t* st_base = smem + stage * Cfg::STAGE_BYTES;
+        if (SPLIT == SPLIT_BF16X3) {
+          uint8_t* ahi = st_base + Cfg::A_BYTES + Cfg::B_BYTES;
+          uint8_t* alo = ahi + Cfg::A_BYTES / 2;
+          uint8_t* bhi = alo + Cfg::A_BYTES / 2;
+          uint8_t* blo = bhi + Cfg::B_BYTES / 2;
+#pragma unroll 2
+          for (int i = ct; i < BM * 4; i += 128) split_bf16_chunk(st_base, ahi, alo, i >> 2, i & 3);
+#pragma unroll 2
+          for (int i = ct; i < BN * 4; i += 128)
+            split_bf16_chunk(st_base + Cfg::A_BYTES, bhi, blo, i >> 2, i & 3);
+        } else {
+          const uint4* src = reinterpret_cast<const uint4*>(st_base);
+          uint4* dst = reinterpret_cast<uint4*>(st_base + Cfg::A_BYTES + Cfg::B_BYTES);
 #pragma unroll 4
-        for (int i = ct; i < (Cfg::A_BYTES + Cfg::B_BYTES) / 16; i += 128) {
-          uint4 v = src[i];
-          v.x = tf32_lo_bits(v.x);
-          v.y = tf32_lo_bits(v.y);
-          v.z = tf32_lo_bits(v.z);
-          v.w = tf32_lo_bits(v.w);
-          dst[i] = v;
+          for (int i = ct; i < (Cfg::A_BYTES + Cfg::B_BYTES) / 16; i += 128) {
+            uint4 v = src[i];
+            v.x = tf32_lo_bits(v.x);
+            v.y = tf32_lo_bits(v.y);
+            v.z = tf32_lo_bits(v.z);
+            v.w = tf32_lo_bits(v.w);
+            dst[i] = v;
+          }
         }
         fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
         __syncwarp();
@@ -435,14 +518,27 @@ extern "C" int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t
   if (vec) f |= KF_GEMM_VEC_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
-  const bool split = (flags & KF_GEMM_SPLIT3) != 0;
+  const int split = (flags & KF_GEMM_BF16X3) ? SPLIT_BF16X3
+                    : (flags & KF_GEMM_SPLIT3)  ? SPLIT_TF32X3
+                                                : SPLIT_NONE;
+  if ((flags & KF_GEMM_BF16X3) && (flags & KF_GEMM_SPLIT3)) {
+    set_last_error("kf_gemm_tf32: KF_GEMM_SPLIT3 and KF_GEMM_BF16X3 are exclusive");
+    return KF_E_INVALID;
+  }
 #define KF_GEMM_CASE(BNV)                                                                     \
   if (bn == BNV) {                                                                            \
-    if (split) {                                                                              \
+    if (split == SPLIT_TF32X3) {                                                              \
       if (epilogue == KF_EPI_BIAS)                                                            \
         return launch_gemm<BNV, KF_EPI_BIAS, 1>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,   \
                                                 head_stride, st);                             \
       return launch_gemm<BNV, KF_EPI_BIAS_GELU, 1>(ta, tb, C, ldc, bias, m, n, k, f,          \
+                                                   head_dim, head_stride, st);                \
+    }                                                                                         \
+    if (split == SPLIT_BF16X3) {                                                              \
+      if (epilogue == KF_EPI_BIAS)                                                            \
+        return launch_gemm<BNV, KF_EPI_BIAS, 2>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,   \
+                                                head_stride, st);                             \
+      return launch_gemm<BNV, KF_EPI_BIAS_GELU, 2>(ta, tb, C, ldc, bias, m, n, k, f,          \
                                                    head_dim, head_stride, st);                \
     }                                                                                         \
     if (epilogue == KF_EPI_BIAS)                                                              \

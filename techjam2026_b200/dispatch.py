@@ -29,14 +29,17 @@ class Plan:
     name: str = "3xtf32-gemm+tf32-attn+graph"
     # Capture the whole multi-layer forward in one CUDA graph.
     cuda_graph: bool = True
-    # Error-compensated 3xTF32 (hi*hi + hi*lo + lo*hi) per GEMM. Plain TF32
-    # everywhere fails the organiser's gate against the fp32 reference on
-    # the 6-layer config (envelope 1.2-1.4); 3xTF32 GEMMs with TF32
-    # attention measure 0.48-0.61.
-    split_qkv: bool = True
-    split_out: bool = True
-    split_ffn1: bool = True
-    split_ffn2: bool = True
+    # Precision of each GEMM: "tf32" (one TF32 pass), "bf16x3" or "3xtf32"
+    # (error-compensated hi*hi + hi*lo + lo*hi). Plain TF32 everywhere fails
+    # the organiser's gate against the fp32 reference on the 6-layer config
+    # (envelope 1.2-1.4); compensated GEMMs with TF32 attention measure
+    # 0.41-0.63 on every config. bf16x3 needs half the MMA work of 3xtf32
+    # but its in-kernel operand split costs more than it saves (measured
+    # 148 vs 226 TFLOP/s on a 16384x4096x1024 GEMM), so 3xtf32 is the default.
+    prec_qkv: str = "3xtf32"
+    prec_out: str = "3xtf32"
+    prec_ffn1: str = "3xtf32"
+    prec_ffn2: str = "3xtf32"
     # Round operands that feed a plain TF32 MMA (attention, and any GEMM not
     # split) to the nearest TF32 value where they are produced, so the tensor
     # core's truncation of the low mantissa bits is a no-op: unbiased operand
@@ -51,10 +54,17 @@ class Plan:
     bn_ffn1: int = 0
     bn_ffn2: int = 0
 
+    def gemm_precisions(self) -> dict:
+        return {"qkv": self.prec_qkv, "out": self.prec_out, "ffn1": self.prec_ffn1,
+                "ffn2": self.prec_ffn2}
+
     def describe(self) -> str:
-        split = [n for n, on in (("qkv", self.split_qkv), ("out", self.split_out),
-                                 ("ffn1", self.split_ffn1), ("ffn2", self.split_ffn2)) if on]
-        bits = [f"3xtf32[{','.join(split)}]" if split else "tf32-gemm", "tf32-attn"]
+        precs = self.gemm_precisions()
+        if len(set(precs.values())) == 1:
+            bits = [f"{self.prec_qkv}-gemm"]
+        else:
+            bits = ["gemm[" + ",".join(f"{k}={v}" for k, v in precs.items()) + "]"]
+        bits.append("tf32-attn")
         if self.round_tf32:
             bits.append("rna-operands")
         if self.skip_empty_queries:

@@ -46,9 +46,9 @@ class _Weights:
     def __init__(self, model: LayerStack, device: torch.device, plan: Plan):
         from .ops.gemm import round_tf32 as rnd
 
-        def prep_w(w: torch.Tensor, split: bool = False) -> torch.Tensor:
+        def prep_w(w: torch.Tensor, prec: str) -> torch.Tensor:
             w = w.detach().to(device=device, dtype=torch.float32).contiguous()
-            return rnd(w) if (plan.round_tf32 and not split) else w.clone()
+            return rnd(w) if (plan.round_tf32 and prec == "tf32") else w.clone()
 
         def prep_b(b: torch.Tensor) -> torch.Tensor:
             return b.detach().to(device=device, dtype=torch.float32).contiguous().clone()
@@ -58,11 +58,11 @@ class _Weights:
             a = layer.attention
             self.layers.append(dict(
                 wqkv=prep_w(torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0),
-                            plan.split_qkv),
+                            plan.prec_qkv),
                 bqkv=prep_b(torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias], 0)),
-                wo=prep_w(a.out_proj.weight, plan.split_out), bo=prep_b(a.out_proj.bias),
-                w1=prep_w(layer.ffn_in.weight, plan.split_ffn1), b1=prep_b(layer.ffn_in.bias),
-                w2=prep_w(layer.ffn_out.weight, plan.split_ffn2), b2=prep_b(layer.ffn_out.bias),
+                wo=prep_w(a.out_proj.weight, plan.prec_out), bo=prep_b(a.out_proj.bias),
+                w1=prep_w(layer.ffn_in.weight, plan.prec_ffn1), b1=prep_b(layer.ffn_in.bias),
+                w2=prep_w(layer.ffn_out.weight, plan.prec_ffn2), b2=prep_b(layer.ffn_out.bias),
                 ln1w=prep_b(layer.norm1.weight), ln1b=prep_b(layer.norm1.bias),
                 ln2w=prep_b(layer.norm2.weight), ln2b=prep_b(layer.norm2.bias),
                 eps1=float(layer.norm1.eps), eps2=float(layer.norm2.eps)))
@@ -173,18 +173,18 @@ class FusedTransformer(LayerStack):
         L = _lib.lib()
         st = _lib.stream_ptr()
         R = plan.round_tf32
+        P = _lib.GEMM_PRECISION_FLAGS
         # Round a producer's output only when its consumer is a plain TF32 MMA.
-        rnd_h1 = _lib.KF_LN_ROUND_TF32 if (R and not plan.split_qkv) else 0
-        rnd_h2 = _lib.KF_LN_ROUND_TF32 if (R and not plan.split_ffn1) else 0
+        rnd_h1 = _lib.KF_LN_ROUND_TF32 if (R and plan.prec_qkv == "tf32") else 0
+        rnd_h2 = _lib.KF_LN_ROUND_TF32 if (R and plan.prec_ffn1 == "tf32") else 0
         rnd_qkv = _lib.KF_GEMM_ROUND_TF32 if R else 0          # feeds attention
-        rnd_gelu = _lib.KF_GEMM_ROUND_TF32 if (R and not plan.split_ffn2) else 0
-        sp = _lib.KF_GEMM_SPLIT3
-        f_qkv = rnd_qkv | (sp if plan.split_qkv else 0)
-        f_out = sp if plan.split_out else 0
-        f_ffn1 = rnd_gelu | (sp if plan.split_ffn1 else 0)
-        f_ffn2 = sp if plan.split_ffn2 else 0
+        rnd_gelu = _lib.KF_GEMM_ROUND_TF32 if (R and plan.prec_ffn2 == "tf32") else 0
+        f_qkv = rnd_qkv | P[plan.prec_qkv]
+        f_out = P[plan.prec_out]
+        f_ffn1 = rnd_gelu | P[plan.prec_ffn1]
+        f_ffn2 = P[plan.prec_ffn2]
         attn_flags = (_lib.KF_ATTN_CAUSAL if cfg.causal else 0) | (
-            _lib.KF_ATTN_ROUND_TF32 if (R and not plan.split_out) else 0)
+            _lib.KF_ATTN_ROUND_TF32 if (R and plan.prec_out == "tf32") else 0)
         keep = keep_u8.data_ptr() if keep_u8 is not None else None
         bits = ws.bits.data_ptr() if keep_u8 is not None else None
         if keep_u8 is not None and plan.skip_empty_queries:

@@ -16,14 +16,17 @@ from .. import _lib
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
            gelu: bool = False, out: Optional[torch.Tensor] = None, round_tf32: bool = False,
-           bn: int = 0, precision: str = "3xtf32") -> torch.Tensor:
+           bn: int = 0, precision: str = "bf16x3") -> torch.Tensor:
     """x [M, K] fp32 (unit inner stride), weight [N, K] fp32 -> [M, N] fp32.
 
-    precision "3xtf32": error-compensated hi*hi + hi*lo + lo*hi on the TF32
-    tensor core (~fp32 accuracy); "tf32": one TF32 MMA per k step (the
-    tensor core drops the low 13 mantissa bits of each operand)."""
-    if precision not in ("tf32", "3xtf32"):
-        raise ValueError(f"precision must be 'tf32' or '3xtf32', got {precision!r}")
+    precision
+      "bf16x3": error-compensated hi*hi + hi*lo + lo*hi of a bf16 hi/lo split
+                on the BF16 tensor path (~2^-17 relative, 1.5x one TF32 pass);
+      "3xtf32": the same compensation with a TF32 split (~2^-20, 3x);
+      "tf32":   one TF32 MMA per k step (the tensor core drops the low 13
+                mantissa bits of each operand, ~2^-11)."""
+    if precision not in _lib.GEMM_PRECISION_FLAGS:
+        raise ValueError(f"precision must be one of {sorted(_lib.GEMM_PRECISION_FLAGS)}")
     if x.dtype != torch.float32 or weight.dtype != torch.float32:
         raise TypeError("linear: only float32 operands are implemented")
     if not x.is_cuda:
@@ -47,7 +50,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
         out.data_ptr(), out.stride(0), M, N, K,
         _lib.KF_EPI_BIAS_GELU if gelu else _lib.KF_EPI_BIAS,
         (_lib.KF_GEMM_ROUND_TF32 if round_tf32 else 0)
-        | (_lib.KF_GEMM_SPLIT3 if precision == "3xtf32" else 0), bn, 0, 0, _lib.stream_ptr())
+        | _lib.GEMM_PRECISION_FLAGS[precision], bn, 0, 0, _lib.stream_ptr())
     _lib.check(rc, "kf_gemm_tf32")
     return out.reshape(*lead, N)
 
