@@ -128,6 +128,35 @@ int kf_flash_fwd_tf32(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm, 
                       int64_t o_sm, const uint32_t* keep_bits, int64_t B, int64_t H, int64_t S,
                       int dh, int dh_out, float sm_scale, int flags, void* stream);
 
+/* ----------------------------------------------------------- no-allocation variant */
+
+/* Capacity of the library's static key-bit scratch: 1 MiB per device. */
+#define KF_NOALLOC_KEEP_WORDS_MAX 262144
+
+/* kf_flash_fwd_tf32 for callers that cannot allocate device memory: code
+ * running inside a global-mode stream capture (cudaMalloc is illegal there),
+ * host functions enqueued with cudaLaunchHostFunc (no CUDA calls allowed) and
+ * hosts whose device memory is a fixed arena they cannot grow. It takes the
+ * uint8 keep mask [B, S] (row stride ld_keep, required) instead of a
+ * kf_keep_bits workspace and packs the key bits into a static device array of
+ * the library (KF_NOALLOC_KEEP_WORDS_MAX words, held on every device that
+ * loads the library until exit); it calls no allocator. B * ceil(S/32) above
+ * the maximum returns KF_E_UNSUPPORTED before any launch. The first call on a
+ * device resolves the array's address with cudaGetSymbolAddress: make it
+ * before any stream capture. All calls share the array: the packer rewrites
+ * every word the kernel reads, so nothing needs clearing, but calls that
+ * overlap on the GPU race -- order them on one stream or with events.
+ * Other arguments, semantics and results as kf_flash_fwd_tf32.
+ * No counterpart in the reference (its flash_attention allocates through
+ * PyTorch). */
+int kf_flash_fwd_tf32_keep_noalloc(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
+                                   const float* k, int64_t k_sb, int64_t k_sh, int64_t k_sm,
+                                   const float* v, int64_t v_sb, int64_t v_sh, int64_t v_sm,
+                                   float* o, int64_t o_sb, int64_t o_sh, int64_t o_sm,
+                                   const uint8_t* keep, int64_t ld_keep, int64_t B, int64_t H,
+                                   int64_t S, int dh, int dh_out, float sm_scale, int flags,
+                                   void* stream);
+
 /* ----------------------------------------------------------- utilities */
 
 /* dst[i] = round_to_tf32(src[i]) for n fp32 values (weight preparation). */

@@ -38,6 +38,12 @@ SIGNATURES = {
                                    _c_ptr, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_float,
                                    _c_int, _c_ptr]),
     "kf_round_tf32": (_c_int, [_c_ptr, _c_ptr, _c_i64, _c_ptr]),
+    "kf_flash_fwd_tf32_keep_noalloc": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64,
+                                                _c_ptr, _c_i64, _c_i64, _c_i64,
+                                                _c_ptr, _c_i64, _c_i64, _c_i64,
+                                                _c_ptr, _c_i64, _c_i64, _c_i64,
+                                                _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64,
+                                                _c_int, _c_int, _c_float, _c_int, _c_ptr]),
 }
 
 # C-ABI constants (include/kf_sm100.h)
@@ -58,6 +64,7 @@ GEMM_PRECISION_FLAGS = {"tf32": 0, "3xtf32": KF_GEMM_SPLIT3, "bf16x3": KF_GEMM_B
 KF_ATTN_CAUSAL = 1
 KF_ATTN_SKIP_EMPTY_Q = 2
 KF_ATTN_ROUND_TF32 = 4
+KF_NOALLOC_KEEP_WORDS_MAX = 262144
 
 _lib = None
 _lock = threading.Lock()

@@ -4,3 +4,4 @@
 #include "ln_sm100.cu"
 #include "gemm_sm100.cu"
 #include "flash_sm100.cu"
+#include "noalloc_sm100.cu"
