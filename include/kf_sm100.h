@@ -52,6 +52,8 @@ int kf_device_status(int reset);
 
 #define KF_LN_MASK_OUT 1   /* zero h on rows whose keep byte is 0 (final norm) */
 #define KF_LN_ROUND_TF32 2 /* round h to TF32 (it only feeds a TF32 GEMM) */
+#define KF_LN_SKIP_PADDED 4 /* leave s and h of padded rows untouched (valid
+                               only when every consumer masks those rows) */
 
 /* Fused residual-add + row mask + LayerNorm over rows of width d:
  *     s = keep[r] ? x[r] + y[r] : 0          (y optional, keep optional)
@@ -78,6 +80,12 @@ int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64_t ldy, con
                                 tensor path (~2^-17 relative, 1.5x one TF32
                                 pass); exclusive with KF_GEMM_SPLIT3 */
 
+/* Compact list of the 128-row tiles of an [M] keep-byte vector that hold at
+ * least one nonzero byte: tiles[0..*count) in ascending order. `tiles` needs
+ * ceil(M/128) entries. Feeds kf_gemm_tf32's live-tile schedule. */
+int kf_live_row_tiles(const uint8_t* keep, int64_t M, int32_t* tiles, int32_t* count,
+                      void* stream);
+
 /* C[M,N] = epilogue(A[M,K] . W[N,K]^T + bias[N]) on tcgen05 TF32 tensor cores
  * with an FP32 TMEM accumulator (nn.Linear layout: W row-major [N,K]).
  * flags: KF_GEMM_ROUND_TF32 | (KF_GEMM_SPLIT3 or KF_GEMM_BF16X3).
@@ -86,12 +94,15 @@ int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64_t ldy, con
  * 64/128/256). When head_dim > 0, output column n is written to column
  * (n / head_dim) * head_stride + n % head_dim of its row (used to zero-pad
  * head_dim 8 to 16 for the attention MMA); columns never written keep their
- * contents.
+ * contents. live_tiles/live_count (both null, or both device pointers from
+ * kf_live_row_tiles): compute only those 128-row tiles; rows of other tiles
+ * keep their contents.
  * Replaces the cuBLAS F.linear calls of kernelforge/optimized.py:441-446
  * (FFN1 + F.gelu, FFN2), :483 (fused QKV) and :573 (out_proj). */
 int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t ldw, const float* bias,
                  float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int flags,
-                 int bn, int head_dim, int head_stride, void* stream);
+                 int bn, int head_dim, int head_stride, const int32_t* live_tiles,
+                 const int32_t* live_count, void* stream);
 
 /* ----------------------------------------------------------- attention */
 

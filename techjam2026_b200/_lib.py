@@ -28,7 +28,8 @@ SIGNATURES = {
                                 _c_int, _c_ptr]),
     "kf_gemm_tf32": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
                               _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int,
-                              _c_ptr]),
+                              _c_ptr, _c_ptr, _c_ptr]),
+    "kf_live_row_tiles": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_ptr, _c_ptr]),
     "kf_keep_bits_words": (ctypes.c_size_t, [_c_i64, _c_i64]),
     "kf_keep_bits": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr]),
     "kf_flash_fwd_tf32": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64,
@@ -54,6 +55,7 @@ KF_E_CUDA = 3
 KF_E_NO_DEVICE = 4
 KF_LN_MASK_OUT = 1
 KF_LN_ROUND_TF32 = 2
+KF_LN_SKIP_PADDED = 4
 KF_EPI_BIAS = 0
 KF_EPI_BIAS_GELU = 1
 KF_GEMM_ROUND_TF32 = 1

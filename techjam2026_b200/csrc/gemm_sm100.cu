@@ -167,7 +167,8 @@ template <int BN, int EPI, int SPLIT>
 __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int M,
-                     int N, int K, int flags, int head_dim, int head_stride) {
+                     int N, int K, int flags, int head_dim, int head_stride,
+                     const int32_t* __restrict__ live_tiles, const int32_t* __restrict__ live_count) {
   using Cfg = GemmCfg<BN, SPLIT>;
   constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -185,8 +186,15 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_n = (N + BN - 1) / BN;
-  const int num_m = (M + BM - 1) / BM;
+  // Optional list of the 128-row tiles that hold at least one live row
+  // (kf_live_row_tiles); other row tiles are not computed and keep their
+  // contents. Every role reads the same list, so they agree on the schedule.
+  const int num_m = live_tiles ? __ldg(live_count) : (M + BM - 1) / BM;
   const int num_tiles = num_m * num_n;
+  auto row0 = [&](int tile) -> int {
+    const int mi = tile / num_n;
+    return (live_tiles ? __ldg(live_tiles + mi) : mi) * BM;
+  };
   const int num_kb = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -222,7 +230,7 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
       long long issued = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / num_n) * BM;
+        const int m0 = row0(tile);
         const int n0 = (tile % num_n) * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, KF_DEV_WAIT_TIMEOUT_TMA)) {
@@ -372,7 +380,7 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int m0 = (tile / num_n) * BM;
+      const int m0 = row0(tile);
       const int n0 = (tile % num_n) * BN;
       if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, KF_DEV_WAIT_TIMEOUT_EPI)) break;
       tc_fence_after();
@@ -409,7 +417,7 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
 template <int BN, int EPI, int SPLIT>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, float* C, int64_t ldc,
                        const float* bias, int M, int N, int K, int flags, int hd, int hs,
-                       cudaStream_t st) {
+                       const int32_t* live_tiles, const int32_t* live_count, cudaStream_t st) {
   using Cfg = GemmCfg<BN, SPLIT>;
   auto kern = gemm_tf32_kernel<BN, EPI, SPLIT>;
   static int attr_set[64] = {0};
@@ -422,10 +430,12 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, float* C, i
     if (e != cudaSuccess) return cuda_status(e, "kf_gemm_tf32: set smem attribute");
     attr_set[dev] = 1;
   }
+  // With a live-tile list the count is only known on the device: launch one
+  // CTA per SM and let CTAs without work exit.
   const int tiles = ((M + Cfg::BM - 1) / Cfg::BM) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, C, ldc, bias, M, N, K, flags, hd,
-                                                     hs);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, C, ldc, bias, M, N, K, flags, hd, hs,
+                                                     live_tiles, live_count);
   return cuda_status(cudaGetLastError(), "kf_gemm_tf32 launch");
 }
 
@@ -456,7 +466,8 @@ using namespace kf;
 extern "C" int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t ldw,
                             const float* bias, float* C, int64_t ldc, int64_t M, int64_t N,
                             int64_t K, int epilogue, int flags, int bn, int head_dim,
-                            int head_stride, void* stream) {
+                            int head_stride, const int32_t* live_tiles,
+                            const int32_t* live_count, void* stream) {
   if (!A || !W || !C || M < 0 || N < 0 || K < 0) {
     set_last_error("kf_gemm_tf32: invalid arguments");
     return KF_E_INVALID;
@@ -485,6 +496,10 @@ extern "C" int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t
   const int64_t out_cols = head_dim > 0 ? ((N + head_dim - 1) / head_dim) * head_stride : N;
   if (ldc < out_cols && M > 1) {
     set_last_error("kf_gemm_tf32: ldc %lld smaller than the output row", (long long)ldc);
+    return KF_E_INVALID;
+  }
+  if ((live_tiles == nullptr) != (live_count == nullptr)) {
+    set_last_error("kf_gemm_tf32: live_tiles and live_count go together");
     return KF_E_INVALID;
   }
   if (bn == 0) bn = choose_bn(M, N);
@@ -530,22 +545,22 @@ extern "C" int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t
     if (split == SPLIT_TF32X3) {                                                              \
       if (epilogue == KF_EPI_BIAS)                                                            \
         return launch_gemm<BNV, KF_EPI_BIAS, 1>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,   \
-                                                head_stride, st);                             \
+                                                head_stride, live_tiles, live_count, st);                             \
       return launch_gemm<BNV, KF_EPI_BIAS_GELU, 1>(ta, tb, C, ldc, bias, m, n, k, f,          \
-                                                   head_dim, head_stride, st);                \
+                                                   head_dim, head_stride, live_tiles, live_count, st);                \
     }                                                                                         \
     if (split == SPLIT_BF16X3) {                                                              \
       if (epilogue == KF_EPI_BIAS)                                                            \
         return launch_gemm<BNV, KF_EPI_BIAS, 2>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,   \
-                                                head_stride, st);                             \
+                                                head_stride, live_tiles, live_count, st);                             \
       return launch_gemm<BNV, KF_EPI_BIAS_GELU, 2>(ta, tb, C, ldc, bias, m, n, k, f,          \
-                                                   head_dim, head_stride, st);                \
+                                                   head_dim, head_stride, live_tiles, live_count, st);                \
     }                                                                                         \
     if (epilogue == KF_EPI_BIAS)                                                              \
       return launch_gemm<BNV, KF_EPI_BIAS, 0>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,     \
-                                              head_stride, st);                               \
+                                              head_stride, live_tiles, live_count, st);                               \
     return launch_gemm<BNV, KF_EPI_BIAS_GELU, 0>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,  \
-                                                 head_stride, st);                            \
+                                                 head_stride, live_tiles, live_count, st);                            \
   }
   KF_GEMM_CASE(64)
   KF_GEMM_CASE(128)

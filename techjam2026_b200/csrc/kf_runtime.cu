@@ -95,6 +95,61 @@ __global__ void keep_bits_kernel(const uint8_t* __restrict__ keep, int64_t ld_ke
   if (lane == 0) bits[warp_global] = m;
 }
 
+// Compact list of the 128-row tiles of [M] keep bytes that hold a live row.
+// One CTA of 1024 threads: each pass flags 1024 tiles, a block-wide prefix
+// sum places the live ones in ascending order.
+__global__ void __launch_bounds__(1024) live_row_tiles_kernel(const uint8_t* __restrict__ keep,
+                                                              int64_t M, int32_t* __restrict__ tiles,
+                                                              int32_t* __restrict__ count) {
+  __shared__ int warp_sums[32];
+  __shared__ int base;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t n_tiles = (M + 127) / 128;
+  if (tid == 0) base = 0;
+  __syncthreads();
+  for (int64_t t0 = 0; t0 < n_tiles; t0 += 1024) {
+    const int64_t t = t0 + tid;
+    int live = 0;
+    if (t < n_tiles) {
+      const int64_t r0 = t * 128;
+      const int64_t r1 = (r0 + 128 < M) ? r0 + 128 : M;
+      if (r1 - r0 == 128 && (reinterpret_cast<uintptr_t>(keep + r0) & 15u) == 0) {
+        const uint4* p = reinterpret_cast<const uint4*>(keep + r0);
+        uint32_t acc = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 v = p[i];
+          acc |= v.x | v.y | v.z | v.w;
+        }
+        live = acc != 0;
+      } else {
+        for (int64_t r = r0; r < r1 && !live; ++r) live = keep[r] != 0;
+      }
+    }
+    // block-wide exclusive prefix sum of `live`
+    const unsigned ballot = __ballot_sync(0xffffffffu, live);
+    const int in_warp = __popc(ballot & ((1u << lane) - 1u));
+    if (lane == 0) warp_sums[warp] = __popc(ballot);
+    __syncthreads();
+    if (warp == 0) {
+      const int v = warp_sums[lane];
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      warp_sums[lane] = incl - v;
+    }
+    __syncthreads();
+    if (live) tiles[base + warp_sums[warp] + in_warp] = static_cast<int32_t>(t);
+    __syncthreads();
+    if (tid == 1023) base += warp_sums[31] + __popc(ballot);
+    __syncthreads();
+  }
+  if (tid == 0) *count = base;
+}
+
 __global__ void round_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst,
                                   int64_t n) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -143,6 +198,16 @@ extern "C" int kf_keep_bits(const uint8_t* keep, int64_t ld_keep, int64_t B, int
   keep_bits_kernel<<<static_cast<unsigned>(blocks), threads, 0,
                      static_cast<cudaStream_t>(stream)>>>(keep, ld_keep, B, S, bits);
   return cuda_status(cudaGetLastError(), "kf_keep_bits launch");
+}
+
+extern "C" int kf_live_row_tiles(const uint8_t* keep, int64_t M, int32_t* tiles, int32_t* count,
+                                 void* stream) {
+  if (!keep || !tiles || !count || M < 0 || M > (int64_t)INT32_MAX * 128) {
+    set_last_error("kf_live_row_tiles: invalid arguments");
+    return KF_E_INVALID;
+  }
+  live_row_tiles_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(keep, M, tiles, count);
+  return cuda_status(cudaGetLastError(), "kf_live_row_tiles launch");
 }
 
 extern "C" int kf_round_tf32(const float* src, float* dst, int64_t n, void* stream) {

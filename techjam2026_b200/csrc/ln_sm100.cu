@@ -38,6 +38,7 @@ __global__ void __launch_bounds__(256) ln_add_mask_vec_kernel(
   if (row >= M) return;
   const int nv4 = d >> 2;
   const bool kept = keep ? (keep[row] != 0) : true;
+  if (!kept && (flags & KF_LN_SKIP_PADDED)) return;
 
   float4 v[NV];
   float sum = 0.f;
@@ -110,6 +111,7 @@ __global__ void __launch_bounds__(256) ln_add_mask_scalar_kernel(
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= M) return;
   const bool kept = keep ? (keep[row] != 0) : true;
+  if (!kept && (flags & KF_LN_SKIP_PADDED)) return;
   auto val = [&](int c) -> float {
     if (!kept) return 0.f;
     float a = x[row * ldx + c];

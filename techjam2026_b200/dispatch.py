@@ -48,6 +48,9 @@ class Plan:
     # Attention writes 0 for query tiles without a valid token instead of
     # computing them (those rows are masked right after out_proj).
     skip_empty_queries: bool = True
+    # GEMMs compute only 128-row tiles holding a real token and the non-final
+    # norms leave padded rows untouched (every consumer masks those rows).
+    skip_padded_rows: bool = True
     # N tile of each GEMM (0 = pick by wave quantisation at launch).
     bn_qkv: int = 0
     bn_out: int = 0
@@ -69,6 +72,8 @@ class Plan:
             bits.append("rna-operands")
         if self.skip_empty_queries:
             bits.append("skip-empty-q")
+        if self.skip_padded_rows:
+            bits.append("skip-padded-rows")
         if self.cuda_graph:
             bits.append("cuda-graph")
         tiles = (self.bn_qkv, self.bn_out, self.bn_ffn1, self.bn_ffn2)

@@ -73,8 +73,11 @@ class _Weights:
 
 class _Workspace:
     """Activation buffers for one (B, S): allocated once, reused every call.
-    The QKV buffer is zeroed once so head-padding columns (head_dim 8 stored
-    as 16) stay exactly zero."""
+
+    Zeroed once at allocation: the head-padding columns of the QKV buffer
+    (head_dim 8 stored as 16) must stay exactly zero, and rows of padded
+    tokens that the plan skips keep whatever an earlier call left -- always
+    finite values, so a masked key (P = 0) times its stale V stays 0."""
 
     def __init__(self, cfg, B: int, S: int, device: torch.device):
         d, F, H = cfg.d_model, cfg.ffn_dim, cfg.num_heads
@@ -82,18 +85,22 @@ class _Workspace:
         self.dh_store = max(16, self.dh)
         M = B * S
         f32 = dict(dtype=torch.float32, device=device)
-        self.res = torch.empty(M, d, **f32)
-        self.h = torch.empty(M, d, **f32)
+        self.res = torch.zeros(M, d, **f32)
+        self.h = torch.zeros(M, d, **f32)
         self.qkv = torch.zeros(M, 3 * H * self.dh_store, **f32)
-        self.ctx = torch.empty(M, d, **f32)
-        self.y = torch.empty(M, d, **f32)
-        self.ffn = torch.empty(M, F, **f32)
+        self.ctx = torch.zeros(M, d, **f32)
+        self.y = torch.zeros(M, d, **f32)
+        self.ffn = torch.zeros(M, F, **f32)
         words = (S + 31) // 32
-        self.bits = torch.empty(B * words, dtype=torch.int32, device=device)
+        i32 = dict(dtype=torch.int32, device=device)
+        self.bits = torch.zeros(B * words, **i32)
+        self.live_tiles = torch.zeros((M + 127) // 128, **i32)
+        self.live_count = torch.zeros(1, **i32)
 
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size()
-                   for t in (self.res, self.h, self.qkv, self.ctx, self.y, self.ffn, self.bits))
+                   for t in (self.res, self.h, self.qkv, self.ctx, self.y, self.ffn, self.bits,
+                             self.live_tiles, self.live_count))
 
 
 class FusedTransformer(LayerStack):
@@ -189,6 +196,14 @@ class FusedTransformer(LayerStack):
         bits = ws.bits.data_ptr() if keep_u8 is not None else None
         if keep_u8 is not None and plan.skip_empty_queries:
             attn_flags |= _lib.KF_ATTN_SKIP_EMPTY_Q
+        # Padded rows: GEMMs compute only 128-row tiles holding a real token
+        # and the (non-final) norms leave padded rows alone.
+        skip_rows = keep_u8 is not None and plan.skip_padded_rows
+        lt = ws.live_tiles.data_ptr() if skip_rows else None
+        lc = ws.live_count.data_ptr() if skip_rows else None
+        ln_skip = _lib.KF_LN_SKIP_PADDED if skip_rows else 0
+        rnd_h1 |= ln_skip
+        rnd_h2 |= ln_skip
         res, h, y, ctx, ffn, qkv = (ws.res.data_ptr(), ws.h.data_ptr(), ws.y.data_ptr(),
                                     ws.ctx.data_ptr(), ws.ffn.data_ptr(), ws.qkv.data_ptr())
         ldq = 3 * H * dhs
@@ -207,24 +222,26 @@ class FusedTransformer(LayerStack):
 
         if keep is not None:
             run("keep_bits", L.kf_keep_bits, keep, S, B, S, bits, st)
+        if skip_rows:
+            run("keep_bits", L.kf_live_row_tiles, keep, M, lt, lc, st)
         l0 = w.layers[0]
         run("ln", L.kf_ln_add_mask, x.data_ptr(), d, None, 0, keep, l0["ln1w"].data_ptr(),
             l0["ln1b"].data_ptr(), res, d, h, d, M, d, l0["eps1"], rnd_h1, st)
         nl = len(w.layers)
         for i, lw in enumerate(w.layers):
             run("qkv", L.kf_gemm_tf32, h, d, lw["wqkv"].data_ptr(), d, lw["bqkv"].data_ptr(),
-                qkv, ldq, M, 3 * d, d, _lib.KF_EPI_BIAS, f_qkv, plan.bn_qkv, hd, hs, st)
+                qkv, ldq, M, 3 * d, d, _lib.KF_EPI_BIAS, f_qkv, plan.bn_qkv, hd, hs, lt, lc, st)
             run("attention", L.kf_flash_fwd_tf32, qkv, S * ldq, dhs, ldq,
                 qkv + 4 * H * dhs, S * ldq, dhs, ldq, qkv + 8 * H * dhs, S * ldq, dhs, ldq,
                 ctx, S * d, dh, d, bits, B, H, S, dhs, dh, dh ** -0.5, attn_flags, st)
             run("out_proj", L.kf_gemm_tf32, ctx, d, lw["wo"].data_ptr(), d, lw["bo"].data_ptr(),
-                y, d, M, d, d, _lib.KF_EPI_BIAS, f_out, plan.bn_out, 0, 0, st)
+                y, d, M, d, d, _lib.KF_EPI_BIAS, f_out, plan.bn_out, 0, 0, lt, lc, st)
             run("ln", L.kf_ln_add_mask, res, d, y, d, keep, lw["ln2w"].data_ptr(),
                 lw["ln2b"].data_ptr(), res, d, h, d, M, d, lw["eps2"], rnd_h2, st)
             run("ffn1", L.kf_gemm_tf32, h, d, lw["w1"].data_ptr(), d, lw["b1"].data_ptr(), ffn,
-                F, M, F, d, _lib.KF_EPI_BIAS_GELU, f_ffn1, plan.bn_ffn1, 0, 0, st)
+                F, M, F, d, _lib.KF_EPI_BIAS_GELU, f_ffn1, plan.bn_ffn1, 0, 0, lt, lc, st)
             run("ffn2", L.kf_gemm_tf32, ffn, F, lw["w2"].data_ptr(), F, lw["b2"].data_ptr(), y,
-                d, M, d, F, _lib.KF_EPI_BIAS, f_ffn2, plan.bn_ffn2, 0, 0, st)
+                d, M, d, F, _lib.KF_EPI_BIAS, f_ffn2, plan.bn_ffn2, 0, 0, lt, lc, st)
             if i == nl - 1:
                 run("ln", L.kf_ln_add_mask, res, d, y, d, keep, w.finw.data_ptr(),
                     w.finb.data_ptr(), None, 0, out.data_ptr(), d, M, d, w.fin_eps,

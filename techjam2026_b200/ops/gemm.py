@@ -50,7 +50,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
         out.data_ptr(), out.stride(0), M, N, K,
         _lib.KF_EPI_BIAS_GELU if gelu else _lib.KF_EPI_BIAS,
         (_lib.KF_GEMM_ROUND_TF32 if round_tf32 else 0)
-        | _lib.GEMM_PRECISION_FLAGS[precision], bn, 0, 0, _lib.stream_ptr())
+        | _lib.GEMM_PRECISION_FLAGS[precision], bn, 0, 0, None, None, _lib.stream_ptr())
     _lib.check(rc, "kf_gemm_tf32")
     return out.reshape(*lead, N)
 

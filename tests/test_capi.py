@@ -50,7 +50,7 @@ def test_version_and_workspace_size(lib):
 
 
 def test_invalid_arguments_are_rejected_without_a_device(lib):
-    assert lib.kf_gemm_tf32(None, 4, None, 4, None, None, 4, 4, 4, 4, 0, 0, 0, 0, 0, None) == \
+    assert lib.kf_gemm_tf32(None, 4, None, 4, None, None, 4, 4, 4, 4, 0, 0, 0, 0, 0, None, None, None) == \
         _lib.KF_E_INVALID
     assert b"invalid" in lib.kf_last_error()
     assert lib.kf_ln_add_mask(None, 8, None, 0, None, None, None, None, 0, None, 8, 4, 8, 1e-5,
@@ -63,17 +63,17 @@ def test_invalid_arguments_are_rejected_without_a_device(lib):
 
 def test_unsupported_shapes_are_reported(lib):
     fake = ctypes.c_void_p(0x1000)   # never dereferenced: rejected by the shape checks
-    rc = lib.kf_gemm_tf32(fake, 6, fake, 6, None, fake, 8, 8, 8, 6, 0, 0, 0, 0, 0, None)
+    rc = lib.kf_gemm_tf32(fake, 6, fake, 6, None, fake, 8, 8, 8, 6, 0, 0, 0, 0, 0, None, None, None)
     assert rc == _lib.KF_E_UNSUPPORTED and b"K % 4" in lib.kf_last_error()
     rc = lib.kf_flash_fwd_tf32(fake, 64, 64, 64, fake, 64, 64, 64, fake, 64, 64, 64,
                                fake, 64, 64, 64, None, 1, 1, 8, 48, 48, 0.1, 0, None)
     assert rc == _lib.KF_E_UNSUPPORTED
-    rc = lib.kf_gemm_tf32(fake, 8, fake, 8, None, fake, 8, 8, 8, 8, 7, 0, 0, 0, 0, None)
+    rc = lib.kf_gemm_tf32(fake, 8, fake, 8, None, fake, 8, 8, 8, 8, 7, 0, 0, 0, 0, None, None, None)
     assert rc == _lib.KF_E_INVALID
 
 
 def test_empty_problems_are_no_ops(lib):
     fake = ctypes.c_void_p(0x1000)
-    assert lib.kf_gemm_tf32(fake, 8, fake, 8, None, fake, 8, 0, 8, 8, 0, 0, 0, 0, 0, None) == 0
+    assert lib.kf_gemm_tf32(fake, 8, fake, 8, None, fake, 8, 0, 8, 8, 0, 0, 0, 0, 0, None, None, None) == 0
     assert lib.kf_ln_add_mask(fake, 8, None, 0, None, fake, fake, None, 0, fake, 8, 0, 8, 1e-5,
                               0, None) == 0

@@ -177,7 +177,7 @@ def test_gemm_head_padded_output():
     w = tf32_round(torch.randn(N, K, device="cuda") / math.sqrt(K))
     out = torch.full((M, 3 * 16 * 16), 7.0, device="cuda")
     rc = _lib.lib().kf_gemm_tf32(a.data_ptr(), K, w.data_ptr(), K, None, out.data_ptr(),
-                                 out.stride(0), M, N, K, 0, 0, 0, 8, 16, _lib.stream_ptr())
+                                 out.stride(0), M, N, K, 0, 0, 0, 8, 16, None, None, _lib.stream_ptr())
     _lib.check(rc, "kf_gemm_tf32")
     ref = (a.double() @ w.double().t()).view(M, 48, 8)
     got = out.view(M, 48, 16)
@@ -272,3 +272,69 @@ def test_flash_long_sequence_causal_padded():
 def test_device_status_clean_after_kernels():
     from techjam2026_b200 import _lib
     assert _lib.lib().kf_device_status(0) == 0
+
+
+# --------------------------------------------------------------- padded-row skipping
+
+def _live_tiles(keep_u8):
+    from techjam2026_b200 import _lib
+    M = keep_u8.numel()
+    tiles = torch.full(((M + 127) // 128,), -1, dtype=torch.int32, device="cuda")
+    count = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.check(_lib.lib().kf_live_row_tiles(keep_u8.data_ptr(), M, tiles.data_ptr(),
+                                            count.data_ptr(), _lib.stream_ptr()),
+               "kf_live_row_tiles")
+    return tiles, count
+
+
+@pytest.mark.parametrize("M", [1, 127, 128, 4096, 131072 + 77])
+def test_live_row_tiles_lists_exactly_the_tiles_with_a_real_row(M):
+    g = torch.Generator().manual_seed(M)
+    keep = (torch.rand(M, generator=g) < 0.002).to(torch.uint8)
+    keep[: min(M, 5)] = 1 if M > 300 else keep[: min(M, 5)]
+    tiles, count = _live_tiles(keep.cuda())
+    want = [t for t in range((M + 127) // 128) if bool(keep[t * 128:(t + 1) * 128].any())]
+    n = int(count.item())
+    assert tiles[:n].tolist() == want
+
+
+def test_gemm_computes_only_live_row_tiles():
+    from techjam2026_b200 import _lib
+    torch.manual_seed(6)
+    M, N, K = 1000, 384, 256
+    a = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / math.sqrt(K)
+    keep = torch.zeros(M, dtype=torch.uint8, device="cuda")
+    keep[5] = 1          # tile 0
+    keep[300:310] = 1    # tile 2
+    keep[999] = 1        # tile 7 (ragged last tile)
+    tiles, count = _live_tiles(keep)
+    out = torch.full((M, N), 7.0, device="cuda")
+    rc = _lib.lib().kf_gemm_tf32(a.data_ptr(), K, w.data_ptr(), K, None, out.data_ptr(), N, M,
+                                 N, K, 0, _lib.KF_GEMM_SPLIT3, 0, 0, 0, tiles.data_ptr(),
+                                 count.data_ptr(), _lib.stream_ptr())
+    _lib.check(rc, "kf_gemm_tf32")
+    ref = a.double() @ w.double().t()
+    for t in range(8):
+        rows = slice(t * 128, min(M, (t + 1) * 128))
+        if t in (0, 2, 7):
+            assert (out[rows].double() - ref[rows]).abs().max().item() < 2e-4
+        else:
+            assert torch.all(out[rows] == 7.0)
+
+
+def test_layernorm_skip_padded_leaves_padded_rows_untouched():
+    from techjam2026_b200 import _lib
+    M, d = 64, 128
+    x = torch.randn(M, d, device="cuda")
+    keep = (torch.arange(M, device="cuda") % 3 != 0).to(torch.uint8)
+    w, b = torch.ones(d, device="cuda"), torch.zeros(d, device="cuda")
+    s = torch.full((M, d), 5.0, device="cuda")
+    h = torch.full((M, d), 6.0, device="cuda")
+    rc = _lib.lib().kf_ln_add_mask(x.data_ptr(), d, None, 0, keep.data_ptr(), w.data_ptr(),
+                                   b.data_ptr(), s.data_ptr(), d, h.data_ptr(), d, M, d, 1e-5,
+                                   _lib.KF_LN_SKIP_PADDED, _lib.stream_ptr())
+    _lib.check(rc, "kf_ln_add_mask")
+    dead = keep == 0
+    assert torch.all(s[dead] == 5.0) and torch.all(h[dead] == 6.0)
+    assert torch.equal(s[~dead], x[~dead])
