@@ -13,10 +13,13 @@
 //               and releases the smem stage with tcgen05.commit;
 //   warps 2-5   epilogue: tcgen05.ld the accumulator of a finished tile (warp w
 //               owns TMEM lanes 32*(w%4)..+31 = 32 output rows), add bias,
-//               optionally GELU(erf) and TF32 rounding, store fp32 to HBM,
-//               then hand the accumulator back to the MMA warp. Double
-//               buffering lets the epilogue of tile i overlap the main loop of
-//               tile i+1;
+//               optionally GELU(erf) and TF32 rounding, then write each
+//               128x32 chunk into a 128B-swizzled shared buffer and store it
+//               with one TMA bulk store (two buffers in flight), so global
+//               writes are full lines instead of one 16-byte piece per row
+//               per thread; then hand the accumulator back to the MMA warp.
+//               Double buffering lets the epilogue of tile i overlap the main
+//               loop of tile i+1;
 //   warps 6-9   (split modes only) converters: once a stage has landed they
 //               write a hi/lo split of both fp32 tiles next to them in shared
 //               memory, so the MMA warp can issue the error-compensated
@@ -31,11 +34,13 @@
 //                         so 1.5x the cost of one TF32 pass), ~2^-17.
 #include <cuda_bf16.h>
 
+#include <cstring>
+
 #include "kf_common.cuh"
 
 namespace kf {
 
-enum : int { KF_GEMM_VEC_OK = 1 << 8 };
+enum : int { KF_GEMM_VEC_OK = 1 << 8, KF_GEMM_TMA_OUT = 1 << 9 };
 enum : int { SPLIT_NONE = 0, SPLIT_TF32X3 = 1, SPLIT_BF16X3 = 2 };
 
 template <int BN, int SPLIT>
@@ -50,10 +55,13 @@ struct GemmCfg {
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int THREADS = SPLIT ? 320 : 192;
   static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int EPI_BUF_BYTES = BM * 32 * 4;  // one 128x32 fp32 output chunk
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = EPI_OFF + 2 * EPI_BUF_BYTES;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static constexpr int SMEM_BYTES = BAR_OFF + BAR_BYTES + 1024;
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
-  static_assert(STAGES >= 2, "stages");
+  static_assert(STAGES >= 2 && STAGES <= 8, "stages");
   static_assert(SMEM_BYTES <= 232448, "smem");
 };
 
@@ -166,7 +174,7 @@ __device__ __forceinline__ void gemm_store_chunk(const float (&v)[32], float* __
 template <int BN, int EPI, int SPLIT>
 __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int M,
+                     const __grid_constant__ CUtensorMap tmC, float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int M,
                      int N, int K, int flags, int head_dim, int head_stride,
                      const int32_t* __restrict__ live_tiles, const int32_t* __restrict__ live_count) {
   using Cfg = GemmCfg<BN, SPLIT>;
@@ -174,7 +182,7 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
   uint64_t* empty = full + STAGES;
   uint64_t* conv = empty + STAGES;  // split mode: lo tiles written
   uint64_t* acc_full = conv + STAGES;
@@ -182,6 +190,7 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* epi_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -212,6 +221,7 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (flags & KF_GEMM_TMA_OUT) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -377,14 +387,25 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
   } else {
     // -------------------------------------------------- epilogue (warps 2..5)
     const int quarter = warp & 3;
+    const bool tma_out = (flags & KF_GEMM_TMA_OUT) != 0;
+    const bool leader = threadIdx.x == 64;
+    const bool rnd = (flags & KF_GEMM_ROUND_TF32) != 0;
+    int chunk = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m0 = row0(tile);
       const int n0 = (tile % num_n) * BN;
-      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, KF_DEV_WAIT_TIMEOUT_EPI)) break;
+      // One bounded wait by the leader, shared through the named barrier, so
+      // all four warps always reach the same barriers (no warp can be left
+      // waiting for one that gave up).
+      if (leader) *epi_ok = mbar_wait(&acc_full[acc], acc_phase, abort_flag,
+                                      KF_DEV_WAIT_TIMEOUT_EPI) ? 1 : 0;
+      named_bar_sync(1, 128);
+      if (!*epi_ok) break;
       tc_fence_after();
-      const int row = m0 + quarter * 32 + lane;
+      const int r = quarter * 32 + lane;
+      const int row = m0 + r;
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       float* crow = C + static_cast<int64_t>(row) * ldc;
@@ -393,16 +414,52 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
         if (n0 + c >= N) break;  // warp-uniform
         float v[32];
         tmem_ld32(tbase + static_cast<uint32_t>(c), v);
-        if (row < M) gemm_store_chunk<EPI>(v, crow, bias, n0 + c, N, flags, head_dim, head_stride);
+        if (tma_out) {
+          uint8_t* buf = smem + Cfg::EPI_OFF + (chunk & 1) * Cfg::EPI_BUF_BYTES;
+          if (leader) bulk_wait_group_read<1>();  // the store that used `buf` is done reading
+          named_bar_sync(1, 128);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int col = n0 + c + 4 * j;
+            float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (bias && col < N) bb = __ldg(reinterpret_cast<const float4*>(bias + col));
+            float4 o = make_float4(v[4 * j] + bb.x, v[4 * j + 1] + bb.y, v[4 * j + 2] + bb.z,
+                                   v[4 * j + 3] + bb.w);
+            if (EPI == KF_EPI_BIAS_GELU) {
+              o.x = gelu_erf(o.x);
+              o.y = gelu_erf(o.y);
+              o.z = gelu_erf(o.z);
+              o.w = gelu_erf(o.w);
+            }
+            if (rnd) {
+              o.x = round_tf32(o.x);
+              o.y = round_tf32(o.y);
+              o.z = round_tf32(o.z);
+              o.w = round_tf32(o.w);
+            }
+            *reinterpret_cast<float4*>(buf + r * 128 + ((j ^ (r & 7)) << 4)) = o;
+          }
+          fence_proxy_async_smem();  // generic smem writes -> TMA store reads
+          named_bar_sync(1, 128);
+          if (leader) {
+            tma_store_2d(&tmC, buf, n0 + c, m0);
+            bulk_commit_group();
+          }
+          ++chunk;
+        } else if (row < M) {
+          gemm_store_chunk<EPI>(v, crow, bias, n0 + c, N, flags, head_dim, head_stride);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      named_bar_sync(1, 128);  // everyone has read *epi_ok before it is rewritten
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
+    if (tma_out && leader) bulk_wait_group_all();
   }
 
   tc_fence_before();
@@ -415,7 +472,8 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
 }
 
 template <int BN, int EPI, int SPLIT>
-static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, float* C, int64_t ldc,
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                       float* C, int64_t ldc,
                        const float* bias, int M, int N, int K, int flags, int hd, int hs,
                        const int32_t* live_tiles, const int32_t* live_count, cudaStream_t st) {
   using Cfg = GemmCfg<BN, SPLIT>;
@@ -434,8 +492,8 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, float* C, i
   // CTA per SM and let CTAs without work exit.
   const int tiles = ((M + Cfg::BM - 1) / Cfg::BM) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, C, ldc, bias, M, N, K, flags, hd, hs,
-                                                     live_tiles, live_count);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tc, C, ldc, bias, M, N, K, flags, hd,
+                                                     hs, live_tiles, live_count);
   return cuda_status(cudaGetLastError(), "kf_gemm_tf32 launch");
 }
 
@@ -531,6 +589,18 @@ extern "C" int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t
                    !(reinterpret_cast<uintptr_t>(bias) & 15u) &&
                    (head_dim == 0 || (head_dim % 4 == 0 && head_stride % 4 == 0));
   if (vec) f |= KF_GEMM_VEC_OK;
+  // TMA-store epilogue for plain row-major outputs (the head-padded scatter
+  // and unaligned outputs keep direct stores).
+  CUtensorMap tcm;
+  memset(&tcm, 0, sizeof(tcm));
+  if (vec && head_dim == 0 && (ldc * 4) % 16 == 0) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldc) * 4};
+    const uint32_t box[2] = {32, 128};
+    if (encode_tensor_map(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, C, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B) == KF_OK)
+      f |= KF_GEMM_TMA_OUT;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
   const int split = (flags & KF_GEMM_BF16X3) ? SPLIT_BF16X3
@@ -544,22 +614,22 @@ extern "C" int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t
   if (bn == BNV) {                                                                            \
     if (split == SPLIT_TF32X3) {                                                              \
       if (epilogue == KF_EPI_BIAS)                                                            \
-        return launch_gemm<BNV, KF_EPI_BIAS, 1>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,   \
+        return launch_gemm<BNV, KF_EPI_BIAS, 1>(ta, tb, tcm, C, ldc, bias, m, n, k, f, head_dim,   \
                                                 head_stride, live_tiles, live_count, st);                             \
-      return launch_gemm<BNV, KF_EPI_BIAS_GELU, 1>(ta, tb, C, ldc, bias, m, n, k, f,          \
+      return launch_gemm<BNV, KF_EPI_BIAS_GELU, 1>(ta, tb, tcm, C, ldc, bias, m, n, k, f,          \
                                                    head_dim, head_stride, live_tiles, live_count, st);                \
     }                                                                                         \
     if (split == SPLIT_BF16X3) {                                                              \
       if (epilogue == KF_EPI_BIAS)                                                            \
-        return launch_gemm<BNV, KF_EPI_BIAS, 2>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,   \
+        return launch_gemm<BNV, KF_EPI_BIAS, 2>(ta, tb, tcm, C, ldc, bias, m, n, k, f, head_dim,   \
                                                 head_stride, live_tiles, live_count, st);                             \
-      return launch_gemm<BNV, KF_EPI_BIAS_GELU, 2>(ta, tb, C, ldc, bias, m, n, k, f,          \
+      return launch_gemm<BNV, KF_EPI_BIAS_GELU, 2>(ta, tb, tcm, C, ldc, bias, m, n, k, f,          \
                                                    head_dim, head_stride, live_tiles, live_count, st);                \
     }                                                                                         \
     if (epilogue == KF_EPI_BIAS)                                                              \
-      return launch_gemm<BNV, KF_EPI_BIAS, 0>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,     \
+      return launch_gemm<BNV, KF_EPI_BIAS, 0>(ta, tb, tcm, C, ldc, bias, m, n, k, f, head_dim,     \
                                               head_stride, live_tiles, live_count, st);                               \
-    return launch_gemm<BNV, KF_EPI_BIAS_GELU, 0>(ta, tb, C, ldc, bias, m, n, k, f, head_dim,  \
+    return launch_gemm<BNV, KF_EPI_BIAS_GELU, 0>(ta, tb, tcm, C, ldc, bias, m, n, k, f, head_dim,  \
                                                  head_stride, live_tiles, live_count, st);                            \
   }
   KF_GEMM_CASE(64)
