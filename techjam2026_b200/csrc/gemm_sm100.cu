@@ -20,7 +20,7 @@
 //               per thread; then hand the accumulator back to the MMA warp.
 //               Double buffering lets the epilogue of tile i overlap the main
 //               loop of tile i+1;
-//   warps 6-9   (split modes only) converters: once a stage has landed they
+//   warps 6-13  (split modes only) converters: once a stage has landed they
 //               write a hi/lo split of both fp32 tiles next to them in shared
 //               memory, so the MMA warp can issue the error-compensated
 //               product  A.B ~= hi(A).hi(B) + hi(A).lo(B) + lo(A).hi(B)
@@ -53,7 +53,8 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (SPLIT ? 2 : 1);
   static constexpr int STAGES_FIT = 196608 / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
-  static constexpr int THREADS = SPLIT ? 320 : 192;
+  static constexpr int CONV_THREADS = 256;  // split modes: 8 converter warps
+  static constexpr int THREADS = SPLIT ? 192 + CONV_THREADS : 192;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int EPI_BUF_BYTES = BM * 32 * 4;  // one 128x32 fp32 output chunk
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
@@ -172,7 +173,7 @@ __device__ __forceinline__ void gemm_store_chunk(const float (&v)[32], float* __
 }
 
 template <int BN, int EPI, int SPLIT>
-__global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
+__global__ void __launch_bounds__(SPLIT ? 448 : 192, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int M,
                      int N, int K, int flags, int head_dim, int head_stride,
@@ -210,7 +211,7 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&conv[s], 4);
+      mbar_init(&conv[s], Cfg::CONV_THREADS / 32);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
@@ -358,21 +359,26 @@ __global__ void __launch_bounds__(SPLIT ? 320 : 192, 1)
           uint8_t* bhi = alo + Cfg::A_BYTES / 2;
           uint8_t* blo = bhi + Cfg::B_BYTES / 2;
 #pragma unroll 2
-          for (int i = ct; i < BM * 4; i += 128) split_bf16_chunk(st_base, ahi, alo, i >> 2, i & 3);
+          for (int i = ct; i < BM * 4; i += Cfg::CONV_THREADS)
+            split_bf16_chunk(st_base, ahi, alo, i >> 2, i & 3);
 #pragma unroll 2
-          for (int i = ct; i < BN * 4; i += 128)
+          for (int i = ct; i < BN * 4; i += Cfg::CONV_THREADS)
             split_bf16_chunk(st_base + Cfg::A_BYTES, bhi, blo, i >> 2, i & 3);
         } else {
           const uint4* src = reinterpret_cast<const uint4*>(st_base);
           uint4* dst = reinterpret_cast<uint4*>(st_base + Cfg::A_BYTES + Cfg::B_BYTES);
-#pragma unroll 4
-          for (int i = ct; i < (Cfg::A_BYTES + Cfg::B_BYTES) / 16; i += 128) {
-            uint4 v = src[i];
-            v.x = tf32_lo_bits(v.x);
-            v.y = tf32_lo_bits(v.y);
-            v.z = tf32_lo_bits(v.z);
-            v.w = tf32_lo_bits(v.w);
-            dst[i] = v;
+          constexpr int NV = (Cfg::A_BYTES + Cfg::B_BYTES) / 16 / Cfg::CONV_THREADS;
+          static_assert(NV * 16 * Cfg::CONV_THREADS == Cfg::A_BYTES + Cfg::B_BYTES, "split");
+          uint4 v[NV];
+#pragma unroll
+          for (int t = 0; t < NV; ++t) v[t] = src[ct + t * Cfg::CONV_THREADS];  // all loads in flight
+#pragma unroll
+          for (int t = 0; t < NV; ++t) {
+            v[t].x = tf32_lo_bits(v[t].x);
+            v[t].y = tf32_lo_bits(v[t].y);
+            v[t].z = tf32_lo_bits(v[t].z);
+            v[t].w = tf32_lo_bits(v[t].w);
+            dst[ct + t * Cfg::CONV_THREADS] = v[t];
           }
         }
         fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
