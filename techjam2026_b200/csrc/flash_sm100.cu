@@ -26,7 +26,7 @@
 
 namespace kf {
 
-template <int DH, int BN, int KST, int VST>
+template <int DH, int BN, int KST, int VST, int MINB = 1>
 struct FlashCfg {
   static constexpr int BM = 128;
   static constexpr int RB = (DH * 4 < 128) ? DH * 4 : 128;  // bytes per swizzle row
@@ -47,12 +47,17 @@ struct FlashCfg {
   static constexpr int V_OFF = K_OFF + KST * KV_BYTES;
   static constexpr int BAR_OFF = V_OFF + VST * V_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
-  static constexpr int TMEM_COLS = 512;
+  // Power-of-two TMEM allocation covering two S buffers and O; with MINB CTAs
+  // per SM the allocations must fit the SM's 512 columns together.
+  static constexpr int TMEM_NEED = 2 * BN + DH;
+  static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64
+                                 : TMEM_NEED <= 128 ? 128 : TMEM_NEED <= 256 ? 256 : 512;
   static constexpr int O_COL = 2 * BN;
   static_assert(DH >= 16 && DH <= 256 && (DH & (DH - 1)) == 0, "DH");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "BN");
   static_assert(2 * BN + DH <= 512, "TMEM");
-  static_assert(SMEM_BYTES <= 232448, "smem");
+  static_assert(SMEM_BYTES * MINB <= 232448, "smem");
+  static_assert(TMEM_COLS * MINB <= 512, "TMEM");
 };
 
 // Does KV tile j (keys [j*BN, j*BN+BN)) hold at least one valid key?
@@ -70,15 +75,15 @@ __device__ __forceinline__ bool kv_tile_live(const uint32_t* __restrict__ bits_b
   return any != 0;
 }
 
-template <int DH, int BN, int KST, int VST>
-__global__ void __launch_bounds__(192, 1)
+template <int DH, int BN, int KST, int VST, int MINB>
+__global__ void __launch_bounds__(192, MINB)
     flash_fwd_tf32_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, float* __restrict__ O,
                           int64_t o_sb, int64_t o_sh, int64_t o_sm,
                           const uint32_t* __restrict__ keep_bits, int H, int S, int dh_out,
                           float scale_log2, int flags) {
-  using Cfg = FlashCfg<DH, BN, KST, VST>;
+  using Cfg = FlashCfg<DH, BN, KST, VST, MINB>;
   constexpr int BM = Cfg::BM;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -102,11 +107,16 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
+  // Grid (query tiles, heads): blocks launch in linear order, so the query
+  // tiles of one (b, h) run together and share its K/V in L2 (a long
+  // sequence's K/V is 32 MB per head -- streaming every head at once would
+  // re-read K/V from HBM for every query tile). Within a head the heaviest
+  // causal tiles go first.
+  const int bh = blockIdx.y;
   const int b = bh / H;
   const int h = bh % H;
-  const int n_qt = gridDim.y;
-  const int qt = n_qt - 1 - static_cast<int>(blockIdx.y);  // heaviest causal tiles first
+  const int n_qt = gridDim.x;
+  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);
   const int q0 = qt * BM;
   const bool causal = (flags & KF_ATTN_CAUSAL) != 0;
   const int words = (S + 31) >> 5;
@@ -449,12 +459,12 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-template <int DH, int BN, int KST, int VST>
+template <int DH, int BN, int KST, int VST, int MINB = 1>
 static int launch_flash(const float* q, const int64_t* qs, const float* k, const int64_t* ks,
                         const float* v, const int64_t* vs, float* o, const int64_t* os,
                         const uint32_t* bits, int B, int H, int S, int dh_stored, int dh_out,
                         float scale_log2, int flags, cudaStream_t st) {
-  using Cfg = FlashCfg<DH, BN, KST, VST>;
+  using Cfg = FlashCfg<DH, BN, KST, VST, MINB>;
   CUtensorMap tq, tk, tv;
   const uint64_t dims[4] = {static_cast<uint64_t>(dh_stored), static_cast<uint64_t>(S),
                             static_cast<uint64_t>(H), static_cast<uint64_t>(B)};
@@ -479,7 +489,7 @@ static int launch_flash(const float* q, const int64_t* qs, const float* k, const
   }
   if (rc) return rc;
 
-  auto kern = flash_fwd_tf32_kernel<DH, BN, KST, VST>;
+  auto kern = flash_fwd_tf32_kernel<DH, BN, KST, VST, MINB>;
   static int attr_set[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -491,7 +501,7 @@ static int launch_flash(const float* q, const int64_t* qs, const float* k, const
     attr_set[dev] = 1;
   }
   const int n_qt = (S + Cfg::BM - 1) / Cfg::BM;
-  dim3 grid(static_cast<unsigned>(B * H), static_cast<unsigned>(n_qt));
+  dim3 grid(static_cast<unsigned>(n_qt), static_cast<unsigned>(B * H));
   kern<<<grid, 192, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, o, os[0], os[1], os[2], bits, H, S,
                                              dh_out, scale_log2, flags);
   return cuda_status(cudaGetLastError(), "kf_flash_fwd_tf32 launch");
@@ -533,8 +543,8 @@ extern "C" int kf_flash_fwd_tf32(const float* q, int64_t q_sb, int64_t q_sh, int
     set_last_error("kf_flash_fwd_tf32: Q/K/V must be 16-byte aligned");
     return KF_E_UNSUPPORTED;
   }
-  if (B * H > INT32_MAX || S > (int64_t)65535 * 128 || S > INT32_MAX) {
-    set_last_error("kf_flash_fwd_tf32: B*H or S too large");
+  if (B * H > 65535 || S > INT32_MAX) {
+    set_last_error("kf_flash_fwd_tf32: B*H must be <= 65535 (grid y) and S < 2^31");
     return KF_E_UNSUPPORTED;
   }
   int f = flags & (KF_ATTN_CAUSAL | KF_ATTN_SKIP_EMPTY_Q | KF_ATTN_ROUND_TF32);
@@ -548,13 +558,13 @@ extern "C" int kf_flash_fwd_tf32(const float* q, int64_t q_sb, int64_t q_sh, int
   const int Bi = static_cast<int>(B), Hi = static_cast<int>(H), Si = static_cast<int>(S);
   switch (dh) {
     case 16:
-      return launch_flash<16, 128, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+      return launch_flash<16, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
                                          dh_out, scale_log2, f, st);
     case 32:
-      return launch_flash<32, 128, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+      return launch_flash<32, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
                                          dh_out, scale_log2, f, st);
     case 64:
-      return launch_flash<64, 128, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+      return launch_flash<64, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
                                          dh_out, scale_log2, f, st);
     case 128:
       return launch_flash<128, 64, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
