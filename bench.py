@@ -147,7 +147,10 @@ def sig(cfg):
 # ----------------------------------------------------------------- clocks
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi samples every 10 ms; summary() keeps those stamped inside the
+    timed window (mark_start/mark_end), falling back to the nearest ones when
+    the window is shorter than the sampling period."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -155,6 +158,13 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.t0 = self.t1 = None
+
+    def mark_start(self):
+        self.t0 = datetime.datetime.now()
+
+    def mark_end(self):
+        self.t1 = datetime.datetime.now()
 
     def __enter__(self):
         try:
@@ -163,7 +173,7 @@ class ClockSampler:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "10"],
                 stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -181,26 +191,32 @@ class ClockSampler:
     def summary(self) -> dict:
         if not self.path or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
-        sms, maxes, reasons = [], [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        rows = []
         with open(self.path) as f:
             for line in f:
                 parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
+                if len(parts) < 10:
                     continue
                 try:
-                    sms.append(float(parts[1]))
-                    maxes.append(float(parts[2]))
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                    rows.append((ts, float(parts[2]), float(parts[3]),
+                                 [n for n, v in zip(names, parts[6:10]) if v.lower() == "active"]))
                 except ValueError:
                     continue
-                for name, val in zip(names, parts[5:9]):
-                    if val.lower() == "active":
-                        reasons.add(name)
         os.unlink(self.path)
-        if not sms:
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
-                "samples": len(sms), "reasons": sorted(reasons)}
+        inside = [r for r in rows if self.t0 and self.t1 and self.t0 <= r[0] <= self.t1]
+        window = "inside the timed region"
+        if not inside and self.t0:
+            after = [r for r in rows if r[0] >= self.t0][:2]
+            before = [r for r in rows if r[0] < self.t0][-1:]
+            inside, window = before + after, "nearest to the timed region (shorter than 10 ms)"
+        inside = inside or rows
+        return {"sm_mhz": statistics.median(r[1] for r in inside),
+                "sm_max_mhz": max(r[2] for r in inside), "samples": len(inside),
+                "window": window, "reasons": sorted({n for r in inside for n in r[3]})}
 
 
 # ----------------------------------------------------------------- GPU legs
@@ -219,11 +235,16 @@ class LaunchTimer:
 
 
 def kernel_breakdown(model, x, keep, ws, weights, repeats: int = 5):
-    """Per-kind average launch time (ms) from events around every launch."""
+    """Per-kind average launch time (ms) from events around every launch.
+
+    A 10 ms device spin is queued first, so the host has enqueued the whole
+    instrumented forward before the GPU reaches it: events then bracket
+    device execution, not host launch gaps."""
     out = torch.empty_like(x)
     totals, counts = {}, {}
     for _ in range(repeats):
         timer = LaunchTimer()
+        torch.cuda._sleep(20_000_000)
         model.launch(x, keep, out, ws, weights, timer=timer)
         torch.cuda.synchronize()
         for kind, s, e in timer.records:
@@ -302,12 +323,14 @@ def main():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        clocks.mark_start()
         for k in range(args.steps):
             flush.zero_()                       # evict L2 between steps (untimed)
             starts[k].record()
             runner.replay()
             ends[k].record()
         torch.cuda.synchronize()
+        clocks.mark_end()
         if world > 1:
             dist.barrier()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]

@@ -54,6 +54,8 @@ int kf_device_status(int reset);
 #define KF_LN_ROUND_TF32 2 /* round h to TF32 (it only feeds a TF32 GEMM) */
 #define KF_LN_SKIP_PADDED 4 /* leave s and h of padded rows untouched (valid
                                only when every consumer masks those rows) */
+#define KF_LN_OUT_BF16X2 8  /* write h as bf16 hi/lo planes: h_out is then a
+                               uint16 [2][M][ldh] buffer (kf_gemm_bf16x3 input) */
 
 /* Fused residual-add + row mask + LayerNorm over rows of width d:
  *     s = keep[r] ? x[r] + y[r] : 0          (y optional, keep optional)
@@ -104,6 +106,23 @@ int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t ldw, const
                  int bn, int head_dim, int head_stride, const int32_t* live_tiles,
                  const int32_t* live_count, void* stream);
 
+#define KF_GEMM_OUT_BF16X2 8 /* kf_gemm_bf16x3: write C as bf16 hi/lo planes */
+
+/* Error-compensated GEMM on operands already split into bf16 planes:
+ * A2 = [2][M][lda] (hi plane, then lo plane, with hi + lo = the fp32 value to
+ * ~2^-17), W2 = [2][N][ldw] likewise; C = epilogue(A.W^T + bias) computed as
+ * hi(A)hi(W) + hi(A)lo(W) + lo(A)hi(W) on the BF16 tensor path with an FP32
+ * TMEM accumulator. C is fp32 [M][ldc], or with KF_GEMM_OUT_BF16X2 bf16
+ * planes [2][M][ldc] in the same split format (to feed another
+ * kf_gemm_bf16x3). Needs K, lda, ldw % 8 == 0 and 16-byte aligned pointers.
+ * head_dim/head_stride (fp32 output only) and live_tiles/live_count as
+ * kf_gemm_tf32. Replaces the same F.linear calls
+ * as kf_gemm_tf32, at fp32-class accuracy. */
+int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t ldw,
+                   const float* bias, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                   int epilogue, int flags, int bn, int head_dim, int head_stride,
+                   const int32_t* live_tiles, const int32_t* live_count, void* stream);
+
 /* ----------------------------------------------------------- attention */
 
 /* Words of the packed key-validity workspace for a [B, S] keep mask. */
@@ -120,6 +139,10 @@ int kf_keep_bits(const uint8_t* keep, int64_t ld_keep, int64_t B, int64_t S, uin
                                   (valid only when the caller masks those rows
                                   afterwards, as the layer stack does) */
 #define KF_ATTN_ROUND_TF32 4  /* round O to TF32 (it only feeds a TF32 GEMM) */
+#define KF_ATTN_OUT_BF16X2 8  /* write O as bf16 hi/lo planes: o is then a uint16
+                                 buffer with the given strides (in bf16
+                                 elements), lo plane B * o_sb elements after
+                                 the hi plane (kf_gemm_bf16x3 input) */
 
 /* O = softmax(Q K^T * sm_scale + causal(-inf) + keypad(-inf)) V per (b, h),
  * softmax in fp32, TF32 tensor-core contractions, FP32 accumulation in TMEM.
@@ -169,6 +192,12 @@ int kf_flash_fwd_tf32_keep_noalloc(const float* q, int64_t q_sb, int64_t q_sh, i
                                    void* stream);
 
 /* ----------------------------------------------------------- utilities */
+
+/* Split src [rows][ld_src] fp32 into bf16 planes dst2 = [2][rows][ld_dst]
+ * (hi = bf16_rn(x), lo = bf16_rn(x - hi)); weight preparation for
+ * kf_gemm_bf16x3. */
+int kf_split_bf16x2(const float* src, int64_t rows, int64_t cols, int64_t ld_src, uint16_t* dst2,
+                    int64_t ld_dst, void* stream);
 
 /* dst[i] = round_to_tf32(src[i]) for n fp32 values (weight preparation). */
 int kf_round_tf32(const float* src, float* dst, int64_t n, void* stream);

@@ -30,6 +30,10 @@ SIGNATURES = {
                               _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int,
                               _c_ptr, _c_ptr, _c_ptr]),
     "kf_live_row_tiles": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_ptr, _c_ptr]),
+    "kf_gemm_bf16x3": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
+                                _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                _c_ptr, _c_ptr, _c_ptr]),
+    "kf_split_bf16x2": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_i64, _c_ptr]),
     "kf_keep_bits_words": (ctypes.c_size_t, [_c_i64, _c_i64]),
     "kf_keep_bits": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr]),
     "kf_flash_fwd_tf32": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64,
@@ -56,6 +60,7 @@ KF_E_NO_DEVICE = 4
 KF_LN_MASK_OUT = 1
 KF_LN_ROUND_TF32 = 2
 KF_LN_SKIP_PADDED = 4
+KF_LN_OUT_BF16X2 = 8
 KF_EPI_BIAS = 0
 KF_EPI_BIAS_GELU = 1
 KF_GEMM_ROUND_TF32 = 1
@@ -66,6 +71,8 @@ GEMM_PRECISION_FLAGS = {"tf32": 0, "3xtf32": KF_GEMM_SPLIT3, "bf16x3": KF_GEMM_B
 KF_ATTN_CAUSAL = 1
 KF_ATTN_SKIP_EMPTY_Q = 2
 KF_ATTN_ROUND_TF32 = 4
+KF_ATTN_OUT_BF16X2 = 8
+KF_GEMM_OUT_BF16X2 = 8
 KF_NOALLOC_KEEP_WORDS_MAX = 262144
 
 _lib = None

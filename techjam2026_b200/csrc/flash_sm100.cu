@@ -131,9 +131,16 @@ __global__ void __launch_bounds__(192, MINB)
         const int r = (warp & 3) * 32 + lane;
         const int qi = q0 + r;
         if (qi < S) {
-          float* orow = O + static_cast<int64_t>(b) * o_sb + static_cast<int64_t>(h) * o_sh +
-                        static_cast<int64_t>(qi) * o_sm;
-          for (int c = 0; c < dh_out; ++c) orow[c] = 0.f;
+          const int64_t off = static_cast<int64_t>(b) * o_sb + static_cast<int64_t>(h) * o_sh +
+                              static_cast<int64_t>(qi) * o_sm;
+          if (flags & KF_ATTN_OUT_BF16X2) {
+            uint16_t* ohi = reinterpret_cast<uint16_t*>(O) + off;
+            uint16_t* olo = ohi + static_cast<int64_t>(gridDim.y / H) * o_sb;
+            for (int c = 0; c < dh_out; ++c) ohi[c] = olo[c] = 0;
+          } else {
+            float* orow = O + off;
+            for (int c = 0; c < dh_out; ++c) orow[c] = 0.f;
+          }
         }
       }
       return;
@@ -410,6 +417,12 @@ __global__ void __launch_bounds__(192, MINB)
       float* orow = O + static_cast<int64_t>(b) * o_sb + static_cast<int64_t>(h) * o_sh +
                     static_cast<int64_t>(qi) * o_sm;
       const bool rnd = (flags & KF_ATTN_ROUND_TF32) != 0;
+      const bool split = (flags & KF_ATTN_OUT_BF16X2) != 0;
+      // Split output: bf16 hi plane at O (bf16 elements, same strides), lo
+      // plane B * o_sb elements further.
+      uint16_t* ohi = reinterpret_cast<uint16_t*>(O) + static_cast<int64_t>(b) * o_sb +
+                      static_cast<int64_t>(h) * o_sh + static_cast<int64_t>(qi) * o_sm;
+      uint16_t* olo = ohi + static_cast<int64_t>(gridDim.y / H) * o_sb;
       if (it > 0) {
         // o_final (one phase) rather than o_done: by now o_done may be two
         // phases behind, where a parity wait cannot tell the phases apart.
@@ -433,7 +446,15 @@ __global__ void __launch_bounds__(192, MINB)
                     v4.z = round_tf32(v4.z);
                     v4.w = round_tf32(v4.w);
                   }
-                  if (col + 3 < dh_out && (flags & (1 << 8))) {
+                  if (split) {
+                    if (col + 3 < dh_out) {
+                      store_split4(ohi + col, olo + col, v4);
+                    } else {
+                      const float tmp[4] = {v4.x, v4.y, v4.z, v4.w};
+                      for (int u = 0; u < 4 && col + u < dh_out; ++u)
+                        split_bf16(tmp[u], ohi[col + u], olo[col + u]);
+                    }
+                  } else if (col + 3 < dh_out && (flags & (1 << 8))) {
                     *reinterpret_cast<float4*>(orow + col) = v4;
                   } else {
                     const float tmp[4] = {v4.x, v4.y, v4.z, v4.w};
@@ -445,7 +466,14 @@ __global__ void __launch_bounds__(192, MINB)
           }
         }
       } else if (qi < S) {
-        for (int c = 0; c < dh_out; ++c) orow[c] = 0.f;
+        for (int c = 0; c < dh_out; ++c) {
+          if (split) {
+            ohi[c] = 0;
+            olo[c] = 0;
+          } else {
+            orow[c] = 0.f;
+          }
+        }
       }
     }
   }
@@ -547,7 +575,13 @@ extern "C" int kf_flash_fwd_tf32(const float* q, int64_t q_sb, int64_t q_sh, int
     set_last_error("kf_flash_fwd_tf32: B*H must be <= 65535 (grid y) and S < 2^31");
     return KF_E_UNSUPPORTED;
   }
-  int f = flags & (KF_ATTN_CAUSAL | KF_ATTN_SKIP_EMPTY_Q | KF_ATTN_ROUND_TF32);
+  int f = flags & (KF_ATTN_CAUSAL | KF_ATTN_SKIP_EMPTY_Q | KF_ATTN_ROUND_TF32 | KF_ATTN_OUT_BF16X2);
+  if ((f & KF_ATTN_OUT_BF16X2) && ((f & KF_ATTN_ROUND_TF32) || o_sm % 4 || o_sb % 4 || o_sh % 4 ||
+                                   (reinterpret_cast<uintptr_t>(o) & 7u))) {
+    set_last_error("kf_flash_fwd_tf32: split output needs strides %% 4 == 0, 8-byte alignment "
+                   "and no TF32 rounding");
+    return KF_E_INVALID;
+  }
   if ((o_sm % 4 == 0) && !(reinterpret_cast<uintptr_t>(o) & 15u) && o_sb % 4 == 0 &&
       o_sh % 4 == 0)
     f |= (1 << 8);

@@ -40,21 +40,25 @@
 
 namespace kf {
 
-enum : int { KF_GEMM_VEC_OK = 1 << 8, KF_GEMM_TMA_OUT = 1 << 9 };
-enum : int { SPLIT_NONE = 0, SPLIT_TF32X3 = 1, SPLIT_BF16X3 = 2 };
+enum : int { KF_GEMM_VEC_OK = 1 << 8, KF_GEMM_TMA_OUT = 1 << 9, KF_GEMM_OUT_SPLIT = 1 << 10 };
+// SPLIT_BF16X3_PRE: operands arrive already split into bf16 hi/lo planes
+// (kf_gemm_bf16x3); TMA loads the four planes, no converter warps.
+enum : int { SPLIT_NONE = 0, SPLIT_TF32X3 = 1, SPLIT_BF16X3 = 2, SPLIT_BF16X3_PRE = 3 };
 
 template <int BN, int SPLIT>
 struct GemmCfg {
   static constexpr int BM = 128;
-  static constexpr int BK = 32;  // 32 fp32 = 128 bytes = one swizzle row
-  static constexpr int A_BYTES = BM * BK * 4;
-  static constexpr int B_BYTES = BN * BK * 4;
+  // One 128-byte swizzle row per k block: 32 fp32 or (pre-split) 64 bf16.
+  static constexpr int BK = SPLIT == 3 ? 64 : 32;
+  static constexpr int A_BYTES = BM * 128;  // one plane
+  static constexpr int B_BYTES = BN * 128;
   // stage layout: A | B [| lo(A) | lo(B)]
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (SPLIT ? 2 : 1);
   static constexpr int STAGES_FIT = 196608 / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int CONV_THREADS = 256;  // split modes: 8 converter warps
-  static constexpr int THREADS = SPLIT ? 192 + CONV_THREADS : 192;
+  static constexpr bool CONVERTS = SPLIT == 1 || SPLIT == 2;
+  static constexpr int THREADS = CONVERTS ? 192 + CONV_THREADS : 192;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int EPI_BUF_BYTES = BM * 32 * 4;  // one 128x32 fp32 output chunk
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
@@ -173,7 +177,7 @@ __device__ __forceinline__ void gemm_store_chunk(const float (&v)[32], float* __
 }
 
 template <int BN, int EPI, int SPLIT>
-__global__ void __launch_bounds__(SPLIT ? 448 : 192, 1)
+__global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 448 : 192, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int M,
                      int N, int K, int flags, int head_dim, int head_stride,
@@ -249,9 +253,19 @@ __global__ void __launch_bounds__(SPLIT ? 448 : 192, 1)
             break;
           }
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::B_BYTES);
-          tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
-          tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full[stage], kb * BK, n0);
+          if (SPLIT == SPLIT_BF16X3_PRE) {
+            // planes: A_hi | B_hi | A_lo | B_lo (3-D maps, plane = coordinate 2)
+            mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+            tma_load_3d(sa, &tmA, &full[stage], kb * BK, m0, 0);
+            tma_load_3d(sa + Cfg::A_BYTES, &tmB, &full[stage], kb * BK, n0, 0);
+            tma_load_3d(sa + Cfg::A_BYTES + Cfg::B_BYTES, &tmA, &full[stage], kb * BK, m0, 1);
+            tma_load_3d(sa + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &tmB, &full[stage], kb * BK, n0,
+                        1);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::B_BYTES);
+            tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
+            tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full[stage], kb * BK, n0);
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -285,7 +299,7 @@ __global__ void __launch_bounds__(SPLIT ? 448 : 192, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(SPLIT ? &conv[stage] : &full[stage], phase, abort_flag,
+          if (!mbar_wait(Cfg::CONVERTS ? &conv[stage] : &full[stage], phase, abort_flag,
                          KF_DEV_WAIT_TIMEOUT_MMA)) {
             ok = false;
             break;
@@ -295,7 +309,19 @@ __global__ void __launch_bounds__(SPLIT ? 448 : 192, 1)
           const uint32_t b_addr = a_addr + Cfg::A_BYTES;
           const uint32_t alo_addr = b_addr + Cfg::B_BYTES;
           const uint32_t blo_addr = alo_addr + Cfg::A_BYTES;
-          if (SPLIT == SPLIT_BF16X3) {
+          if (SPLIT == SPLIT_BF16X3_PRE) {
+            // TMA-loaded bf16 planes, 128-byte rows (SW128): 4 k steps of 16.
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint64_t ah = make_smem_desc(a_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+              const uint64_t bh = make_smem_desc(b_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+              const uint64_t al = make_smem_desc(alo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+              const uint64_t bl = make_smem_desc(blo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+              mma_bf16_ss(d_tmem, al, bh, idesc_bf, (kb | k) != 0 ? 1u : 0u);
+              mma_bf16_ss(d_tmem, ah, bl, idesc_bf, 1u);
+              mma_bf16_ss(d_tmem, ah, bh, idesc_bf, 1u);
+            }
+          } else if (SPLIT == SPLIT_BF16X3) {
             // bf16 tiles: A_hi | A_lo | B_hi | B_lo, 64-byte rows (SW64).
             const uint32_t ahi = alo_addr, alo = ahi + Cfg::A_BYTES / 2;
             const uint32_t bhi = alo + Cfg::A_BYTES / 2, blo = bhi + Cfg::B_BYTES / 2;
@@ -340,7 +366,7 @@ __global__ void __launch_bounds__(SPLIT ? 448 : 192, 1)
       mma_commit(drain);
       mbar_wait_drain(drain, 0, KF_DEV_WAIT_TIMEOUT_MMA);
     }
-  } else if (SPLIT && warp >= 6) {
+  } else if (Cfg::CONVERTS && warp >= 6) {
     // -------------------------------------------------- converters (warps 6..9)
     const int ct = threadIdx.x - 192;
     int stage = 0;
@@ -420,7 +446,44 @@ __global__ void __launch_bounds__(SPLIT ? 448 : 192, 1)
         if (n0 + c >= N) break;  // warp-uniform
         float v[32];
         tmem_ld32(tbase + static_cast<uint32_t>(c), v);
-        if (tma_out) {
+        if (tma_out && (flags & KF_GEMM_OUT_SPLIT)) {
+          // bf16 hi/lo planes: two 128x32 bf16 tiles (64-byte rows, SW64).
+          uint8_t* buf = smem + Cfg::EPI_OFF + (chunk & 1) * Cfg::EPI_BUF_BYTES;
+          if (leader) bulk_wait_group_read<1>();
+          named_bar_sync(1, 128);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {  // 8 columns -> one 16-byte bf16 chunk
+            float o[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              const int col = n0 + c + 8 * j + t;
+              float x = v[8 * j + t] + ((bias && col < N) ? __ldg(bias + col) : 0.f);
+              if (EPI == KF_EPI_BIAS_GELU) x = gelu_erf(x);
+              o[t] = x;
+            }
+            __nv_bfloat16 hi[8], lo[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              hi[t] = __float2bfloat16_rn(o[t]);
+              lo[t] = __float2bfloat16_rn(o[t] - __bfloat162float(hi[t]));
+            }
+            const int off = r * 64 + ((j ^ ((r >> 1) & 3)) << 4);
+            *reinterpret_cast<uint4*>(buf + off) =
+                make_uint4(pack_bf16x2(hi[0], hi[1]), pack_bf16x2(hi[2], hi[3]),
+                           pack_bf16x2(hi[4], hi[5]), pack_bf16x2(hi[6], hi[7]));
+            *reinterpret_cast<uint4*>(buf + Cfg::EPI_BUF_BYTES / 2 + off) =
+                make_uint4(pack_bf16x2(lo[0], lo[1]), pack_bf16x2(lo[2], lo[3]),
+                           pack_bf16x2(lo[4], lo[5]), pack_bf16x2(lo[6], lo[7]));
+          }
+          fence_proxy_async_smem();
+          named_bar_sync(1, 128);
+          if (leader) {
+            tma_store_3d(&tmC, buf, n0 + c, m0, 0);
+            tma_store_3d(&tmC, buf + Cfg::EPI_BUF_BYTES / 2, n0 + c, m0, 1);
+            bulk_commit_group();
+          }
+          ++chunk;
+        } else if (tma_out) {
           uint8_t* buf = smem + Cfg::EPI_OFF + (chunk & 1) * Cfg::EPI_BUF_BYTES;
           if (leader) bulk_wait_group_read<1>();  // the store that used `buf` is done reading
           named_bar_sync(1, 128);
@@ -642,5 +705,108 @@ extern "C" int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t
   KF_GEMM_CASE(128)
   KF_GEMM_CASE(256)
 #undef KF_GEMM_CASE
+  return KF_E_INVALID;
+}
+
+extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t ldw,
+                              const float* bias, void* C, int64_t ldc, int64_t M, int64_t N,
+                              int64_t K, int epilogue, int flags, int bn, int head_dim,
+                              int head_stride, const int32_t* live_tiles,
+                              const int32_t* live_count, void* stream) {
+  if (!A2 || !W2 || !C || M < 0 || N < 0 || K < 0) {
+    set_last_error("kf_gemm_bf16x3: invalid arguments");
+    return KF_E_INVALID;
+  }
+  if (M == 0 || N == 0) return KF_OK;
+  const bool out_split = (flags & KF_GEMM_OUT_BF16X2) != 0;
+  if (K == 0 || K % 8 || lda % 8 || ldw % 8 || lda < K || ldw < K || ldc < N ||
+      (reinterpret_cast<uintptr_t>(A2) & 15u) || (reinterpret_cast<uintptr_t>(W2) & 15u) ||
+      (reinterpret_cast<uintptr_t>(C) & 15u) || (out_split ? ldc % 8 : ldc % 4) ||
+      (bias && (reinterpret_cast<uintptr_t>(bias) & 15u))) {
+    set_last_error(
+        "kf_gemm_bf16x3: needs K, lda, ldw %% 8 == 0, ldc %% %d == 0, lda/ldw >= K, ldc >= N "
+        "and 16-byte aligned pointers (K=%lld lda=%lld ldw=%lld ldc=%lld)",
+        out_split ? 8 : 4, (long long)K, (long long)lda, (long long)ldw, (long long)ldc);
+    return KF_E_UNSUPPORTED;
+  }
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX) {
+    set_last_error("kf_gemm_bf16x3: dimensions beyond 2^30");
+    return KF_E_UNSUPPORTED;
+  }
+  if (epilogue != KF_EPI_BIAS && epilogue != KF_EPI_BIAS_GELU) {
+    set_last_error("kf_gemm_bf16x3: unknown epilogue %d", epilogue);
+    return KF_E_INVALID;
+  }
+  if ((live_tiles == nullptr) != (live_count == nullptr)) {
+    set_last_error("kf_gemm_bf16x3: live_tiles and live_count go together");
+    return KF_E_INVALID;
+  }
+  if (head_dim < 0 || (head_dim > 0 && (head_stride < head_dim || out_split))) {
+    set_last_error("kf_gemm_bf16x3: head padding needs head_stride >= head_dim and fp32 output");
+    return KF_E_INVALID;
+  }
+  if (bn == 0) bn = choose_bn(M, N);
+  if (bn != 64 && bn != 128 && bn != 256) {
+    set_last_error("kf_gemm_bf16x3: bn must be 0, 64, 128 or 256");
+    return KF_E_INVALID;
+  }
+  CUtensorMap ta, tb, tcm;
+  memset(&tcm, 0, sizeof(tcm));
+  int rc;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M), 2};
+    const uint64_t strides[2] = {static_cast<uint64_t>(lda) * 2,
+                                 static_cast<uint64_t>(M) * static_cast<uint64_t>(lda) * 2};
+    const uint32_t box[3] = {64, 128, 1};
+    rc = encode_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, A2, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N), 2};
+    const uint64_t strides[2] = {static_cast<uint64_t>(ldw) * 2,
+                                 static_cast<uint64_t>(N) * static_cast<uint64_t>(ldw) * 2};
+    const uint32_t box[3] = {64, static_cast<uint32_t>(bn), 1};
+    rc = encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, W2, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  int f = (flags & KF_GEMM_ROUND_TF32) | KF_GEMM_TMA_OUT;
+  if (head_dim == 0 || (head_dim % 4 == 0 && head_stride % 4 == 0)) f |= KF_GEMM_VEC_OK;
+  if (head_dim > 0) {
+    f &= ~KF_GEMM_TMA_OUT;  // scatter into head-padded slots: direct stores
+  } else if (out_split) {
+    f = (f & ~KF_GEMM_ROUND_TF32) | KF_GEMM_OUT_SPLIT;
+    const uint64_t dims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M), 2};
+    const uint64_t strides[2] = {static_cast<uint64_t>(ldc) * 2,
+                                 static_cast<uint64_t>(M) * static_cast<uint64_t>(ldc) * 2};
+    const uint32_t box[3] = {32, 128, 1};
+    rc = encode_tensor_map(&tcm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, C, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_64B);
+  } else {
+    const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldc) * 4};
+    const uint32_t box[2] = {32, 128};
+    rc = encode_tensor_map(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, C, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
+  float* Cf = static_cast<float*>(C);
+#define KF_GEMM_PRE_CASE(BNV)                                                                  \
+  if (bn == BNV) {                                                                             \
+    if (epilogue == KF_EPI_BIAS)                                                               \
+      return launch_gemm<BNV, KF_EPI_BIAS, 3>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,          \
+                                              head_dim, head_stride, live_tiles, live_count,   \
+                                              st);                                             \
+    return launch_gemm<BNV, KF_EPI_BIAS_GELU, 3>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,       \
+                                                 head_dim, head_stride, live_tiles,            \
+                                                 live_count, st);                              \
+  }
+  KF_GEMM_PRE_CASE(64)
+  KF_GEMM_PRE_CASE(128)
+  KF_GEMM_PRE_CASE(256)
+#undef KF_GEMM_PRE_CASE
   return KF_E_INVALID;
 }

@@ -150,6 +150,21 @@ __global__ void __launch_bounds__(1024) live_row_tiles_kernel(const uint8_t* __r
   if (tid == 0) *count = base;
 }
 
+// dst = [2][rows][ld_dst] bf16 planes (hi, then lo) of src [rows][ld_src].
+__global__ void split_bf16x2_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
+                                    int64_t ld_src, uint16_t* __restrict__ dst, int64_t ld_dst) {
+  const int64_t n = rows * cols;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += stride) {
+    const int64_t r = i / cols, c = i % cols;
+    uint16_t hi, lo;
+    split_bf16(src[r * ld_src + c], hi, lo);
+    dst[r * ld_dst + c] = hi;
+    dst[rows * ld_dst + r * ld_dst + c] = lo;
+  }
+}
+
 __global__ void round_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst,
                                   int64_t n) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -208,6 +223,22 @@ extern "C" int kf_live_row_tiles(const uint8_t* keep, int64_t M, int32_t* tiles,
   }
   live_row_tiles_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(keep, M, tiles, count);
   return cuda_status(cudaGetLastError(), "kf_live_row_tiles launch");
+}
+
+extern "C" int kf_split_bf16x2(const float* src, int64_t rows, int64_t cols, int64_t ld_src,
+                               uint16_t* dst2, int64_t ld_dst, void* stream) {
+  if (!src || !dst2 || rows < 0 || cols < 0 || ld_src < cols || ld_dst < cols) {
+    set_last_error("kf_split_bf16x2: invalid arguments");
+    return KF_E_INVALID;
+  }
+  if (rows == 0 || cols == 0) return KF_OK;
+  const int threads = 256;
+  int64_t blocks = (rows * cols + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  split_bf16x2_kernel<<<static_cast<unsigned>(blocks), threads, 0,
+                        static_cast<cudaStream_t>(stream)>>>(src, rows, cols, ld_src, dst2, ld_dst);
+  return cuda_status(cudaGetLastError(), "kf_split_bf16x2 launch");
 }
 
 extern "C" int kf_round_tf32(const float* src, float* dst, int64_t n, void* stream) {

@@ -74,6 +74,9 @@ __global__ void __launch_bounds__(256) ln_add_mask_vec_kernel(
   const float rstd = 1.f / sqrtf(var + eps);
   const bool zero_h = (flags & KF_LN_MASK_OUT) && !kept;
   const bool rnd = (flags & KF_LN_ROUND_TF32) != 0;
+  const bool split = (flags & KF_LN_OUT_BF16X2) != 0;
+  uint16_t* h_hi = reinterpret_cast<uint16_t*>(h_out) + row * ldh;
+  uint16_t* h_lo = h_hi + M * ldh;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int c = lane + 32 * i;
@@ -96,7 +99,10 @@ __global__ void __launch_bounds__(256) ln_add_mask_vec_kernel(
           h.w = round_tf32(h.w);
         }
       }
-      reinterpret_cast<float4*>(h_out + row * ldh)[c] = h;
+      if (split)
+        store_split4(h_hi + 4 * c, h_lo + 4 * c, h);
+      else
+        reinterpret_cast<float4*>(h_out + row * ldh)[c] = h;
     }
   }
 }
@@ -135,7 +141,14 @@ __global__ void __launch_bounds__(256) ln_add_mask_scalar_kernel(
     if (s_out) s_out[row * lds + c] = s;
     float h = zero_h ? 0.f : (s - mean) * rstd * w[c] + b[c];
     if (rnd && !zero_h) h = round_tf32(h);
-    h_out[row * ldh + c] = h;
+    if (flags & KF_LN_OUT_BF16X2) {
+      uint16_t hi, lo;
+      split_bf16(h, hi, lo);
+      reinterpret_cast<uint16_t*>(h_out)[row * ldh + c] = hi;
+      reinterpret_cast<uint16_t*>(h_out)[M * ldh + row * ldh + c] = lo;
+    } else {
+      h_out[row * ldh + c] = h;
+    }
   }
 }
 
@@ -164,6 +177,10 @@ extern "C" int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64
 
   bool vec = (d % 4 == 0) && aligned16(x) && aligned16(w) && aligned16(b) && aligned16(h_out) &&
              ldx % 4 == 0 && ldh % 4 == 0 && d <= 4096;
+  if ((flags & KF_LN_OUT_BF16X2) && (flags & KF_LN_ROUND_TF32)) {
+    set_last_error("kf_ln_add_mask: KF_LN_OUT_BF16X2 and KF_LN_ROUND_TF32 are exclusive");
+    return KF_E_INVALID;
+  }
   if (y) vec = vec && aligned16(y) && ldy % 4 == 0;
   if (s_out) vec = vec && aligned16(s_out) && lds % 4 == 0;
 

@@ -26,20 +26,21 @@ SUPPORTED_ARCHES = ("sm_100", "sm_100a")
 
 @dataclasses.dataclass(frozen=True)
 class Plan:
-    name: str = "3xtf32-gemm+tf32-attn+graph"
+    name: str = "bf16x3-gemm+tf32-attn+graph"
     # Capture the whole multi-layer forward in one CUDA graph.
     cuda_graph: bool = True
-    # Precision of each GEMM: "tf32" (one TF32 pass), "bf16x3" or "3xtf32"
-    # (error-compensated hi*hi + hi*lo + lo*hi). Plain TF32 everywhere fails
-    # the organiser's gate against the fp32 reference on the 6-layer config
-    # (envelope 1.2-1.4); compensated GEMMs with TF32 attention measure
-    # 0.41-0.63 on every config. bf16x3 needs half the MMA work of 3xtf32
-    # but its in-kernel operand split costs more than it saves (measured
-    # 148 vs 226 TFLOP/s on a 16384x4096x1024 GEMM), so 3xtf32 is the default.
-    prec_qkv: str = "3xtf32"
-    prec_out: str = "3xtf32"
-    prec_ffn1: str = "3xtf32"
-    prec_ffn2: str = "3xtf32"
+    # Precision of each GEMM: "tf32" (one TF32 pass), "3xtf32" (fp32
+    # operands, split in shared memory) or "bf16x3" (operands kept as bf16
+    # hi/lo planes by their producers; three BF16 MMAs per k step), the last
+    # two error-compensated (hi*hi + hi*lo + lo*hi). Plain TF32 everywhere
+    # fails the organiser's gate against the fp32 reference on the 6-layer
+    # config (envelope 1.2-1.4); compensated GEMMs with TF32 attention
+    # measure 0.41-0.63 on every config. bf16x3 needs half the MMA time and a
+    # quarter of the shared-memory operand traffic of 3xtf32 per k element.
+    prec_qkv: str = "bf16x3"
+    prec_out: str = "bf16x3"
+    prec_ffn1: str = "bf16x3"
+    prec_ffn2: str = "bf16x3"
     # Round operands that feed a plain TF32 MMA (attention, and any GEMM not
     # split) to the nearest TF32 value where they are produced, so the tensor
     # core's truncation of the low mantissa bits is a no-op: unbiased operand

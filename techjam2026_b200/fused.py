@@ -39,15 +39,23 @@ SUPPORTED_HEAD_DIMS = (8, 16, 32, 64, 128, 256)
 
 
 class _Weights:
-    """Device copies laid out for the kernels: fused [Wq;Wk;Wv]; weights of a
-    GEMM that runs plain TF32 are rounded to the nearest TF32 value once
-    (weights of a 3xTF32 GEMM keep all their bits)."""
+    """Device copies laid out for the kernels, built once per device.
+
+    [Wq;Wk;Wv] is fused. A GEMM running "bf16x3" gets its weight split into
+    bf16 hi/lo planes [2, N, K]; a "tf32" GEMM gets it rounded to TF32; a
+    "3xtf32" GEMM keeps all fp32 bits."""
 
     def __init__(self, model: LayerStack, device: torch.device, plan: Plan):
         from .ops.gemm import round_tf32 as rnd
 
         def prep_w(w: torch.Tensor, prec: str) -> torch.Tensor:
             w = w.detach().to(device=device, dtype=torch.float32).contiguous()
+            if prec == "bf16x3":
+                N, K = w.shape
+                out = torch.empty(2, N, K, dtype=torch.int16, device=device)
+                _lib.check(_lib.lib().kf_split_bf16x2(w.data_ptr(), N, K, K, out.data_ptr(), K,
+                                                      _lib.stream_ptr()), "kf_split_bf16x2")
+                return out
             return rnd(w) if (plan.round_tf32 and prec == "tf32") else w.clone()
 
         def prep_b(b: torch.Tensor) -> torch.Tensor:
@@ -74,23 +82,29 @@ class _Weights:
 class _Workspace:
     """Activation buffers for one (B, S): allocated once, reused every call.
 
+    An activation that feeds a "bf16x3" GEMM is kept as bf16 hi/lo planes
+    [2, M, width] (same 4 bytes per value as fp32); otherwise fp32.
+
     Zeroed once at allocation: the head-padding columns of the QKV buffer
     (head_dim 8 stored as 16) must stay exactly zero, and rows of padded
     tokens that the plan skips keep whatever an earlier call left -- always
     finite values, so a masked key (P = 0) times its stale V stays 0."""
 
-    def __init__(self, cfg, B: int, S: int, device: torch.device):
+    def __init__(self, cfg, B: int, S: int, device: torch.device, plan: Plan):
         d, F, H = cfg.d_model, cfg.ffn_dim, cfg.num_heads
         self.dh = d // H
         self.dh_store = max(16, self.dh)
         M = B * S
         f32 = dict(dtype=torch.float32, device=device)
+        pl = dict(dtype=torch.int16, device=device)
+        split = {g: p == "bf16x3" for g, p in plan.gemm_precisions().items()}
         self.res = torch.zeros(M, d, **f32)
-        self.h = torch.zeros(M, d, **f32)
+        self.h = torch.zeros(M, d, **f32) if not (split["qkv"] and split["ffn1"]) else None
+        self.h2 = torch.zeros(2, M, d, **pl) if (split["qkv"] or split["ffn1"]) else None
         self.qkv = torch.zeros(M, 3 * H * self.dh_store, **f32)
-        self.ctx = torch.zeros(M, d, **f32)
+        self.ctx = torch.zeros(2, M, d, **pl) if split["out"] else torch.zeros(M, d, **f32)
         self.y = torch.zeros(M, d, **f32)
-        self.ffn = torch.zeros(M, F, **f32)
+        self.ffn = torch.zeros(2, M, F, **pl) if split["ffn2"] else torch.zeros(M, F, **f32)
         words = (S + 31) // 32
         i32 = dict(dtype=torch.int32, device=device)
         self.bits = torch.zeros(B * words, **i32)
@@ -99,8 +113,8 @@ class _Workspace:
 
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size()
-                   for t in (self.res, self.h, self.qkv, self.ctx, self.y, self.ffn, self.bits,
-                             self.live_tiles, self.live_count))
+                   for t in (self.res, self.h, self.h2, self.qkv, self.ctx, self.y, self.ffn,
+                             self.bits, self.live_tiles, self.live_count) if t is not None)
 
 
 class FusedTransformer(LayerStack):
@@ -144,7 +158,7 @@ class FusedTransformer(LayerStack):
         key = (B, S, str(device))
         ws = self._workspaces.get(key)
         if ws is None:
-            ws = _Workspace(self.config, B, S, device)
+            ws = _Workspace(self.config, B, S, device, self.plan)
             self._workspaces[key] = ws
         return ws
 
@@ -181,31 +195,37 @@ class FusedTransformer(LayerStack):
         st = _lib.stream_ptr()
         R = plan.round_tf32
         P = _lib.GEMM_PRECISION_FLAGS
-        # Round a producer's output only when its consumer is a plain TF32 MMA.
-        rnd_h1 = _lib.KF_LN_ROUND_TF32 if (R and plan.prec_qkv == "tf32") else 0
-        rnd_h2 = _lib.KF_LN_ROUND_TF32 if (R and plan.prec_ffn1 == "tf32") else 0
-        rnd_qkv = _lib.KF_GEMM_ROUND_TF32 if R else 0          # feeds attention
-        rnd_gelu = _lib.KF_GEMM_ROUND_TF32 if (R and plan.prec_ffn2 == "tf32") else 0
-        f_qkv = rnd_qkv | P[plan.prec_qkv]
-        f_out = P[plan.prec_out]
-        f_ffn1 = rnd_gelu | P[plan.prec_ffn1]
-        f_ffn2 = P[plan.prec_ffn2]
-        attn_flags = (_lib.KF_ATTN_CAUSAL if cfg.causal else 0) | (
-            _lib.KF_ATTN_ROUND_TF32 if (R and plan.prec_out == "tf32") else 0)
+        prec = plan.gemm_precisions()
+        split = {g: p == "bf16x3" for g, p in prec.items()}
         keep = keep_u8.data_ptr() if keep_u8 is not None else None
         bits = ws.bits.data_ptr() if keep_u8 is not None else None
-        if keep_u8 is not None and plan.skip_empty_queries:
-            attn_flags |= _lib.KF_ATTN_SKIP_EMPTY_Q
         # Padded rows: GEMMs compute only 128-row tiles holding a real token
         # and the (non-final) norms leave padded rows alone.
         skip_rows = keep_u8 is not None and plan.skip_padded_rows
         lt = ws.live_tiles.data_ptr() if skip_rows else None
         lc = ws.live_count.data_ptr() if skip_rows else None
         ln_skip = _lib.KF_LN_SKIP_PADDED if skip_rows else 0
-        rnd_h1 |= ln_skip
-        rnd_h2 |= ln_skip
-        res, h, y, ctx, ffn, qkv = (ws.res.data_ptr(), ws.h.data_ptr(), ws.y.data_ptr(),
-                                    ws.ctx.data_ptr(), ws.ffn.data_ptr(), ws.qkv.data_ptr())
+
+        # Producer output formats follow their consumer's precision: bf16
+        # hi/lo planes for "bf16x3", TF32-rounded fp32 for "tf32" (the tensor
+        # core would truncate those bits), plain fp32 for "3xtf32".
+        def ln_out(consumer):
+            if split[consumer]:
+                return ws.h2.data_ptr(), _lib.KF_LN_OUT_BF16X2 | ln_skip
+            rnd = _lib.KF_LN_ROUND_TF32 if (R and prec[consumer] == "tf32") else 0
+            return ws.h.data_ptr(), rnd | ln_skip
+
+        h_qkv, f_ln1 = ln_out("qkv")
+        h_ffn1, f_ln2 = ln_out("ffn1")
+        attn_flags = (_lib.KF_ATTN_CAUSAL if cfg.causal else 0)
+        if split["out"]:
+            attn_flags |= _lib.KF_ATTN_OUT_BF16X2
+        elif R and prec["out"] == "tf32":
+            attn_flags |= _lib.KF_ATTN_ROUND_TF32
+        if keep_u8 is not None and plan.skip_empty_queries:
+            attn_flags |= _lib.KF_ATTN_SKIP_EMPTY_Q
+        res, y, qkv = ws.res.data_ptr(), ws.y.data_ptr(), ws.qkv.data_ptr()
+        ctx, ffn = ws.ctx.data_ptr(), ws.ffn.data_ptr()
         ldq = 3 * H * dhs
         hd, hs = (dh, dhs) if dhs != dh else (0, 0)
         n = 0
@@ -220,28 +240,38 @@ class FusedTransformer(LayerStack):
                 ev1.record()
             n += 1
 
+        def gemm(kind, g, A, lda, W, bias, C, ldc, N, K, epi, flags, bn, hd_=0, hs_=0):
+            if split[g]:
+                run(kind, L.kf_gemm_bf16x3, A, lda, W.data_ptr(), K, bias.data_ptr(), C, ldc,
+                    M, N, K, epi, flags, bn, hd_, hs_, lt, lc, st)
+            else:
+                run(kind, L.kf_gemm_tf32, A, lda, W.data_ptr(), K, bias.data_ptr(), C, ldc, M,
+                    N, K, epi, flags | P[prec[g]], bn, hd_, hs_, lt, lc, st)
+
         if keep is not None:
             run("keep_bits", L.kf_keep_bits, keep, S, B, S, bits, st)
         if skip_rows:
             run("keep_bits", L.kf_live_row_tiles, keep, M, lt, lc, st)
         l0 = w.layers[0]
         run("ln", L.kf_ln_add_mask, x.data_ptr(), d, None, 0, keep, l0["ln1w"].data_ptr(),
-            l0["ln1b"].data_ptr(), res, d, h, d, M, d, l0["eps1"], rnd_h1, st)
+            l0["ln1b"].data_ptr(), res, d, h_qkv, d, M, d, l0["eps1"], f_ln1, st)
         nl = len(w.layers)
+        f_ffn1_out = _lib.KF_GEMM_OUT_BF16X2 if split["ffn2"] else (
+            _lib.KF_GEMM_ROUND_TF32 if (R and prec["ffn2"] == "tf32") else 0)
         for i, lw in enumerate(w.layers):
-            run("qkv", L.kf_gemm_tf32, h, d, lw["wqkv"].data_ptr(), d, lw["bqkv"].data_ptr(),
-                qkv, ldq, M, 3 * d, d, _lib.KF_EPI_BIAS, f_qkv, plan.bn_qkv, hd, hs, lt, lc, st)
+            gemm("qkv", "qkv", h_qkv, d, lw["wqkv"], lw["bqkv"], qkv, ldq, 3 * d, d,
+                 _lib.KF_EPI_BIAS, _lib.KF_GEMM_ROUND_TF32 if R else 0, plan.bn_qkv, hd, hs)
             run("attention", L.kf_flash_fwd_tf32, qkv, S * ldq, dhs, ldq,
                 qkv + 4 * H * dhs, S * ldq, dhs, ldq, qkv + 8 * H * dhs, S * ldq, dhs, ldq,
                 ctx, S * d, dh, d, bits, B, H, S, dhs, dh, dh ** -0.5, attn_flags, st)
-            run("out_proj", L.kf_gemm_tf32, ctx, d, lw["wo"].data_ptr(), d, lw["bo"].data_ptr(),
-                y, d, M, d, d, _lib.KF_EPI_BIAS, f_out, plan.bn_out, 0, 0, lt, lc, st)
+            gemm("out_proj", "out", ctx, d, lw["wo"], lw["bo"], y, d, d, d, _lib.KF_EPI_BIAS, 0,
+                 plan.bn_out)
             run("ln", L.kf_ln_add_mask, res, d, y, d, keep, lw["ln2w"].data_ptr(),
-                lw["ln2b"].data_ptr(), res, d, h, d, M, d, lw["eps2"], rnd_h2, st)
-            run("ffn1", L.kf_gemm_tf32, h, d, lw["w1"].data_ptr(), d, lw["b1"].data_ptr(), ffn,
-                F, M, F, d, _lib.KF_EPI_BIAS_GELU, f_ffn1, plan.bn_ffn1, 0, 0, lt, lc, st)
-            run("ffn2", L.kf_gemm_tf32, ffn, F, lw["w2"].data_ptr(), F, lw["b2"].data_ptr(), y,
-                d, M, d, F, _lib.KF_EPI_BIAS, f_ffn2, plan.bn_ffn2, 0, 0, lt, lc, st)
+                lw["ln2b"].data_ptr(), res, d, h_ffn1, d, M, d, lw["eps2"], f_ln2, st)
+            gemm("ffn1", "ffn1", h_ffn1, d, lw["w1"], lw["b1"], ffn, F, F, d,
+                 _lib.KF_EPI_BIAS_GELU, f_ffn1_out, plan.bn_ffn1)
+            gemm("ffn2", "ffn2", ffn, F, lw["w2"], lw["b2"], y, d, d, F, _lib.KF_EPI_BIAS, 0,
+                 plan.bn_ffn2)
             if i == nl - 1:
                 run("ln", L.kf_ln_add_mask, res, d, y, d, keep, w.finw.data_ptr(),
                     w.finb.data_ptr(), None, 0, out.data_ptr(), d, M, d, w.fin_eps,
@@ -249,7 +279,7 @@ class FusedTransformer(LayerStack):
             else:
                 nx = w.layers[i + 1]
                 run("ln", L.kf_ln_add_mask, res, d, y, d, keep, nx["ln1w"].data_ptr(),
-                    nx["ln1b"].data_ptr(), res, d, h, d, M, d, nx["eps1"], rnd_h1, st)
+                    nx["ln1b"].data_ptr(), res, d, h_qkv, d, M, d, nx["eps1"], f_ln1, st)
         self.launches_per_forward = n
         return n
 
@@ -305,7 +335,7 @@ class GraphRunner:
         self.static_out = torch.empty_like(self.static_x)
         self.weights = model.prepare(x.device)
         # A workspace of its own: eager calls of other shapes never alias it.
-        self.ws = _Workspace(model.config, B, S, x.device)
+        self.ws = _Workspace(model.config, B, S, x.device, model.plan)
         side = torch.cuda.Stream(device=x.device)
         side.wait_stream(torch.cuda.current_stream(x.device))
         with torch.cuda.stream(side):

@@ -338,3 +338,100 @@ def test_layernorm_skip_padded_leaves_padded_rows_untouched():
     dead = keep == 0
     assert torch.all(s[dead] == 5.0) and torch.all(h[dead] == 6.0)
     assert torch.equal(s[~dead], x[~dead])
+
+
+# --------------------------------------------------------------- pre-split bf16x3
+
+def to_planes(t: torch.Tensor) -> torch.Tensor:
+    """fp32 [..] -> int16 [2, ..] bf16 planes: hi = bf16_rn(t), lo = bf16_rn(t - hi)."""
+    hi = t.to(torch.bfloat16)
+    lo = (t - hi.float()).to(torch.bfloat16)
+    return torch.stack([hi.view(torch.int16), lo.view(torch.int16)])
+
+
+def from_planes(p: torch.Tensor) -> torch.Tensor:
+    return p[0].view(torch.bfloat16).float() + p[1].view(torch.bfloat16).float()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 64, 64), (517, 384, 512), (4096, 2048, 512),
+                                   (300, 200, 136), (2048, 512, 2048)])
+@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("gelu", [False, True])
+@pytest.mark.parametrize("out_split", [False, True])
+def test_gemm_bf16x3_presplit(M, N, K, bn, gelu, out_split):
+    from techjam2026_b200 import _lib
+    torch.manual_seed(M + N + K + bn)
+    a = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / math.sqrt(K)
+    bias = torch.randn(N, device="cuda")
+    a2, w2 = to_planes(a).contiguous(), to_planes(w).contiguous()
+    if out_split:
+        c = torch.zeros(2, M, N, dtype=torch.int16, device="cuda")
+    else:
+        c = torch.zeros(M, N, device="cuda")
+    flags = _lib.KF_GEMM_OUT_BF16X2 if out_split else 0
+    rc = _lib.lib().kf_gemm_bf16x3(a2.data_ptr(), K, w2.data_ptr(), K, bias.data_ptr(),
+                                   c.data_ptr(), N, M, N, K, 1 if gelu else 0, flags, bn, 0, 0,
+                                   None, None, _lib.stream_ptr())
+    _lib.check(rc, "kf_gemm_bf16x3")
+    got = from_planes(c) if out_split else c
+    ref = a.double() @ w.double().t() + bias.double()
+    if gelu:
+        ref = F.gelu(ref, approximate="none")
+    err = (got.double() - ref).abs().max().item()
+    assert err < 6e-4, f"max abs err {err}"
+
+
+def test_gemm_bf16x3_head_padded_output():
+    from techjam2026_b200 import _lib
+    torch.manual_seed(11)
+    M, N, K = 256, 3 * 128, 128
+    a = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / math.sqrt(K)
+    out = torch.full((M, 3 * 16 * 16), 7.0, device="cuda")
+    a2, w2 = to_planes(a).contiguous(), to_planes(w).contiguous()   # keep them alive
+    rc = _lib.lib().kf_gemm_bf16x3(a2.data_ptr(), K, w2.data_ptr(), K, None,
+                                   out.data_ptr(), out.stride(0), M, N, K, 0, 0, 0, 8, 16,
+                                   None, None, _lib.stream_ptr())
+    _lib.check(rc, "kf_gemm_bf16x3")
+    ref = (a.double() @ w.double().t()).view(M, 48, 8)
+    got = out.view(M, 48, 16)
+    assert (got[..., :8].double() - ref).abs().max().item() < 6e-4
+    assert torch.all(got[..., 8:] == 7.0)
+
+
+def test_layernorm_split_output():
+    from techjam2026_b200 import _lib
+    torch.manual_seed(12)
+    M, d = 517, 512
+    x, y = torch.randn(M, d, device="cuda"), torch.randn(M, d, device="cuda")
+    w, b = torch.randn(d, device="cuda"), torch.randn(d, device="cuda")
+    h2 = torch.zeros(2, M, d, dtype=torch.int16, device="cuda")
+    rc = _lib.lib().kf_ln_add_mask(x.data_ptr(), d, y.data_ptr(), d, None, w.data_ptr(),
+                                   b.data_ptr(), None, 0, h2.data_ptr(), d, M, d, 1e-5,
+                                   _lib.KF_LN_OUT_BF16X2, _lib.stream_ptr())
+    _lib.check(rc, "kf_ln_add_mask")
+    ref = F.layer_norm((x + y).double(), (d,), w.double(), b.double(), 1e-5)
+    assert torch.equal(h2, to_planes(F.layer_norm(x + y, (d,), w, b, 1e-5))) or \
+        (from_planes(h2).double() - ref).abs().max().item() < 1e-4
+
+
+def test_attention_split_output():
+    from techjam2026_b200 import _lib
+    torch.manual_seed(13)
+    B, H, S, Dh = 2, 4, 300, 64
+    q, k, v = (torch.randn(B, H, S, Dh, device="cuda") for _ in range(3))
+    keep = (torch.arange(S, device="cuda")[None, :] < torch.tensor([[300], [170]],
+                                                                    device="cuda")).to(torch.uint8)
+    ref = flash_attention(q, k, v, keep=keep, causal=True)
+    L = _lib.lib()
+    bits = torch.empty(int(L.kf_keep_bits_words(B, S)), dtype=torch.int32, device="cuda")
+    _lib.check(L.kf_keep_bits(keep.data_ptr(), S, B, S, bits.data_ptr(), _lib.stream_ptr()), "b")
+    o2 = torch.zeros(2, B, H, S, Dh, dtype=torch.int16, device="cuda")
+    st = q.stride()
+    rc = L.kf_flash_fwd_tf32(q.data_ptr(), *st[:3], k.data_ptr(), *st[:3], v.data_ptr(), *st[:3],
+                             o2.data_ptr(), *o2[0].stride()[:3], bits.data_ptr(), B, H, S, Dh, Dh,
+                             Dh ** -0.5, _lib.KF_ATTN_CAUSAL | _lib.KF_ATTN_OUT_BF16X2,
+                             _lib.stream_ptr())
+    _lib.check(rc, "kf_flash_fwd_tf32")
+    assert (from_planes(o2) - ref).abs().max().item() < 1e-4
