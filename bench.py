@@ -61,6 +61,8 @@ def parse_args():
                    help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--batch-size", type=int, default=None,
+                   help="rows per rank (default: the workload's batch); for bounded profiling")
     return p.parse_args()
 
 
@@ -150,12 +152,23 @@ class ClockSampler:
     """nvidia-smi samples every 10 ms; summary() keeps those stamped inside the
     timed window (mark_start/mark_end), falling back to the nearest ones when
     the window is shorter than the sampling period."""
-    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+    FIELDS = ("timestamp,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,"
+              "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
+    @staticmethod
+    def _bus(s: str) -> str:
+        # "00000000:1B:00.0" (nvidia-smi) and "0000:1b:00.0" (torch) -> "1b:00.0"
+        return s.strip().lower().split(":", 1)[-1]
+
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+        # nvidia-smi numbers GPUs physically; match this process's GPU by its
+        # PCI bus id, whatever CUDA_VISIBLE_DEVICES remaps.
+        try:
+            self.bus = self._bus(torch.cuda.get_device_properties(gpu_index).pci_bus_id)
+        except Exception:
+            self.bus = None
         self.proc = None
         self.path = None
         self.t0 = self.t1 = None
@@ -172,7 +185,7 @@ class ClockSampler:
             os.close(fd)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "10"],
                 stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
@@ -198,8 +211,13 @@ class ClockSampler:
                 parts = [p.strip() for p in line.split(",")]
                 if len(parts) < 10:
                     continue
+                if self.bus and self._bus(parts[1]) != self.bus:
+                    continue
                 try:
                     ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                except ValueError:
+                    ts = None
+                try:
                     rows.append((ts, float(parts[2]), float(parts[3]),
                                  [n for n, v in zip(names, parts[6:10]) if v.lower() == "active"]))
                 except ValueError:
@@ -207,13 +225,15 @@ class ClockSampler:
         os.unlink(self.path)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        inside = [r for r in rows if self.t0 and self.t1 and self.t0 <= r[0] <= self.t1]
+        stamped = [r for r in rows if r[0] is not None]
+        inside = [r for r in stamped if self.t0 and self.t1 and self.t0 <= r[0] <= self.t1]
         window = "inside the timed region"
-        if not inside and self.t0:
-            after = [r for r in rows if r[0] >= self.t0][:2]
-            before = [r for r in rows if r[0] < self.t0][-1:]
+        if not inside and self.t0 and stamped:
+            after = [r for r in stamped if r[0] >= self.t0][:2]
+            before = [r for r in stamped if r[0] < self.t0][-1:]
             inside, window = before + after, "nearest to the timed region (shorter than 10 ms)"
-        inside = inside or rows
+        if not inside:
+            inside, window = rows, "whole sampling period"
         return {"sm_mhz": statistics.median(r[1] for r in inside),
                 "sm_max_mhz": max(r[2] for r in inside), "samples": len(inside),
                 "window": window, "reasons": sorted({n for r in inside for n in r[3]})}
@@ -295,6 +315,9 @@ def main():
                                 timeout=datetime.timedelta(seconds=120))
 
     w = WORKLOADS[args.config]
+    if args.batch_size:
+        import dataclasses
+        w = dataclasses.replace(w, cfg=dataclasses.replace(w.cfg, batch_size=args.batch_size))
     cfg = w.cfg
     spec = probe(local)
     plan, source = DispatchTable.load_for(spec).lookup(spec.arch, torch.float32, cfg)
