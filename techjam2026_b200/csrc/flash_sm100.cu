@@ -85,6 +85,8 @@ __global__ void __launch_bounds__(192, MINB)
                           float scale_log2, int flags) {
   using Cfg = FlashCfg<DH, BN, KST, VST, MINB>;
   constexpr int BM = Cfg::BM;
+  pdl_launch_dependents();
+  pdl_wait();  // Q/K/V and the key bits come from earlier kernels
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -530,9 +532,9 @@ static int launch_flash(const float* q, const int64_t* qs, const float* k, const
   }
   const int n_qt = (S + Cfg::BM - 1) / Cfg::BM;
   dim3 grid(static_cast<unsigned>(n_qt), static_cast<unsigned>(B * H));
-  kern<<<grid, 192, Cfg::SMEM_BYTES, st>>>(tq, tk, tv, o, os[0], os[1], os[2], bits, H, S,
-                                             dh_out, scale_log2, flags);
-  return cuda_status(cudaGetLastError(), "kf_flash_fwd_tf32 launch");
+  return cuda_status(launch_chained(kern, grid, dim3(192), Cfg::SMEM_BYTES, st, tq, tk, tv, o,
+                                    os[0], os[1], os[2], bits, H, S, dh_out, scale_log2, flags),
+                     "kf_flash_fwd_tf32 launch");
 }
 
 }  // namespace kf

@@ -11,7 +11,7 @@
 //   warp 1      MMA issuer: allocates TMEM (two BN-column accumulators), one
 //               thread issues 4 tcgen05.mma (K = 8 each) per 32-wide k block
 //               and releases the smem stage with tcgen05.commit;
-//   warps 2-5   epilogue: tcgen05.ld the accumulator of a finished tile (warp w
+//   warps 2-9   epilogue (two halves of four, alternate 32-column chunks): tcgen05.ld the accumulator of a finished tile (warp w
 //               owns TMEM lanes 32*(w%4)..+31 = 32 output rows), add bias,
 //               optionally GELU(erf) and TF32 rounding, then write each
 //               128x32 chunk into a 128B-swizzled shared buffer and store it
@@ -20,7 +20,7 @@
 //               per thread; then hand the accumulator back to the MMA warp.
 //               Double buffering lets the epilogue of tile i overlap the main
 //               loop of tile i+1;
-//   warps 6-13  (split modes only) converters: once a stage has landed they
+//   warps 10-17 (split modes only) converters: once a stage has landed they
 //               write a hi/lo split of both fp32 tiles next to them in shared
 //               memory, so the MMA warp can issue the error-compensated
 //               product  A.B ~= hi(A).hi(B) + hi(A).lo(B) + lo(A).hi(B)
@@ -58,9 +58,12 @@ struct GemmCfg {
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int CONV_THREADS = 256;  // split modes: 8 converter warps
   static constexpr bool CONVERTS = SPLIT == 1 || SPLIT == 2;
-  static constexpr int THREADS = CONVERTS ? 192 + CONV_THREADS : 192;
+  static constexpr int EPI_WARPS = 8;       // two per TMEM lane quarter
+  static constexpr int CONV_WARP0 = 2 + EPI_WARPS;
+  static constexpr int THREADS = 32 * CONV_WARP0 + (CONVERTS ? CONV_THREADS : 0);
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int EPI_BUF_BYTES = BM * 32 * 4;  // one 128x32 fp32 output chunk
+  // Two buffers: one per epilogue half (each half stages its own chunks).
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = EPI_OFF + 2 * EPI_BUF_BYTES;
   static constexpr int BAR_BYTES = 256;
@@ -177,7 +180,7 @@ __device__ __forceinline__ void gemm_store_chunk(const float (&v)[32], float* __
 }
 
 template <int BN, int EPI, int SPLIT>
-__global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 448 : 192, 1)
+__global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int M,
                      int N, int K, int flags, int head_dim, int head_stride,
@@ -195,20 +198,12 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 448 : 192, 1)
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* epi_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* epi_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [2], per half
 
+  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_n = (N + BN - 1) / BN;
-  // Optional list of the 128-row tiles that hold at least one live row
-  // (kf_live_row_tiles); other row tiles are not computed and keep their
-  // contents. Every role reads the same list, so they agree on the schedule.
-  const int num_m = live_tiles ? __ldg(live_count) : (M + BM - 1) / BM;
-  const int num_tiles = num_m * num_n;
-  auto row0 = [&](int tile) -> int {
-    const int mi = tile / num_n;
-    return (live_tiles ? __ldg(live_tiles + mi) : mi) * BM;
-  };
   const int num_kb = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -219,7 +214,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 448 : 192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], Cfg::EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -236,6 +231,19 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 448 : 192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+
+  // Everything above overlaps the previous kernel; from here on we read its
+  // outputs (the A operand and the live-tile list).
+  pdl_wait();
+  // Optional list of the 128-row tiles that hold at least one live row
+  // (kf_live_row_tiles); other row tiles are not computed and keep their
+  // contents. Every role reads the same list, so they agree on the schedule.
+  const int num_m = live_tiles ? __ldg(live_count) : (M + BM - 1) / BM;
+  const int num_tiles = num_m * num_n;
+  auto row0 = [&](int tile) -> int {
+    const int mi = tile / num_n;
+    return (live_tiles ? __ldg(live_tiles + mi) : mi) * BM;
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -366,9 +374,9 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 448 : 192, 1)
       mma_commit(drain);
       mbar_wait_drain(drain, 0, KF_DEV_WAIT_TIMEOUT_MMA);
     }
-  } else if (Cfg::CONVERTS && warp >= 6) {
+  } else if (Cfg::CONVERTS && warp >= Cfg::CONV_WARP0) {
     // -------------------------------------------------- converters (warps 6..9)
-    const int ct = threadIdx.x - 192;
+    const int ct = threadIdx.x - 32 * Cfg::CONV_WARP0;
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -417,24 +425,30 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 448 : 192, 1)
       }
     }
   } else {
-    // -------------------------------------------------- epilogue (warps 2..5)
+    // ------------------------------------------ epilogue (warps 2..9, two halves)
+    // Warps 2-5 and 6-9 each cover all four TMEM lane quarters (warp w reads
+    // lanes 32*(w%4)..+31); half 0 takes the even 32-column chunks, half 1
+    // the odd ones, each with its own leader, named barrier (ids 1, 2) and
+    // staging buffer, so the two halves run independently.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int bar_id = 1 + half;
     const bool tma_out = (flags & KF_GEMM_TMA_OUT) != 0;
-    const bool leader = threadIdx.x == 64;
+    const bool leader = threadIdx.x == 64 + 128 * half;
     const bool rnd = (flags & KF_GEMM_ROUND_TF32) != 0;
-    int chunk = 0;
+    uint8_t* buf = smem + Cfg::EPI_OFF + half * Cfg::EPI_BUF_BYTES;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m0 = row0(tile);
       const int n0 = (tile % num_n) * BN;
-      // One bounded wait by the leader, shared through the named barrier, so
-      // all four warps always reach the same barriers (no warp can be left
-      // waiting for one that gave up).
-      if (leader) *epi_ok = mbar_wait(&acc_full[acc], acc_phase, abort_flag,
-                                      KF_DEV_WAIT_TIMEOUT_EPI) ? 1 : 0;
-      named_bar_sync(1, 128);
-      if (!*epi_ok) break;
+      // One bounded wait by the half's leader, shared through the half's
+      // named barrier, so all four warps of a half always reach the same
+      // barriers (no warp can be left waiting for one that gave up).
+      if (leader) epi_ok[half] = mbar_wait(&acc_full[acc], acc_phase, abort_flag,
+                                           KF_DEV_WAIT_TIMEOUT_EPI) ? 1 : 0;
+      named_bar_sync(bar_id, 128);
+      if (!epi_ok[half]) break;
       tc_fence_after();
       const int r = quarter * 32 + lane;
       const int row = m0 + r;
@@ -442,15 +456,14 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 448 : 192, 1)
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       float* crow = C + static_cast<int64_t>(row) * ldc;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        if (n0 + c >= N) break;  // warp-uniform
+      for (int c = 32 * half; c < BN; c += 64) {
+        if (n0 + c >= N) break;  // uniform over the half
         float v[32];
         tmem_ld32(tbase + static_cast<uint32_t>(c), v);
         if (tma_out && (flags & KF_GEMM_OUT_SPLIT)) {
           // bf16 hi/lo planes: two 128x32 bf16 tiles (64-byte rows, SW64).
-          uint8_t* buf = smem + Cfg::EPI_OFF + (chunk & 1) * Cfg::EPI_BUF_BYTES;
-          if (leader) bulk_wait_group_read<1>();
-          named_bar_sync(1, 128);
+          if (leader) bulk_wait_group_read<0>();  // this half's last store has read `buf`
+          named_bar_sync(bar_id, 128);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {  // 8 columns -> one 16-byte bf16 chunk
             float o[8];
@@ -476,17 +489,15 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 448 : 192, 1)
                            pack_bf16x2(lo[4], lo[5]), pack_bf16x2(lo[6], lo[7]));
           }
           fence_proxy_async_smem();
-          named_bar_sync(1, 128);
+          named_bar_sync(bar_id, 128);
           if (leader) {
             tma_store_3d(&tmC, buf, n0 + c, m0, 0);
             tma_store_3d(&tmC, buf + Cfg::EPI_BUF_BYTES / 2, n0 + c, m0, 1);
             bulk_commit_group();
           }
-          ++chunk;
         } else if (tma_out) {
-          uint8_t* buf = smem + Cfg::EPI_OFF + (chunk & 1) * Cfg::EPI_BUF_BYTES;
-          if (leader) bulk_wait_group_read<1>();  // the store that used `buf` is done reading
-          named_bar_sync(1, 128);
+          if (leader) bulk_wait_group_read<0>();  // this half's last store has read `buf`
+          named_bar_sync(bar_id, 128);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const int col = n0 + c + 4 * j;
@@ -509,12 +520,11 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 448 : 192, 1)
             *reinterpret_cast<float4*>(buf + r * 128 + ((j ^ (r & 7)) << 4)) = o;
           }
           fence_proxy_async_smem();  // generic smem writes -> TMA store reads
-          named_bar_sync(1, 128);
+          named_bar_sync(bar_id, 128);
           if (leader) {
             tma_store_2d(&tmC, buf, n0 + c, m0);
             bulk_commit_group();
           }
-          ++chunk;
         } else if (row < M) {
           gemm_store_chunk<EPI>(v, crow, bias, n0 + c, N, flags, head_dim, head_stride);
         }
@@ -522,7 +532,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 448 : 192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
-      named_bar_sync(1, 128);  // everyone has read *epi_ok before it is rewritten
+      named_bar_sync(bar_id, 128);  // the half has read epi_ok before it is rewritten
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -561,9 +571,10 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   // CTA per SM and let CTAs without work exit.
   const int tiles = ((M + Cfg::BM - 1) / Cfg::BM) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tc, C, ldc, bias, M, N, K, flags, hd,
-                                                     hs, live_tiles, live_count);
-  return cuda_status(cudaGetLastError(), "kf_gemm_tf32 launch");
+  return cuda_status(launch_chained(kern, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM_BYTES, st, ta,
+                                    tb, tc, C, ldc, bias, M, N, K, flags, hd, hs, live_tiles,
+                                    live_count),
+                     "kf_gemm_tf32 launch");
 }
 
 // Pick the N tile that minimises (waves x per-tile cost) on this GPU.

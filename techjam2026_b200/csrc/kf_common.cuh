@@ -13,6 +13,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/kf_sm100.h"
 
 // ~2 s at the 1.9 GHz boost clock. Every legitimate wait in these kernels is
@@ -43,6 +45,18 @@ __device__ __forceinline__ void record_device_status(int code) {
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+
+// ---------------------------------------------------------------- launch chaining
+//
+// Every kernel is launched with programmatic stream serialization (see
+// launch_chained below): it signals at entry that the next kernel may be
+// scheduled, and waits for its predecessor grid to complete (memory
+// visible) before it reads anything the predecessor wrote. The next
+// kernel's launch and set-up then overlap this kernel's tail.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ---------------------------------------------------------------- mbarrier
 
@@ -363,5 +377,24 @@ int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank
 
 // Number of SMs of the current device (cached per device).
 int sm_count();
+
+// Launch with programmatic stream serialization, so the kernel may start
+// while its predecessor in the stream finishes (it calls pdl_wait() before
+// touching the predecessor's output).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_chained(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                           cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 }  // namespace kf

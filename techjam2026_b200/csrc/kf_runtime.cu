@@ -83,6 +83,8 @@ int sm_count() {
 // One warp per 32 keys: ballot of keep != 0 (and k < S).
 __global__ void keep_bits_kernel(const uint8_t* __restrict__ keep, int64_t ld_keep, int64_t B,
                                  int64_t S, uint32_t* __restrict__ bits) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t words = (S + 31) / 32;
   const int64_t warp_global = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x & 31;
@@ -101,6 +103,8 @@ __global__ void keep_bits_kernel(const uint8_t* __restrict__ keep, int64_t ld_ke
 __global__ void __launch_bounds__(1024) live_row_tiles_kernel(const uint8_t* __restrict__ keep,
                                                               int64_t M, int32_t* __restrict__ tiles,
                                                               int32_t* __restrict__ count) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ int warp_sums[32];
   __shared__ int base;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -153,6 +157,8 @@ __global__ void __launch_bounds__(1024) live_row_tiles_kernel(const uint8_t* __r
 // dst = [2][rows][ld_dst] bf16 planes (hi, then lo) of src [rows][ld_src].
 __global__ void split_bf16x2_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
                                     int64_t ld_src, uint16_t* __restrict__ dst, int64_t ld_dst) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t n = rows * cols;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
@@ -167,6 +173,8 @@ __global__ void split_bf16x2_kernel(const float* __restrict__ src, int64_t rows,
 
 __global__ void round_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst,
                                   int64_t n) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += stride)
@@ -210,9 +218,10 @@ extern "C" int kf_keep_bits(const uint8_t* keep, int64_t ld_keep, int64_t B, int
   const int64_t warps = B * ((S + 31) / 32);
   const int threads = 256;
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
-  keep_bits_kernel<<<static_cast<unsigned>(blocks), threads, 0,
-                     static_cast<cudaStream_t>(stream)>>>(keep, ld_keep, B, S, bits);
-  return cuda_status(cudaGetLastError(), "kf_keep_bits launch");
+  return cuda_status(launch_chained(keep_bits_kernel, dim3(static_cast<unsigned>(blocks)),
+                                    dim3(threads), 0, static_cast<cudaStream_t>(stream), keep,
+                                    ld_keep, B, S, bits),
+                     "kf_keep_bits launch");
 }
 
 extern "C" int kf_live_row_tiles(const uint8_t* keep, int64_t M, int32_t* tiles, int32_t* count,
@@ -221,8 +230,9 @@ extern "C" int kf_live_row_tiles(const uint8_t* keep, int64_t M, int32_t* tiles,
     set_last_error("kf_live_row_tiles: invalid arguments");
     return KF_E_INVALID;
   }
-  live_row_tiles_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(keep, M, tiles, count);
-  return cuda_status(cudaGetLastError(), "kf_live_row_tiles launch");
+  return cuda_status(launch_chained(live_row_tiles_kernel, dim3(1), dim3(1024), 0,
+                                    static_cast<cudaStream_t>(stream), keep, M, tiles, count),
+                     "kf_live_row_tiles launch");
 }
 
 extern "C" int kf_split_bf16x2(const float* src, int64_t rows, int64_t cols, int64_t ld_src,
@@ -236,9 +246,10 @@ extern "C" int kf_split_bf16x2(const float* src, int64_t rows, int64_t cols, int
   int64_t blocks = (rows * cols + threads - 1) / threads;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
-  split_bf16x2_kernel<<<static_cast<unsigned>(blocks), threads, 0,
-                        static_cast<cudaStream_t>(stream)>>>(src, rows, cols, ld_src, dst2, ld_dst);
-  return cuda_status(cudaGetLastError(), "kf_split_bf16x2 launch");
+  return cuda_status(launch_chained(split_bf16x2_kernel, dim3(static_cast<unsigned>(blocks)),
+                                    dim3(threads), 0, static_cast<cudaStream_t>(stream), src, rows,
+                                    cols, ld_src, dst2, ld_dst),
+                     "kf_split_bf16x2 launch");
 }
 
 extern "C" int kf_round_tf32(const float* src, float* dst, int64_t n, void* stream) {
@@ -251,7 +262,8 @@ extern "C" int kf_round_tf32(const float* src, float* dst, int64_t n, void* stre
   int64_t blocks = (n + threads - 1) / threads;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
-  round_tf32_kernel<<<static_cast<unsigned>(blocks), threads, 0,
-                      static_cast<cudaStream_t>(stream)>>>(src, dst, n);
-  return cuda_status(cudaGetLastError(), "kf_round_tf32 launch");
+  return cuda_status(launch_chained(round_tf32_kernel, dim3(static_cast<unsigned>(blocks)),
+                                    dim3(threads), 0, static_cast<cudaStream_t>(stream), src, dst,
+                                    n),
+                     "kf_round_tf32 launch");
 }

@@ -33,6 +33,8 @@ __global__ void __launch_bounds__(256) ln_add_mask_vec_kernel(
     const float* __restrict__ w, const float* __restrict__ b, float* s_out, int64_t lds,
     float* __restrict__ h_out, int64_t ldh, int64_t M,
     int d, float eps, int flags) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= M) return;
@@ -113,6 +115,8 @@ __global__ void __launch_bounds__(256) ln_add_mask_scalar_kernel(
     const float* __restrict__ w, const float* __restrict__ b, float* s_out, int64_t lds,
     float* __restrict__ h_out, int64_t ldh, int64_t M,
     int d, float eps, int flags) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= M) return;
@@ -184,11 +188,12 @@ extern "C" int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64
   if (y) vec = vec && aligned16(y) && ldy % 4 == 0;
   if (s_out) vec = vec && aligned16(s_out) && lds % 4 == 0;
 
+  cudaError_t e;
   if (vec) {
     const int nv = (di / 4 + 31) / 32;
 #define KF_LN_LAUNCH(NV)                                                                      \
-  ln_add_mask_vec_kernel<NV><<<blocks, threads, 0, st>>>(x, ldx, y, ldy, keep, w, b, s_out, lds, \
-                                                         h_out, ldh, M, di, eps, flags)
+  e = launch_chained(ln_add_mask_vec_kernel<NV>, dim3(blocks), dim3(threads), 0, st, x, ldx, y,  \
+                     ldy, keep, w, b, s_out, lds, h_out, ldh, M, di, eps, flags)
     if (nv <= 1)
       KF_LN_LAUNCH(1);
     else if (nv <= 2)
@@ -205,8 +210,8 @@ extern "C" int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64
       KF_LN_LAUNCH(32);
 #undef KF_LN_LAUNCH
   } else {
-    ln_add_mask_scalar_kernel<<<blocks, threads, 0, st>>>(x, ldx, y, ldy, keep, w, b, s_out, lds,
-                                                          h_out, ldh, M, di, eps, flags);
+    e = launch_chained(ln_add_mask_scalar_kernel, dim3(blocks), dim3(threads), 0, st, x, ldx, y,
+                       ldy, keep, w, b, s_out, lds, h_out, ldh, M, di, eps, flags);
   }
-  return cuda_status(cudaGetLastError(), "kf_ln_add_mask launch");
+  return cuda_status(e, "kf_ln_add_mask launch");
 }
