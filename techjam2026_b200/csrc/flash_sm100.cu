@@ -22,6 +22,8 @@
 // causal mask only tiles up to the diagonal are visited. V is consumed
 // MN-major straight from its [S, Dh] layout (no transpose copy), through the
 // 32-byte-atom swizzle that MN-major TF32 operands require.
+#include <cstring>
+
 #include "kf_common.cuh"
 
 namespace kf {
@@ -46,7 +48,15 @@ struct FlashCfg {
   static constexpr int K_OFF = Q_BYTES;
   static constexpr int V_OFF = K_OFF + KST * KV_BYTES;
   static constexpr int BAR_OFF = V_OFF + VST * V_BYTES;
-  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  // The batch row's packed key bits (one word per 32 keys) are staged in
+  // shared memory behind the barriers, as many words as fit beside the tiles
+  // with MINB CTAs per SM (each CTA also pays 1 KB of system shared memory);
+  // longer rows are read from global memory instead.
+  static constexpr int SMEM_CAP = MINB == 1 ? 232448 : 233472 / MINB - 1024;
+  static constexpr int BITS_OFF = BAR_OFF + 256;
+  static constexpr int BITS_ROOM = (SMEM_CAP - BITS_OFF - 1024) / 4;
+  static constexpr int BITS_WORDS = BITS_ROOM >= 2048 ? 2048 : (BITS_ROOM & ~31);
+  static constexpr int SMEM_BYTES = BITS_OFF + BITS_WORDS * 4 + 1024;
   // Power-of-two TMEM allocation covering two S buffers and O; with MINB CTAs
   // per SM the allocations must fit the SM's 512 columns together.
   static constexpr int TMEM_NEED = 2 * BN + DH;
@@ -56,37 +66,40 @@ struct FlashCfg {
   static_assert(DH >= 16 && DH <= 256 && (DH & (DH - 1)) == 0, "DH");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "BN");
   static_assert(2 * BN + DH <= 512, "TMEM");
-  static_assert(SMEM_BYTES * MINB <= 232448, "smem");
+  static_assert(BITS_WORDS >= 32, "key-bit staging");
+  static_assert(SMEM_BYTES <= SMEM_CAP, "smem");
   static_assert(TMEM_COLS * MINB <= 512, "TMEM");
 };
 
-// Does KV tile j (keys [j*BN, j*BN+BN)) hold at least one valid key?
+// Does KV tile j (keys [j*BN, j*BN+BN)) hold at least one valid key? `kb`
+// is the row's key bits, staged in shared memory or in global memory.
 template <int BN>
-__device__ __forceinline__ bool kv_tile_live(const uint32_t* __restrict__ bits_b, int words, int j,
-                                             int S) {
+__device__ __forceinline__ bool kv_tile_live(const uint32_t* kb, int words, int j, int S) {
   const int k0 = j * BN;
   if (k0 >= S) return false;
-  if (!bits_b) return true;
+  if (!kb) return true;
   const int w0 = k0 >> 5;
   uint32_t any = 0;
 #pragma unroll
   for (int w = 0; w < BN / 32; ++w)
-    if (w0 + w < words) any |= __ldg(bits_b + w0 + w);
+    if (w0 + w < words) any |= kb[w0 + w];
   return any != 0;
 }
+
+// Internal flag: O is written through the tmO tensor map (TMA stores).
+constexpr int KF_ATTN_TMA_OUT = 1 << 9;
 
 template <int DH, int BN, int KST, int VST, int MINB>
 __global__ void __launch_bounds__(192, MINB)
     flash_fwd_tf32_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
-                          const __grid_constant__ CUtensorMap tmV, float* __restrict__ O,
+                          const __grid_constant__ CUtensorMap tmV,
+                          const __grid_constant__ CUtensorMap tmO, float* __restrict__ O,
                           int64_t o_sb, int64_t o_sh, int64_t o_sm,
                           const uint32_t* __restrict__ keep_bits, int H, int S, int dh_out,
                           float scale_log2, int flags) {
   using Cfg = FlashCfg<DH, BN, KST, VST, MINB>;
   constexpr int BM = Cfg::BM;
-  pdl_launch_dependents();
-  pdl_wait();  // Q/K/V and the key bits come from earlier kernels
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -117,46 +130,18 @@ __global__ void __launch_bounds__(192, MINB)
   const int bh = blockIdx.y;
   const int b = bh / H;
   const int h = bh % H;
+  const int nb = static_cast<int>(gridDim.y) / H;
   const int n_qt = gridDim.x;
   const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);
   const int q0 = qt * BM;
   const bool causal = (flags & KF_ATTN_CAUSAL) != 0;
+  const bool split = (flags & KF_ATTN_OUT_BF16X2) != 0;
   const int words = (S + 31) >> 5;
   const uint32_t* bits_b = keep_bits ? keep_bits + static_cast<int64_t>(b) * words : nullptr;
 
-  // Optional skip of a query tile without any valid query (rows later masked).
-  if ((flags & KF_ATTN_SKIP_EMPTY_Q) && bits_b) {
-    uint32_t any = 0;
-    for (int w = q0 >> 5; w < ((q0 + BM) >> 5) && w < words; ++w) any |= __ldg(bits_b + w);
-    if (!any) {
-      if (warp >= 2) {
-        const int r = (warp & 3) * 32 + lane;
-        const int qi = q0 + r;
-        if (qi < S) {
-          const int64_t off = static_cast<int64_t>(b) * o_sb + static_cast<int64_t>(h) * o_sh +
-                              static_cast<int64_t>(qi) * o_sm;
-          if (flags & KF_ATTN_OUT_BF16X2) {
-            uint16_t* ohi = reinterpret_cast<uint16_t*>(O) + off;
-            uint16_t* olo = ohi + static_cast<int64_t>(gridDim.y / H) * o_sb;
-            for (int c = 0; c < dh_out; ++c) ohi[c] = olo[c] = 0;
-          } else {
-            float* orow = O + off;
-            for (int c = 0; c < dh_out; ++c) orow[c] = 0.f;
-          }
-        }
-      }
-      return;
-    }
-  }
-
-  const int n_kv_all = (S + BN - 1) / BN;
-  int kv_end = n_kv_all;
-  if (causal) {
-    const int last_q = (q0 + BM - 1 < S - 1) ? q0 + BM - 1 : S - 1;
-    const int lim = last_q / BN + 1;
-    kv_end = lim < kv_end ? lim : kv_end;
-  }
-
+  // Set-up that reads nothing an earlier kernel writes (barriers, TMEM,
+  // descriptor prefetch) runs before the wait on the previous kernel, so it
+  // overlaps that kernel's tail.
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < KST; ++s) {
@@ -179,6 +164,7 @@ __global__ void __launch_bounds__(192, MINB)
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
+    if (flags & KF_ATTN_TMA_OUT) tma_prefetch_desc(&tmO);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -188,8 +174,83 @@ __global__ void __launch_bounds__(192, MINB)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // The next kernel is released only once every CTA of this one holds its
+  // TMEM, so a CTA of the next kernel that allocates TMEM before its own wait
+  // can only ever wait for columns that a running CTA will free.
+  pdl_launch_dependents();
+  pdl_wait();  // Q/K/V and the key bits come from earlier kernels
 
-  if (warp == 0) {
+  // Optional skip of a query tile without any valid query (rows later masked).
+  bool skip = false;
+  if ((flags & KF_ATTN_SKIP_EMPTY_Q) && bits_b) {
+    uint32_t any = 0;
+    for (int w = q0 >> 5; w < ((q0 + BM) >> 5) && w < words; ++w) any |= __ldg(bits_b + w);
+    skip = (any == 0);
+  }
+
+  const int n_kv_all = (S + BN - 1) / BN;
+  int kv_end = n_kv_all;
+  if (causal) {
+    const int last_q = (q0 + BM - 1 < S - 1) ? q0 + BM - 1 : S - 1;
+    const int lim = last_q / BN + 1;
+    kv_end = lim < kv_end ? lim : kv_end;
+  }
+
+  // Stage the key bits of keys [0, kv_end * BN) once; every role then tests
+  // tiles and masks keys from shared memory.
+  const uint32_t* kb = bits_b;
+  if (bits_b && !skip) {
+    const int need = (kv_end * BN + 31) >> 5;
+    const int nw = need < words ? need : words;
+    if (nw <= Cfg::BITS_WORDS) {
+      uint32_t* sbits = reinterpret_cast<uint32_t*>(smem + Cfg::BITS_OFF);
+      for (int w = threadIdx.x; w < nw; w += blockDim.x) sbits[w] = __ldg(bits_b + w);
+      kb = sbits;
+    }
+  }
+  __syncthreads();
+
+  if (skip) {
+    // Zero rows, written coalesced: one 32-row box of zeros in shared memory
+    // stored by TMA over every box of the tile, or whole rows by all threads.
+    if (flags & KF_ATTN_TMA_OUT) {
+      if (warp == 0) {
+        float4* z = reinterpret_cast<float4*>(sQ);
+        for (int i = lane; i < 32 * 128 / 16; i += 32) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          for (int rg = 0; rg < BM / 32 && q0 + rg * 32 < S; ++rg) {
+            if (!split) {
+              for (int c = 0; c < DH / 32; ++c) tma_store_4d(&tmO, sQ, c * 32, q0 + rg * 32, h, b);
+            } else {
+              for (int pl = 0; pl < 2; ++pl)
+                for (int c = 0; c < DH / 64; ++c)
+                  tma_store_4d(&tmO, sQ, c * 64, q0 + rg * 32, h, b + pl * nb);
+            }
+          }
+          bulk_commit_group();
+          bulk_wait_group_all();
+        }
+      }
+    } else {
+      const int rows = (S - q0 < BM) ? S - q0 : BM;
+      const int n = rows * dh_out;
+      const int64_t base = static_cast<int64_t>(b) * o_sb + static_cast<int64_t>(h) * o_sh +
+                           static_cast<int64_t>(q0) * o_sm;
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int r = i / dh_out;
+        const int64_t off = base + static_cast<int64_t>(r) * o_sm + (i - r * dh_out);
+        if (split) {
+          uint16_t* ohi = reinterpret_cast<uint16_t*>(O);
+          ohi[off] = 0;
+          ohi[off + static_cast<int64_t>(nb) * o_sb] = 0;
+        } else {
+          O[off] = 0.f;
+        }
+      }
+    }
+  } else if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
       mbar_arrive_expect_tx(q_full, Cfg::Q_BYTES);
@@ -201,7 +262,7 @@ __global__ void __launch_bounds__(192, MINB)
       long long k_issued = 0, v_issued = 0;
       bool ok = true;
       for (int j = 0; j < kv_end && ok; ++j) {
-        if (!kv_tile_live<BN>(bits_b, words, j, S)) continue;
+        if (!kv_tile_live<BN>(kb, words, j, S)) continue;
         if (!mbar_wait(&k_empty[ks], kph ^ 1u, abort_flag, KF_DEV_WAIT_TIMEOUT_TMA)) {
           ok = false;
           break;
@@ -279,7 +340,7 @@ __global__ void __launch_bounds__(192, MINB)
         return true;
       };
       for (int j = 0; j < kv_end && ok; ++j) {
-        if (!kv_tile_live<BN>(bits_b, words, j, S)) continue;
+        if (!kv_tile_live<BN>(kb, words, j, S)) continue;
         if (!mbar_wait(&k_full[ks], kph, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA)) {
           ok = false;
           break;
@@ -325,7 +386,7 @@ __global__ void __launch_bounds__(192, MINB)
     int it = 0;
     bool ok = true;
     for (int j = 0; j < kv_end; ++j) {
-      if (!kv_tile_live<BN>(bits_b, words, j, S)) continue;
+      if (!kv_tile_live<BN>(kb, words, j, S)) continue;
       const int sb = it & 1;
       if (!mbar_wait(&s_full[sb], static_cast<uint32_t>((it >> 1) & 1), abort_flag,
                      KF_DEV_WAIT_TIMEOUT_SOFTMAX)) {
@@ -344,26 +405,30 @@ __global__ void __launch_bounds__(192, MINB)
 #pragma unroll
       for (int w = 0; w < BN / 32; ++w) {
         const int wi = (k0 >> 5) + w;
-        kw[w] = bits_b ? (wi < words ? __ldg(bits_b + wi) : 0u) : 0xffffffffu;
+        kw[w] = kb ? (wi < words ? kb[wi] : 0u) : 0xffffffffu;
         all_keys = all_keys && (kw[w] == 0xffffffffu);
       }
       const bool diag = causal && (k0 + BN - 1 > q0);
-      float mx = -INFINITY;
-      if (all_keys && !diag) {
-#pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          s[c] *= scale_log2;
-          mx = fmaxf(mx, s[c]);
-        }
-      } else {
+      // Row max of the raw scores (the scale is positive, so it commutes
+      // with max and rounding is monotonic), then P = 2^(s*scale - m) with
+      // the scale folded into one FMA. Masked keys hold -inf and give P = 0.
+      // Eight partial maxima / sums keep the dependency chains short.
+      if (!(all_keys && !diag)) {
 #pragma unroll
         for (int c = 0; c < BN; ++c) {
           const int kidx = k0 + c;
           const bool valid = ((kw[c >> 5] >> (c & 31)) & 1u) && (kidx < S) && (!causal || kidx <= qi);
-          s[c] = valid ? s[c] * scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s[c]);
+          s[c] = valid ? s[c] : -INFINITY;
         }
       }
+      float mp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mp[u] = s[u];
+#pragma unroll
+      for (int c = 8; c < BN; ++c) mp[c & 7] = fmaxf(mp[c & 7], s[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))) *
+                       scale_log2;
       // Running max with lazy rescale: keep the old reference unless the new
       // max exceeds it by more than 8 (P stays <= 256 in fp32).
       float alpha = 1.f;
@@ -376,15 +441,19 @@ __global__ void __launch_bounds__(192, MINB)
         }
         m_run = mx;
       }
-      const float m_ref = (m_run == -INFINITY) ? 0.f : m_run;
-      float sum = 0.f;
+      const float neg_m = (m_run == -INFINITY) ? 0.f : -m_run;
+      float sp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) sp[u] = 0.f;
 #pragma unroll
       for (int c = 0; c < BN; ++c) {
-        const float p = round_tf32(fast_exp2(s[c] - m_ref));
+        // P is rounded to the nearest TF32 value (the tensor core would
+        // otherwise truncate it), on the integer pipe.
+        const float p = round_tf32_nonneg(fast_exp2(fmaf(s[c], scale_log2, neg_m)));
         s[c] = p;
-        sum += p;
+        sp[c & 7] += p;
       }
-      l_run += sum;
+      l_run += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       if (__any_sync(0xffffffffu, rescale_o)) {
         // O += P_{it-1} V_{it-1} must have landed before this row is rescaled.
         // The s_full arrival just observed implies PV_{it-2} is complete (the
@@ -419,18 +488,74 @@ __global__ void __launch_bounds__(192, MINB)
       float* orow = O + static_cast<int64_t>(b) * o_sb + static_cast<int64_t>(h) * o_sh +
                     static_cast<int64_t>(qi) * o_sm;
       const bool rnd = (flags & KF_ATTN_ROUND_TF32) != 0;
-      const bool split = (flags & KF_ATTN_OUT_BF16X2) != 0;
       // Split output: bf16 hi plane at O (bf16 elements, same strides), lo
       // plane B * o_sb elements further.
       uint16_t* ohi = reinterpret_cast<uint16_t*>(O) + static_cast<int64_t>(b) * o_sb +
                       static_cast<int64_t>(h) * o_sh + static_cast<int64_t>(qi) * o_sm;
-      uint16_t* olo = ohi + static_cast<int64_t>(gridDim.y / H) * o_sb;
+      uint16_t* olo = ohi + static_cast<int64_t>(nb) * o_sb;
       if (it > 0) {
         // o_final (one phase) rather than o_done: by now o_done may be two
         // phases behind, where a parity wait cannot tell the phases apart.
         if (mbar_wait(o_final, 0, abort_flag, KF_DEV_WAIT_TIMEOUT_SOFTMAX)) {
           tc_fence_after();
           const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+          if (flags & KF_ATTN_TMA_OUT) {
+            // The Q buffer is idle once o_final has fired (every MMA reading
+            // it has completed). Each warp stages its 32 rows there in the
+            // 128-byte-swizzled layout of the output map, chunk by chunk, and
+            // one lane stores them: fp32 chunks of 32 columns, or bf16 hi/lo
+            // planes of 64 columns (the lo plane is batch index b + B of the
+            // same map).
+            const int rows0 = q0 + quarter * 32;
+            const uint32_t sw = static_cast<uint32_t>(lane & 7);
+#pragma unroll 1
+            for (int c = 0; c < DH / 32; ++c) {
+              float o[32];
+              tmem_ld32(t_row + Cfg::O_COL + c * 32, o);
+#pragma unroll
+              for (int t = 0; t < 32; ++t) o[t] = rnd ? round_tf32(o[t] * inv_l) : o[t] * inv_l;
+              if (!split) {
+                uint8_t* rowp = sQ + c * BM * 128 + quarter * 32 * 128 + lane * 128;
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                  *reinterpret_cast<float4*>(rowp + ((u ^ sw) << 4)) =
+                      make_float4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
+              } else {
+                uint8_t* hrow = sQ + (c >> 1) * BM * 128 + quarter * 32 * 128 + lane * 128;
+                uint8_t* lrow = hrow + BM * DH * 2;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  uint32_t hw[4], lw[4];
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    uint16_t h0, h1, l0, l1;
+                    split_bf16(o[8 * u + 2 * e], h0, l0);
+                    split_bf16(o[8 * u + 2 * e + 1], h1, l1);
+                    hw[e] = h0 | (static_cast<uint32_t>(h1) << 16);
+                    lw[e] = l0 | (static_cast<uint32_t>(l1) << 16);
+                  }
+                  const uint32_t off = ((static_cast<uint32_t>((c & 1) * 4 + u)) ^ sw) << 4;
+                  *reinterpret_cast<uint4*>(hrow + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                  *reinterpret_cast<uint4*>(lrow + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                }
+              }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && rows0 < S) {
+              if (!split) {
+                for (int c = 0; c < DH / 32; ++c)
+                  tma_store_4d(&tmO, sQ + c * BM * 128 + quarter * 32 * 128, c * 32, rows0, h, b);
+              } else {
+                for (int pl = 0; pl < 2; ++pl)
+                  for (int c = 0; c < DH / 64; ++c)
+                    tma_store_4d(&tmO, sQ + pl * BM * DH * 2 + c * BM * 128 + quarter * 32 * 128,
+                                 c * 64, rows0, h, b + pl * nb);
+              }
+              bulk_commit_group();
+              bulk_wait_group_all();
+            }
+          } else {
 #pragma unroll 1
           for (int c = 0; c < (DH + 31) / 32; ++c) {
             float o[32];
@@ -465,6 +590,7 @@ __global__ void __launch_bounds__(192, MINB)
                 }
               }
             }
+          }
           }
         }
       } else if (qi < S) {
@@ -518,6 +644,33 @@ static int launch_flash(const float* q, const int64_t* qs, const float* k, const
                            CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
   }
   if (rc) return rc;
+  // O through TMA stores when the output rows are whole 128-byte swizzle
+  // rows: fp32 with Dh >= 32, or bf16 planes with Dh >= 64, 16-byte aligned
+  // base and strides. Anything else (a zero-padded head, odd strides) keeps
+  // the per-thread stores.
+  CUtensorMap to;
+  memset(&to, 0, sizeof(to));
+  {
+    const bool split = (flags & KF_ATTN_OUT_BF16X2) != 0;
+    const int esz = split ? 2 : 4;
+    const int64_t align = 16 / esz;
+    const bool ok = dh_out == DH && DH >= (split ? 64 : 32) &&
+                    !(reinterpret_cast<uintptr_t>(o) & 15u) && os[0] % align == 0 &&
+                    os[1] % align == 0 && os[2] % align == 0;
+    if (ok) {
+      const uint64_t odims[4] = {static_cast<uint64_t>(DH), static_cast<uint64_t>(S),
+                                 static_cast<uint64_t>(H),
+                                 static_cast<uint64_t>(split ? 2 * B : B)};
+      const uint64_t ostr[3] = {static_cast<uint64_t>(os[2]) * esz,
+                                static_cast<uint64_t>(os[1]) * esz,
+                                static_cast<uint64_t>(os[0]) * esz};
+      const uint32_t obox[4] = {static_cast<uint32_t>(128 / esz), 32, 1, 1};
+      if (encode_tensor_map(&to, split ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                            4, o, odims, ostr, obox, CU_TENSOR_MAP_SWIZZLE_128B) == KF_OK)
+        flags |= KF_ATTN_TMA_OUT;
+    }
+  }
 
   auto kern = flash_fwd_tf32_kernel<DH, BN, KST, VST, MINB>;
   static int attr_set[64] = {0};
@@ -532,7 +685,7 @@ static int launch_flash(const float* q, const int64_t* qs, const float* k, const
   }
   const int n_qt = (S + Cfg::BM - 1) / Cfg::BM;
   dim3 grid(static_cast<unsigned>(n_qt), static_cast<unsigned>(B * H));
-  return cuda_status(launch_chained(kern, grid, dim3(192), Cfg::SMEM_BYTES, st, tq, tk, tv, o,
+  return cuda_status(launch_chained(kern, grid, dim3(192), Cfg::SMEM_BYTES, st, tq, tk, tv, to, o,
                                     os[0], os[1], os[2], bits, H, S, dh_out, scale_log2, flags),
                      "kf_flash_fwd_tf32 launch");
 }

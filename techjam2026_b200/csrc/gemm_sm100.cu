@@ -127,10 +127,6 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uin
       : "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.f + erff(x * 0.70710678118654752440f));
 }
@@ -200,7 +196,6 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* epi_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [2], per half
 
-  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_n = (N + BN - 1) / BN;
@@ -232,6 +227,10 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // The next kernel is released only once every CTA of this one holds its
+  // TMEM (a CTA of the next kernel may allocate before its own wait, and must
+  // then only ever wait for columns that a running CTA will free).
+  pdl_launch_dependents();
   // Everything above overlaps the previous kernel; from here on we read its
   // outputs (the A operand and the live-tile list).
   pdl_wait();

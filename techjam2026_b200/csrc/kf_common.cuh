@@ -155,6 +155,12 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads of them (TMA stores, tensor-core operand fetches).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Tiled TMA store shared -> global (bulk-group completion). x must be a
 // multiple of 16 bytes and non-negative; out-of-range parts are clipped.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0,
@@ -171,6 +177,14 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
       "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
           reinterpret_cast<uint64_t>(map)),
       "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1,
+                                             int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() {
@@ -348,6 +362,15 @@ __device__ __forceinline__ void store_split4(uint16_t* hi_plane, uint16_t* lo_pl
       make_uint2(h0 | (static_cast<uint32_t>(h1) << 16), h2 | (static_cast<uint32_t>(h3) << 16));
   *reinterpret_cast<uint2*>(lo_plane) =
       make_uint2(l0 | (static_cast<uint32_t>(l1) << 16), l2 | (static_cast<uint32_t>(l3) << 16));
+}
+
+// Round a non-negative finite float to the nearest TF32 value, ties away from
+// zero (the result cvt.rna.tf32.f32 gives), with integer operations: add half
+// a unit in the last of the 10 kept mantissa bits, then clear the 13 dropped
+// bits. A carry out of the mantissa correctly bumps the exponent. Keeps the
+// conversion off the multi-function unit, which the exponentials saturate.
+__device__ __forceinline__ float round_tf32_nonneg(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
 }
 
 // 2^x on the SFU (ex2.approx: max relative error 2^-22 over the full range).

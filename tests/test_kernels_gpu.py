@@ -435,3 +435,99 @@ def test_attention_split_output():
                              _lib.stream_ptr())
     _lib.check(rc, "kf_flash_fwd_tf32")
     assert (from_planes(o2) - ref).abs().max().item() < 1e-4
+
+
+def _flash_raw(q, k, v, keep, o, flags, o_strides=None, dh_out=None):
+    """kf_flash_fwd_tf32 on [B, H, S, Dh] views with an explicit output
+    buffer and strides (batch, head, row)."""
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    B, H, S, Dh = q.shape
+    bits = None
+    if keep is not None:
+        bits = torch.empty(int(L.kf_keep_bits_words(B, S)), dtype=torch.int32, device="cuda")
+        _lib.check(L.kf_keep_bits(keep.data_ptr(), S, B, S, bits.data_ptr(), _lib.stream_ptr()),
+                   "kf_keep_bits")
+    st = q.stride()
+    rc = L.kf_flash_fwd_tf32(q.data_ptr(), *st[:3], k.data_ptr(), *st[:3], v.data_ptr(), *st[:3],
+                             o.data_ptr(), *o_strides, bits.data_ptr() if bits is not None else None,
+                             B, H, S, Dh, dh_out or Dh, Dh ** -0.5, flags, _lib.stream_ptr())
+    _lib.check(rc, "kf_flash_fwd_tf32")
+    torch.cuda.synchronize()
+    return bits
+
+
+@pytest.mark.parametrize("Dh", [32, 64, 128, 256])
+@pytest.mark.parametrize("split", [False, True])
+@pytest.mark.parametrize("row_pad", [0, 4])
+def test_flash_output_paths(Dh, split, row_pad):
+    """The output tile is written by TMA stores when rows are whole 128-byte
+    swizzle rows with 16-byte aligned strides, else by per-thread stores
+    (row_pad = 4 elements breaks the alignment for bf16 planes, and an odd
+    row stride for fp32). Both write the same values, into [B, S, H, Dh]
+    rows, bf16 hi/lo planes B batches apart, and nothing outside the rows."""
+    from techjam2026_b200 import _lib
+    torch.manual_seed(20 + Dh)
+    B, H, S = 2, 3, 333
+    q, k, v = (torch.randn(B, H, S, Dh, device="cuda") for _ in range(3))
+    keep = (torch.arange(S, device="cuda")[None, :] < torch.tensor([[333], [150]],
+                                                                    device="cuda")).to(torch.uint8)
+    ref = reference_attention(q, k, v, keep, True)
+    pad = row_pad if split else (row_pad // 4)     # fp32: 1 element -> unaligned rows
+    row = H * Dh + pad
+    flags = _lib.KF_ATTN_CAUSAL
+    if split:
+        flags |= _lib.KF_ATTN_OUT_BF16X2
+        buf = torch.full((2 * B, S, row), 0x1234, dtype=torch.int16, device="cuda")
+    else:
+        buf = torch.full((B, S, row), 7.0, device="cuda")
+    _flash_raw(q, k, v, keep, buf, flags, (S * row, Dh, row))
+    got_rows = buf[..., :H * Dh]
+    if split:
+        got = from_planes(got_rows.reshape(2, B, S, H * Dh))
+        if pad:
+            assert torch.all(buf[..., H * Dh:] == 0x1234)
+        tol = 1e-4                            # the bf16 pair carries ~2^-17 relative error
+    else:
+        got = got_rows
+        if pad:
+            assert torch.all(buf[..., H * Dh:] == 7.0)
+        tol = 5e-3
+    got = got.reshape(B, S, H, Dh).permute(0, 2, 1, 3).double()
+    fa = flash_attention(q, k, v, keep=keep, causal=True)
+    if split:
+        assert (got - fa.double()).abs().max().item() < tol
+    assert (got - ref).abs().max().item() < 5e-3
+
+
+def _reference_rows(q, k, v, keep, causal, rows):
+    """float64 attention for the query rows `rows` only (against all keys)."""
+    scale = q.shape[-1] ** -0.5
+    qs = q[:, :, rows].double()
+    scores = qs @ k.double().transpose(-2, -1) * scale
+    S = k.shape[2]
+    if causal:
+        r = torch.as_tensor(rows, device=q.device)[:, None]
+        scores = scores.masked_fill(torch.arange(S, device=q.device)[None, :] > r, float("-inf"))
+    if keep is not None:
+        scores = scores.masked_fill(~keep.bool()[:, None, None, :], float("-inf"))
+    p = torch.nan_to_num(torch.softmax(scores, dim=-1), nan=0.0)
+    return p @ v.double()
+
+
+@pytest.mark.parametrize("Dh,S", [(64, 66000), (256, 15000)])
+def test_flash_key_bits_beyond_shared_memory_staging(Dh, S):
+    """Rows whose key bits exceed the shared-memory staging area (2048 words
+    at Dh 64, 448 at Dh 256) read them from global memory; a non-prefix mask
+    makes every tile's bits matter."""
+    from techjam2026_b200 import _lib
+    torch.manual_seed(30)
+    B, H = 1, 1
+    q, k, v = (torch.randn(B, H, S, Dh, device="cuda") for _ in range(3))
+    keep = (torch.rand(B, S, device="cuda") > 0.3).to(torch.uint8)
+    keep[:, 5000:9000] = 0
+    o = torch.empty(B, H, S, Dh, device="cuda")
+    _flash_raw(q, k, v, keep, o, _lib.KF_ATTN_CAUSAL, o.stride()[:3])
+    rows = list(range(0, 64)) + list(range(6000, 6100)) + list(range(S - 200, S))
+    ref = _reference_rows(q, k, v, keep, True, rows)
+    assert (o[:, :, rows].double() - ref).abs().max().item() < 5e-3
