@@ -3,11 +3,12 @@
 //
 // One CTA = one (batch, head, 128-query tile). Warp roles:
 //   warp 0      TMA producer: Q once, then K and V tiles of BN keys through
-//               two independent smem rings (K released as soon as S = QK^T is
-//               done, V after O += PV);
-//   warp 1      MMA issuer and TMEM owner. TMEM holds two S buffers (BN fp32
+//               two independent smem rings, each refilled as soon as its slot
+//               frees (K once S = QK^T is done, V after O += PV);
+//   warp 1      MMA issuer and TMEM owner. TMEM holds three S buffers (BN fp32
 //               columns each) and the O accumulator (DH columns). S_j = Q K_j^T
-//               is issued one tile ahead of the softmax, and O += P_j V_j
+//               is issued right after O += P_{j-2} V_{j-2}, a whole softmax
+//               pass before it is needed, and O += P_j V_j
 //               reads P straight from TMEM (tcgen05.mma A operand in TMEM), so
 //               P never touches shared memory;
 //   warps 2-5   softmax: one thread per query row (TMEM lane). Reads its S row,
@@ -57,15 +58,22 @@ struct FlashCfg {
   static constexpr int BITS_ROOM = (SMEM_CAP - BITS_OFF - 1024) / 4;
   static constexpr int BITS_WORDS = BITS_ROOM >= 2048 ? 2048 : (BITS_ROOM & ~31);
   static constexpr int SMEM_BYTES = BITS_OFF + BITS_WORDS * 4 + 1024;
-  // Power-of-two TMEM allocation covering two S buffers and O; with MINB CTAs
+  // Power-of-two TMEM allocation covering the S buffers and O; with MINB CTAs
   // per SM the allocations must fit the SM's 512 columns together.
-  static constexpr int TMEM_NEED = 2 * BN + DH;
+  // S buffers in TMEM: with three, S = Q K^T runs two KV tiles ahead of the
+  // softmax, so the next S is ready when a softmax pass ends.
+  static constexpr int NSB = 3;
+  static constexpr int TMEM_NEED = NSB * BN + DH;
   static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64
                                  : TMEM_NEED <= 128 ? 128 : TMEM_NEED <= 256 ? 256 : 512;
-  static constexpr int O_COL = 2 * BN;
+  static constexpr int O_COL = NSB * BN;
   static_assert(DH >= 16 && DH <= 256 && (DH & (DH - 1)) == 0, "DH");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "BN");
-  static_assert(2 * BN + DH <= 512, "TMEM");
+  static_assert(NSB * BN + DH <= 512, "TMEM");
+  // The producer reuses a K slot on the s_full phase of the tile KST back and
+  // a V slot on the o_done phase of the tile VST back; those parity tests are
+  // exact only with KST <= NSB and VST <= 2.
+  static_assert(KST <= NSB && VST <= 2, "ring depths");
   static_assert(BITS_WORDS >= 32, "key-bit staging");
   static_assert(SMEM_BYTES <= SMEM_CAP, "smem");
   static_assert(TMEM_COLS * MINB <= 512, "TMEM");
@@ -109,13 +117,11 @@ __global__ void __launch_bounds__(192, MINB)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;
-  uint64_t* k_empty = k_full + KST;
-  uint64_t* v_full = k_empty + KST;
-  uint64_t* v_empty = v_full + VST;
-  uint64_t* s_full = v_empty + VST;  // [2]
-  uint64_t* p_full = s_full + 2;     // [2]
-  uint64_t* o_done = p_full + 2;
-  uint64_t* o_final = o_done + 1;
+  uint64_t* v_full = k_full + KST;
+  uint64_t* s_full = v_full + VST;        // [NSB]
+  uint64_t* p_full = s_full + Cfg::NSB;   // [NSB]
+  uint64_t* o_done = p_full + Cfg::NSB;   // [2]: P V products of even / odd index
+  uint64_t* o_final = o_done + 2;
   uint64_t* drain = o_final + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -146,17 +152,16 @@ __global__ void __launch_bounds__(192, MINB)
     mbar_init(q_full, 1);
     for (int s = 0; s < KST; ++s) {
       mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
     }
     for (int s = 0; s < VST; ++s) {
       mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < Cfg::NSB; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], 4);
     }
-    mbar_init(o_done, 1);
+    mbar_init(&o_done[0], 1);
+    mbar_init(&o_done[1], 1);
     mbar_init(o_final, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -257,39 +262,72 @@ __global__ void __launch_bounds__(192, MINB)
 #pragma unroll
       for (int c = 0; c < Cfg::NCH; ++c)
         tma_load_4d(sQ + c * BM * Cfg::RB, &tmQ, q_full, c * Cfg::CH, q0, h, b);
+      // K and V advance independently: the next K tile is loaded as soon as
+      // its ring slot is free, without queueing behind the V slot, which
+      // frees only after the slower P V product. One thread polls both rings.
+      // A K slot is free once S of the tile KST back has completed (its
+      // s_full phase), a V slot once P V of the tile VST back has (its o_done
+      // phase); no separate release barriers. Loads go out in tile order, so
+      // each of those barriers is at most one phase behind the one tested and
+      // the parity test is exact.
       int ks = 0, vs = 0;
-      uint32_t kph = 0, vph = 0;
       long long k_issued = 0, v_issued = 0;
       bool ok = true;
-      for (int j = 0; j < kv_end && ok; ++j) {
-        if (!kv_tile_live<BN>(kb, words, j, S)) continue;
-        if (!mbar_wait(&k_empty[ks], kph ^ 1u, abort_flag, KF_DEV_WAIT_TIMEOUT_TMA)) {
+      auto k_slot_free = [&]() -> bool {
+        if (k_issued < KST) return true;
+        const long long i = k_issued - KST;
+        return mbar_test_wait(&s_full[i % Cfg::NSB], static_cast<uint32_t>((i / Cfg::NSB) & 1));
+      };
+      auto v_slot_free = [&]() -> bool {
+        if (v_issued < VST) return true;
+        const long long i = v_issued - VST;
+        return mbar_test_wait(&o_done[i & 1], static_cast<uint32_t>((i >> 1) & 1));
+      };
+      auto next_live = [&](int j) {
+        while (j < kv_end && !kv_tile_live<BN>(kb, words, j, S)) ++j;
+        return j;
+      };
+      int jk = next_live(0), jv = jk;
+      long long t_idle = clock64();
+      while (jk < kv_end || jv < kv_end) {
+        bool progress = false;
+        if (jk < kv_end && k_slot_free()) {
+          mbar_arrive_expect_tx(&k_full[ks], Cfg::KV_BYTES);
+#pragma unroll
+          for (int c = 0; c < Cfg::NCH; ++c)
+            tma_load_4d(sK + ks * Cfg::KV_BYTES + c * BN * Cfg::RB, &tmK, &k_full[ks], c * Cfg::CH,
+                        jk * BN, h, b);
+          ++k_issued;
+          if (++ks == KST) ks = 0;
+          jk = next_live(jk + 1);
+          progress = true;
+        }
+        if (jv < kv_end && v_slot_free()) {
+          mbar_arrive_expect_tx(&v_full[vs], Cfg::V_BYTES);
+#pragma unroll
+          for (int c = 0; c < Cfg::VCH; ++c)
+            tma_load_4d(sV + vs * Cfg::V_BYTES + c * BN * 128, &tmV, &v_full[vs], c * 32, jv * BN, h,
+                        b);
+          ++v_issued;
+          if (++vs == VST) vs = 0;
+          jv = next_live(jv + 1);
+          progress = true;
+        }
+        if (progress) {
+          t_idle = clock64();
+          continue;
+        }
+        // Nothing to issue: back off briefly so the poll does not take issue
+        // slots from the softmax warp that shares this scheduler.
+        __nanosleep(64);
+        if (*abort_flag) {
           ok = false;
           break;
-        }
-        mbar_arrive_expect_tx(&k_full[ks], Cfg::KV_BYTES);
-#pragma unroll
-        for (int c = 0; c < Cfg::NCH; ++c)
-          tma_load_4d(sK + ks * Cfg::KV_BYTES + c * BN * Cfg::RB, &tmK, &k_full[ks], c * Cfg::CH,
-                      j * BN, h, b);
-        ++k_issued;
-        if (++ks == KST) {
-          ks = 0;
-          kph ^= 1u;
-        }
-        if (!mbar_wait(&v_empty[vs], vph ^ 1u, abort_flag, KF_DEV_WAIT_TIMEOUT_TMA)) {
+        } else if (clock64() - t_idle > KF_WAIT_CYCLES) {
+          *abort_flag = 1;
+          record_device_status(KF_DEV_WAIT_TIMEOUT_TMA);
           ok = false;
           break;
-        }
-        mbar_arrive_expect_tx(&v_full[vs], Cfg::V_BYTES);
-#pragma unroll
-        for (int c = 0; c < Cfg::VCH; ++c)
-          tma_load_4d(sV + vs * Cfg::V_BYTES + c * BN * 128, &tmV, &v_full[vs], c * 32, j * BN, h,
-                      b);
-        ++v_issued;
-        if (++vs == VST) {
-          vs = 0;
-          vph ^= 1u;
         }
       }
       if (!ok) {
@@ -315,8 +353,8 @@ __global__ void __launch_bounds__(192, MINB)
       bool ok = mbar_wait(q_full, 0, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA);
       int it = 0;
       auto issue_pv = [&](int i) -> bool {
-        const int sb = i & 1;
-        if (!mbar_wait(&p_full[sb], static_cast<uint32_t>((i >> 1) & 1), abort_flag,
+        const int sb = i % Cfg::NSB;
+        if (!mbar_wait(&p_full[sb], static_cast<uint32_t>((i / Cfg::NSB) & 1), abort_flag,
                        KF_DEV_WAIT_TIMEOUT_MMA))
           return false;
         if (!mbar_wait(&v_full[vs], vph, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA)) return false;
@@ -331,8 +369,7 @@ __global__ void __launch_bounds__(192, MINB)
           mma_tf32_ts(tmem_base + Cfg::O_COL, tmem_base + sb * BN + kk * 8, bd, idesc_o,
                       (i > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(&v_empty[vs]);
-        mma_commit(o_done);
+        mma_commit(&o_done[i & 1]);
         if (++vs == VST) {
           vs = 0;
           vph ^= 1u;
@@ -341,12 +378,20 @@ __global__ void __launch_bounds__(192, MINB)
       };
       for (int j = 0; j < kv_end && ok; ++j) {
         if (!kv_tile_live<BN>(kb, words, j, S)) continue;
+        // P V of tile it - (NSB - 1) first: it waits only for that tile's
+        // softmax, never for the K load of tile it, and it frees the S buffer
+        // that S_it overwrites (the pipe runs in issue order). S_it is then
+        // issued a whole softmax pass before it is needed.
+        if (it >= Cfg::NSB - 1 && !issue_pv(it - (Cfg::NSB - 1))) {
+          ok = false;
+          break;
+        }
         if (!mbar_wait(&k_full[ks], kph, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int sb = it & 1;
+        const int sb = it % Cfg::NSB;
         const uint32_t kbase = sKa + ks * Cfg::KV_BYTES;
 #pragma unroll
         for (int kk = 0; kk < DH / 8; ++kk) {
@@ -358,19 +403,16 @@ __global__ void __launch_bounds__(192, MINB)
                                              8 * Cfg::RB, Cfg::LAYOUT);
           mma_tf32_ss(tmem_base + sb * BN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
-        mma_commit(&k_empty[ks]);
         mma_commit(&s_full[sb]);
         if (++ks == KST) {
           ks = 0;
           kph ^= 1u;
         }
-        if (it > 0 && !issue_pv(it - 1)) {
-          ok = false;
-          break;
-        }
         ++it;
       }
-      if (ok && it > 0 && issue_pv(it - 1)) mma_commit(o_final);
+      for (int i = (it > Cfg::NSB - 1 ? it - (Cfg::NSB - 1) : 0); ok && i < it; ++i)
+        ok = issue_pv(i);
+      if (ok && it > 0) mma_commit(o_final);
       mma_commit(drain);
       mbar_wait_drain(drain, 0, KF_DEV_WAIT_TIMEOUT_MMA);
     }
@@ -387,8 +429,8 @@ __global__ void __launch_bounds__(192, MINB)
     bool ok = true;
     for (int j = 0; j < kv_end; ++j) {
       if (!kv_tile_live<BN>(kb, words, j, S)) continue;
-      const int sb = it & 1;
-      if (!mbar_wait(&s_full[sb], static_cast<uint32_t>((it >> 1) & 1), abort_flag,
+      const int sb = it % Cfg::NSB;
+      if (!mbar_wait(&s_full[sb], static_cast<uint32_t>((it / Cfg::NSB) & 1), abort_flag,
                      KF_DEV_WAIT_TIMEOUT_SOFTMAX)) {
         ok = false;
         break;
@@ -457,10 +499,11 @@ __global__ void __launch_bounds__(192, MINB)
       if (__any_sync(0xffffffffu, rescale_o)) {
         // O += P_{it-1} V_{it-1} must have landed before this row is rescaled.
         // The s_full arrival just observed implies PV_{it-2} is complete (the
-        // MMA pipe completes in issue order and S_it was issued after it), so
-        // o_done is at most one phase behind and the parity wait is exact.
-        if (!mbar_wait(o_done, static_cast<uint32_t>((it - 1) & 1), abort_flag,
-                       KF_DEV_WAIT_TIMEOUT_SOFTMAX)) {
+        // MMA pipe completes in issue order and S_it was issued after it).
+        // o_done[(it-1) & 1] counts the products of that parity, so it is at
+        // most one phase (PV_{it-1} itself) behind and the parity wait is exact.
+        if (!mbar_wait(&o_done[(it - 1) & 1], static_cast<uint32_t>(((it - 1) >> 1) & 1),
+                       abort_flag, KF_DEV_WAIT_TIMEOUT_SOFTMAX)) {
           ok = false;
           break;
         }
@@ -615,7 +658,7 @@ __global__ void __launch_bounds__(192, MINB)
   }
 }
 
-template <int DH, int BN, int KST, int VST, int MINB = 1>
+template <int DH, int BN, int KST, int VST, int MINB>
 static int launch_flash(const float* q, const int64_t* qs, const float* k, const int64_t* ks,
                         const float* v, const int64_t* vs, float* o, const int64_t* os,
                         const uint32_t* bits, int B, int H, int S, int dh_stored, int dh_out,
@@ -748,18 +791,18 @@ extern "C" int kf_flash_fwd_tf32(const float* q, int64_t q_sb, int64_t q_sh, int
   switch (dh) {
     case 16:
       return launch_flash<16, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
-                                         dh_out, scale_log2, f, st);
+                                           dh_out, scale_log2, f, st);
     case 32:
       return launch_flash<32, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
-                                         dh_out, scale_log2, f, st);
+                                           dh_out, scale_log2, f, st);
     case 64:
       return launch_flash<64, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
-                                         dh_out, scale_log2, f, st);
+                                           dh_out, scale_log2, f, st);
     case 128:
-      return launch_flash<128, 64, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
-                                         dh_out, scale_log2, f, st);
+      return launch_flash<128, 64, 2, 2, 1>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+                                            dh_out, scale_log2, f, st);
     default:
-      return launch_flash<256, 32, 2, 1>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
-                                         dh_out, scale_log2, f, st);
+      return launch_flash<256, 32, 2, 1, 1>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+                                            dh_out, scale_log2, f, st);
   }
 }

@@ -91,6 +91,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes (or about `ns` nanoseconds pass) instead of re-polling. Many warps
+// re-polling barriers in a tight loop saturate the shared-memory barrier unit
+// and slow every other barrier operation of the SM.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking test of the same condition (for a thread that polls several
+// barriers and must not be suspended on one of them).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with the given parity has completed. Returns false
 // (and raises the CTA abort flag) when the wait times out or another role in
 // the CTA already aborted; callers then unwind without issuing more work.
@@ -99,7 +129,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    // Sleep on the barrier; wake at least every 20 us to look at the abort
+    // flag and the time limit.
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > KF_WAIT_CYCLES) {
       *abort_flag = 1;
