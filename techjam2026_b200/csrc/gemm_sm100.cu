@@ -127,8 +127,32 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uin
       : "memory");
 }
 
+// GELU(x) = x/2 (1 + erf(x / sqrt 2)), with erf from Abramowitz & Stegun,
+// Handbook of Mathematical Functions, formula 7.1.26: for z >= 0,
+//   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) e^(-z^2),
+//   t = 1 / (1 + p z),  |error| <= 1.5e-7,
+// so with q = poly(t) e^(-z^2) and z = |x| / sqrt 2:
+//   GELU(x) = x - x q / 2 for x >= 0,  x q / 2 for x < 0.
+// One reciprocal and one exp2 on the multi-function unit and six FMAs; the
+// GELU error stays below 1e-7 |x|, far under the bf16 hi/lo pair that
+// carries the result (2^-17 relative).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.f + erff(x * 0.70710678118654752440f));
+  constexpr float kP = 0.3275911f;
+  constexpr float kA1 = 0.254829592f, kA2 = -0.284496736f, kA3 = 1.421413741f;
+  constexpr float kA4 = -1.453152027f, kA5 = 1.061405429f;
+  constexpr float kInvSqrt2 = 0.70710678118654752440f;
+  constexpr float kNegLog2e = -1.44269504088896340736f;
+  const float z = fabsf(x) * kInvSqrt2;
+  const float t = rcp_approx(fmaf(kP, z, 1.f));
+  const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, kA5, kA4), kA3), kA2), kA1);
+  const float q = poly * fast_exp2(z * z * kNegLog2e);
+  const float h = 0.5f * x * q;
+  return x >= 0.f ? x - h : h;
 }
 
 template <int EPI>
@@ -461,31 +485,49 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
         tmem_ld32(tbase + static_cast<uint32_t>(c), v);
         if (tma_out && (flags & KF_GEMM_OUT_SPLIT)) {
           // bf16 hi/lo planes: two 128x32 bf16 tiles (64-byte rows, SW64).
+          // The arithmetic runs before the wait for the staging buffer, so
+          // it overlaps the previous chunk's TMA store.
+          uint4 hu[4], lu[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {  // 8 columns -> one 16-byte unit per plane
+            const int col = n0 + c + 8 * j;
+            float o[8];
+            if (bias && col + 8 <= N) {
+              const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + col));
+              const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + col + 4));
+              o[0] = v[8 * j] + b0.x, o[1] = v[8 * j + 1] + b0.y;
+              o[2] = v[8 * j + 2] + b0.z, o[3] = v[8 * j + 3] + b0.w;
+              o[4] = v[8 * j + 4] + b1.x, o[5] = v[8 * j + 5] + b1.y;
+              o[6] = v[8 * j + 6] + b1.z, o[7] = v[8 * j + 7] + b1.w;
+            } else {
+#pragma unroll
+              for (int t = 0; t < 8; ++t)
+                o[t] = v[8 * j + t] + ((bias && col + t < N) ? __ldg(bias + col + t) : 0.f);
+            }
+            if (EPI == KF_EPI_BIAS_GELU) {
+#pragma unroll
+              for (int t = 0; t < 8; ++t) o[t] = gelu_erf(o[t]);
+            }
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const __nv_bfloat162 hi = __floats2bfloat162_rn(o[2 * t], o[2 * t + 1]);
+              const float2 hf = __bfloat1622float2(hi);
+              const __nv_bfloat162 lo =
+                  __floats2bfloat162_rn(o[2 * t] - hf.x, o[2 * t + 1] - hf.y);
+              hw[t] = *reinterpret_cast<const uint32_t*>(&hi);
+              lw[t] = *reinterpret_cast<const uint32_t*>(&lo);
+            }
+            hu[j] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            lu[j] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          }
           if (leader) bulk_wait_group_read<0>();  // this half's last store has read `buf`
           named_bar_sync(bar_id, 128);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {  // 8 columns -> one 16-byte bf16 chunk
-            float o[8];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-              const int col = n0 + c + 8 * j + t;
-              float x = v[8 * j + t] + ((bias && col < N) ? __ldg(bias + col) : 0.f);
-              if (EPI == KF_EPI_BIAS_GELU) x = gelu_erf(x);
-              o[t] = x;
-            }
-            __nv_bfloat16 hi[8], lo[8];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-              hi[t] = __float2bfloat16_rn(o[t]);
-              lo[t] = __float2bfloat16_rn(o[t] - __bfloat162float(hi[t]));
-            }
+          for (int j = 0; j < 4; ++j) {
             const int off = r * 64 + ((j ^ ((r >> 1) & 3)) << 4);
-            *reinterpret_cast<uint4*>(buf + off) =
-                make_uint4(pack_bf16x2(hi[0], hi[1]), pack_bf16x2(hi[2], hi[3]),
-                           pack_bf16x2(hi[4], hi[5]), pack_bf16x2(hi[6], hi[7]));
-            *reinterpret_cast<uint4*>(buf + Cfg::EPI_BUF_BYTES / 2 + off) =
-                make_uint4(pack_bf16x2(lo[0], lo[1]), pack_bf16x2(lo[2], lo[3]),
-                           pack_bf16x2(lo[4], lo[5]), pack_bf16x2(lo[6], lo[7]));
+            *reinterpret_cast<uint4*>(buf + off) = hu[j];
+            *reinterpret_cast<uint4*>(buf + Cfg::EPI_BUF_BYTES / 2 + off) = lu[j];
           }
           fence_proxy_async_smem();
           named_bar_sync(bar_id, 128);
@@ -495,13 +537,18 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
             bulk_commit_group();
           }
         } else if (tma_out) {
-          if (leader) bulk_wait_group_read<0>();  // this half's last store has read `buf`
-          named_bar_sync(bar_id, 128);
+          float4 ov[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const int col = n0 + c + 4 * j;
             float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (bias && col < N) bb = __ldg(reinterpret_cast<const float4*>(bias + col));
+            if (bias && col + 4 <= N) {
+              bb = __ldg(reinterpret_cast<const float4*>(bias + col));
+            } else if (bias) {
+              float tb[4] = {0.f, 0.f, 0.f, 0.f};
+              for (int t = 0; t < 4 && col + t < N; ++t) tb[t] = __ldg(bias + col + t);
+              bb = make_float4(tb[0], tb[1], tb[2], tb[3]);
+            }
             float4 o = make_float4(v[4 * j] + bb.x, v[4 * j + 1] + bb.y, v[4 * j + 2] + bb.z,
                                    v[4 * j + 3] + bb.w);
             if (EPI == KF_EPI_BIAS_GELU) {
@@ -516,8 +563,14 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
               o.z = round_tf32(o.z);
               o.w = round_tf32(o.w);
             }
-            *reinterpret_cast<float4*>(buf + r * 128 + ((j ^ (r & 7)) << 4)) = o;
+            ov[j] = o;
           }
+          // Arithmetic done; now wait until this half's last store has read `buf`.
+          if (leader) bulk_wait_group_read<0>();
+          named_bar_sync(bar_id, 128);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(buf + r * 128 + ((j ^ (r & 7)) << 4)) = ov[j];
           fence_proxy_async_smem();  // generic smem writes -> TMA store reads
           named_bar_sync(bar_id, 128);
           if (leader) {

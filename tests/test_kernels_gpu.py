@@ -531,3 +531,41 @@ def test_flash_key_bits_beyond_shared_memory_staging(Dh, S):
     rows = list(range(0, 64)) + list(range(6000, 6100)) + list(range(S - 200, S))
     ref = _reference_rows(q, k, v, keep, True, rows)
     assert (o[:, :, rows].double() - ref).abs().max().item() < 5e-3
+
+
+@pytest.mark.parametrize("out_split", [False, True])
+def test_gemm_gelu_epilogue_error_bound(out_split):
+    """The GELU epilogue evaluates erf with Abramowitz & Stegun 7.1.26
+    (|error| <= 1.5e-7). Inputs exactly representable in bf16 and an identity
+    weight make the GEMM itself exact, so the output isolates the epilogue:
+    within 3e-7 * max(1, |x|) of float64 GELU (erf) for fp32 output, plus the
+    bf16 hi/lo pair's own rounding (2^-16 relative) for split output."""
+    from techjam2026_b200 import _lib
+    torch.manual_seed(14)
+    M, K = 4096, 16
+    x = (torch.rand(M, K, device="cuda") * 20 - 10).to(torch.bfloat16).float()
+    x[0, :8] = torch.tensor([0.0, -0.0, 1e-3, -1e-3, 5.0, -5.0, 9.5, -9.5])
+    w = torch.eye(K, device="cuda")
+    bias = torch.zeros(K, device="cuda")
+    a2, w2 = to_planes(x).contiguous(), to_planes(w).contiguous()
+    if out_split:
+        out = torch.zeros(2, M, K, dtype=torch.int16, device="cuda")
+        flags = _lib.KF_GEMM_OUT_BF16X2
+    else:
+        out = torch.zeros(M, K, device="cuda")
+        flags = 0
+    rc = _lib.lib().kf_gemm_bf16x3(a2.data_ptr(), K, w2.data_ptr(), K, bias.data_ptr(),
+                                   out.data_ptr(), K, M, K, K, _lib.KF_EPI_BIAS_GELU, flags, 0, 0,
+                                   0, None, None, _lib.stream_ptr())
+    _lib.check(rc, "kf_gemm_bf16x3")
+    torch.cuda.synchronize()
+    got = (from_planes(out) if out_split else out).double()
+    xd = x.double()
+    ref = 0.5 * xd * (1 + torch.erf(xd / math.sqrt(2)))
+    err = (got - ref).abs()
+    bound = 3e-7 * xd.abs().clamp(min=1)
+    if out_split:
+        bound = bound + 2.0 ** -16 * ref.abs()
+    assert bool((err <= bound).all()), f"max err {err.max().item()}"
+    # and against the fp32 erf GELU that torch computes on the GPU
+    assert (got - F.gelu(x).double()).abs().max().item() < 2e-5
