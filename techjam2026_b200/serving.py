@@ -1,0 +1,104 @@
+"""Streamed forward over a sequence of host batches (the serving loop).
+
+A serving process receives batches in host memory and returns results in
+host memory. Run one after another, every batch pays its host->device copy,
+the forward, and its device->host copy in turn. `StreamedForward` overlaps
+them: while the forward of batch k runs on the caller's stream, the upload
+of batch k+1 runs on one copy stream and the download of result k-1 on
+another. PCIe is full duplex and the GPU has several copy engines, so in
+steady state a batch costs the longest of the three, not their sum. Device
+buffers are double-buffered; every batch still crosses PCIe both ways.
+
+The forward itself is the model's CUDA graph (`FusedTransformer.graph_runner`),
+so results are bit-identical to calling the model on each batch.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence
+
+import torch
+
+from .fused import FusedTransformer
+
+
+class StreamedForward:
+    """Pipelined forward of one fixed batch shape.
+
+    `x_example` / `mask_example` are device tensors of that shape (their
+    values are not used). Host tensors passed to `run` should be pinned;
+    otherwise the copies are synchronous and nothing overlaps."""
+
+    def __init__(self, model: FusedTransformer, x_example: torch.Tensor,
+                 mask_example: Optional[torch.Tensor] = None):
+        if not x_example.is_cuda:
+            raise ValueError("x_example must be a CUDA tensor of the batch shape")
+        self.device = x_example.device
+        self.runner = model.graph_runner(x_example, mask_example)
+        self.with_mask = mask_example is not None
+        self.xd = [torch.empty_like(x_example) for _ in range(2)]
+        self.md = ([torch.empty_like(mask_example) for _ in range(2)]
+                   if self.with_mask else [None, None])
+        self.od = [torch.empty_like(x_example) for _ in range(2)]
+        self.up = torch.cuda.Stream(device=self.device)
+        self.down = torch.cuda.Stream(device=self.device)
+
+    def run(self, xs: Sequence[torch.Tensor], masks: Optional[Sequence[torch.Tensor]],
+            outs: Sequence[torch.Tensor], before_step=None) -> None:
+        """Forward xs[k] (with masks[k]) into outs[k] for every k.
+
+        Everything is queued asynchronously; the caller's current stream
+        waits for the last download, so outs are ready once that stream is
+        synchronized. `before_step(k)`, if given, is called on the caller's
+        stream just before forward k is queued (the benchmark flushes L2
+        there). Host tensors must stay alive until then."""
+        n = len(xs)
+        if n == 0:
+            return
+        if len(outs) != n or (self.with_mask and (masks is None or len(masks) != n)):
+            raise ValueError("xs, masks and outs must have the same length")
+        comp = torch.cuda.current_stream(self.device)
+        uploaded = [torch.cuda.Event() for _ in range(n)]
+        loaded = [torch.cuda.Event() for _ in range(n)]
+        computed = [torch.cuda.Event() for _ in range(n)]
+        downloaded = [torch.cuda.Event() for _ in range(n)]
+        self.up.wait_stream(comp)
+        self.down.wait_stream(comp)
+
+        def upload(k: int) -> None:
+            b = k % 2
+            with torch.cuda.stream(self.up):
+                if k >= 2:
+                    self.up.wait_event(loaded[k - 2])  # forward k-2 has read buffer b
+                self.xd[b].copy_(xs[k], non_blocking=True)
+                if self.with_mask:
+                    self.md[b].copy_(masks[k], non_blocking=True)
+                uploaded[k].record(self.up)
+
+        upload(0)
+        for k in range(n):
+            b = k % 2
+            if k + 1 < n:
+                upload(k + 1)
+            if before_step is not None:
+                before_step(k)
+            comp.wait_event(uploaded[k])
+            self.runner.load_inputs(self.xd[b], self.md[b])
+            loaded[k].record(comp)
+            self.runner.replay()
+            if k >= 2:
+                comp.wait_event(downloaded[k - 2])  # result k-2 has left buffer b
+            self.od[b].copy_(self.runner.static_out)
+            computed[k].record(comp)
+            with torch.cuda.stream(self.down):
+                self.down.wait_event(computed[k])
+                outs[k].copy_(self.od[b], non_blocking=True)
+                downloaded[k].record(self.down)
+        comp.wait_event(downloaded[n - 1])
+
+    def __call__(self, xs: List[torch.Tensor], masks: Optional[List[torch.Tensor]] = None
+                 ) -> List[torch.Tensor]:
+        """Convenience form: returns new pinned host outputs, synchronized."""
+        outs = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in xs]
+        self.run(xs, masks, outs)
+        torch.cuda.current_stream(self.device).synchronize()
+        return outs

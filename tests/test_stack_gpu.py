@@ -170,3 +170,25 @@ def test_native_library_is_the_one_loaded():
     maps = open(f"/proc/{os.getpid()}/maps", encoding="utf-8").read()
     assert build.LIB_PATH in maps
     assert _lib.lib().kf_device_status(0) == 0
+
+
+def test_streamed_forward_matches_per_batch_calls():
+    """The serving loop (uploads and downloads on their own streams, double
+    buffers) returns, batch for batch, exactly what calling the model on each
+    batch returns, including when consecutive batches differ."""
+    from techjam2026_b200.serving import StreamedForward
+    case = load_case("mini_s333")
+    cfg = case["cfg"]
+    m = _model(cfg, case["state_dict"])
+    xs, masks = [], []
+    for seed in range(5):
+        x, mask = generate_case(cfg, 100 + seed, 0.5)
+        xs.append(x.pin_memory())
+        masks.append(mask.pin_memory())
+    pipe = StreamedForward(m, xs[0].cuda(), masks[0].cuda())
+    outs = pipe(xs, masks)
+    again = pipe(xs[::-1], masks[::-1])
+    for k in range(5):
+        ref = m(xs[k].cuda(), masks[k].cuda()).cpu()
+        assert torch.equal(outs[k], ref), f"batch {k}"
+        assert torch.equal(again[4 - k], ref), f"reversed batch {k}"
