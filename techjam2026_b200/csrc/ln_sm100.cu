@@ -39,26 +39,62 @@ __global__ void __launch_bounds__(256) ln_add_mask_vec_kernel(
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= M) return;
   const int nv4 = d >> 2;
-  const bool kept = keep ? (keep[row] != 0) : true;
-  if (!kept && (flags & KF_LN_SKIP_PADDED)) return;
-
-  float4 v[NV];
-  float sum = 0.f;
+  // The kernel is latency-bound (one short row per warp), so every load it
+  // needs -- the row's keep byte, x, y and, for rows of up to 1024 floats,
+  // gamma and beta -- is issued up front instead of one dependent round trip
+  // after another; a padded row's loads are simply not used.
+  constexpr bool PREFETCH_WB = NV <= 8;
+  constexpr int NW = PREFETCH_WB ? NV : 1;
+  const bool kept = keep ? (__ldg(keep + row) != 0) : true;
+  // Long rows add y as it arrives (registers for two copies would spill).
+  constexpr int NT = PREFETCH_WB ? NV : 1;
+  float4 v[NV], t[NT], gw[NW], gb[NW];
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int c = lane + 32 * i;
     v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (c < nv4 && kept) {
-      float4 a = reinterpret_cast<const float4*>(x + row * ldx)[c];
+    if (PREFETCH_WB) t[i] = v[i];
+    if (c < nv4) {
+      v[i] = reinterpret_cast<const float4*>(x + row * ldx)[c];
       if (y) {
-        const float4 t = reinterpret_cast<const float4*>(y + row * ldy)[c];
-        a.x += t.x;
-        a.y += t.y;
-        a.z += t.z;
-        a.w += t.w;
+        const float4 yy = reinterpret_cast<const float4*>(y + row * ldy)[c];
+        if (PREFETCH_WB) {
+          t[i] = yy;
+        } else {
+          v[i].x += yy.x;
+          v[i].y += yy.y;
+          v[i].z += yy.z;
+          v[i].w += yy.w;
+        }
       }
-      v[i] = a;
-      sum += (a.x + a.y) + (a.z + a.w);
+    }
+  }
+  if (PREFETCH_WB) {
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+      const int c = lane + 32 * i;
+      gw[i] = gb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < nv4) {
+        gw[i] = __ldg(reinterpret_cast<const float4*>(w) + c);
+        gb[i] = __ldg(reinterpret_cast<const float4*>(b) + c);
+      }
+    }
+  }
+  if (!kept && (flags & KF_LN_SKIP_PADDED)) return;
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nv4 && kept) {
+      if (PREFETCH_WB) {
+        v[i].x += t[i < NT ? i : 0].x;
+        v[i].y += t[i < NT ? i : 0].y;
+        v[i].z += t[i < NT ? i : 0].z;
+        v[i].w += t[i < NT ? i : 0].w;
+      }
+      sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    } else {
+      v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
   const float inv_d = 1.f / static_cast<float>(d);
@@ -88,8 +124,8 @@ __global__ void __launch_bounds__(256) ln_add_mask_vec_kernel(
       if (zero_h) {
         h = make_float4(0.f, 0.f, 0.f, 0.f);
       } else {
-        const float4 ww = __ldg(reinterpret_cast<const float4*>(w) + c);
-        const float4 bb = __ldg(reinterpret_cast<const float4*>(b) + c);
+        const float4 ww = PREFETCH_WB ? gw[i < NW ? i : 0] : __ldg(reinterpret_cast<const float4*>(w) + c);
+        const float4 bb = PREFETCH_WB ? gb[i < NW ? i : 0] : __ldg(reinterpret_cast<const float4*>(b) + c);
         h.x = (v[i].x - mean) * rstd * ww.x + bb.x;
         h.y = (v[i].y - mean) * rstd * ww.y + bb.y;
         h.z = (v[i].z - mean) * rstd * ww.z + bb.z;
