@@ -116,6 +116,20 @@ class _Workspace:
                    for t in (self.res, self.h, self.h2, self.qkv, self.ctx, self.y, self.ffn,
                              self.bits, self.live_tiles, self.live_count) if t is not None)
 
+    @staticmethod
+    def estimate(cfg, B: int, S: int, plan: Plan) -> int:
+        """Bytes __init__ would allocate for (B, S), without allocating."""
+        d, F, H = cfg.d_model, cfg.ffn_dim, cfg.num_heads
+        dh_store = max(16, d // H)
+        M = B * S
+        split = {g: p == "bf16x3" for g, p in plan.gemm_precisions().items()}
+        per_row = 4 * d                                        # res
+        per_row += 0 if (split["qkv"] and split["ffn1"]) else 4 * d   # h
+        per_row += 4 * d if (split["qkv"] or split["ffn1"]) else 0    # h2 planes
+        per_row += 4 * 3 * H * dh_store + 4 * d + 4 * d + 4 * F       # qkv, ctx, y, ffn
+        words = (S + 31) // 32
+        return M * per_row + 4 * B * words + 4 * ((M + 127) // 128) + 4
+
 
 class FusedTransformer(LayerStack):
     """Drop-in for BaselineTransformer (identical state_dict keys).
@@ -124,9 +138,16 @@ class FusedTransformer(LayerStack):
     sm_100 GPU and valid_token_mask bool [B, S] (True = real token).
     """
 
-    def __init__(self, config, plan: Optional[Plan] = None):
+    def __init__(self, config, plan: Optional[Plan] = None,
+                 memory_budget_bytes: Optional[int] = None):
         super().__init__(config)
         self.plan = plan or DEFAULT_PLAN
+        # Device bytes one forward may use for its workspace and its input /
+        # output staging; a batch that needs more runs in slices of whole
+        # sequences (no op mixes batch elements, so slicing is exact).
+        # None = 90% of the device memory free at the first call of a shape.
+        self.memory_budget_bytes = memory_budget_bytes
+        self._slice_rows: Dict[Tuple, int] = {}
         self._weights: Optional[_Weights] = None
         self._weights_key = None
         self._workspaces: Dict[Tuple, _Workspace] = {}
@@ -165,6 +186,7 @@ class FusedTransformer(LayerStack):
     def release_buffers(self) -> None:
         self._graphs.clear()
         self._workspaces.clear()
+        self._slice_rows.clear()
 
     # ------------------------------------------------------------ the forward
 
@@ -302,12 +324,49 @@ class FusedTransformer(LayerStack):
         self.launch(x, self._keep_u8(valid_token_mask), out, ws, w)
         return out
 
-    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None
-                ) -> torch.Tensor:
+    def bytes_per_sequence(self, S: int) -> int:
+        """Device bytes one sequence of length S costs a forward: its share of
+        the workspace plus the graph's static input and output and the
+        returned copy (3 x S x d fp32)."""
+        return (_Workspace.estimate(self.config, 1, S, self.plan)
+                + 3 * 4 * S * self.config.d_model)
+
+    def slice_rows(self, B: int, S: int, device: torch.device) -> int:
+        """Sequences per slice for a [B, S] batch under the memory budget
+        (decided once per shape and device)."""
+        key = (B, S, str(device))
+        rows = self._slice_rows.get(key)
+        if rows is None:
+            budget = self.memory_budget_bytes
+            if budget is None:
+                free, _ = torch.cuda.mem_get_info(device)
+                budget = int(0.9 * free) + sum(
+                    w.nbytes() for k, w in self._workspaces.items() if k[2] == str(device))
+            rows = max(1, min(B, budget // max(1, self.bytes_per_sequence(S))))
+            self._slice_rows[key] = rows
+        return rows
+
+    def _forward_whole(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]
+                       ) -> torch.Tensor:
         if self.plan.cuda_graph and not torch.cuda.is_current_stream_capturing():
-            self._check_inputs(x, valid_token_mask)
             return self.graph_runner(x, valid_token_mask)(x, valid_token_mask)
         return self.eager_forward(x, valid_token_mask)
+
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None
+                ) -> torch.Tensor:
+        self._check_inputs(x, valid_token_mask)
+        B, S, _ = x.shape
+        rows = self.slice_rows(B, S, x.device) if B > 1 else 1
+        if rows >= B:
+            return self._forward_whole(x, valid_token_mask)
+        # Batch streaming: whole sequences per slice, results written into
+        # one output (at most two captured graphs: full slices and the rest).
+        out = torch.empty_like(x)
+        for b0 in range(0, B, rows):
+            b1 = min(B, b0 + rows)
+            m = None if valid_token_mask is None else valid_token_mask[b0:b1]
+            out[b0:b1].copy_(self._forward_whole(x[b0:b1], m))
+        return out
 
     def graph_runner(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]
                      ) -> "GraphRunner":

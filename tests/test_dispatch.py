@@ -51,3 +51,34 @@ def test_table_round_trips(tmp_path, monkeypatch):
     t.save("sm_100")
     back = DispatchTable.load("sm_100")
     assert back.lookup("sm_100", torch.float32, cfg)[0] == Plan(name="x", bn_out=128)
+
+
+def test_workspace_estimate_matches_allocation():
+    """The batch-streaming budget uses _Workspace.estimate; it must equal what
+    the workspace really allocates, for every precision mix."""
+    import dataclasses
+    from techjam2026_b200.configs import WORKLOADS
+    from techjam2026_b200.fused import _Workspace
+    from techjam2026_b200.dispatch import DEFAULT_PLAN
+    plans = [DEFAULT_PLAN,
+             dataclasses.replace(DEFAULT_PLAN, prec_qkv="tf32", prec_out="3xtf32",
+                                 prec_ffn1="tf32", prec_ffn2="bf16x3")]
+    for name in ("c1", "c3a", "c2"):
+        cfg = WORKLOADS[name].cfg
+        for plan in plans:
+            B, S = 2, min(cfg.seq_len, 96)
+            ws = _Workspace(cfg, B, S, torch.device("cpu"), plan)
+            assert _Workspace.estimate(cfg, B, S, plan) == ws.nbytes(), (name, plan.prec_qkv)
+
+
+def test_batch_streaming_slice_rows_follow_the_budget():
+    from techjam2026_b200.configs import WORKLOADS
+    from techjam2026_b200.fused import FusedTransformer
+    cfg = WORKLOADS["c2"].cfg
+    m = FusedTransformer(cfg)
+    per = m.bytes_per_sequence(cfg.seq_len)
+    cpu = torch.device("cpu")
+    for budget, rows in ((per * 3 + per // 2, 3), (per // 2, 1), (per * 100, 8)):
+        m.memory_budget_bytes = budget
+        m._slice_rows.clear()
+        assert m.slice_rows(8, cfg.seq_len, cpu) == rows

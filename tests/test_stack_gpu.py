@@ -192,3 +192,24 @@ def test_streamed_forward_matches_per_batch_calls():
         ref = m(xs[k].cuda(), masks[k].cuda()).cpu()
         assert torch.equal(outs[k], ref), f"batch {k}"
         assert torch.equal(again[4 - k], ref), f"reversed batch {k}"
+
+
+def test_batch_streaming_under_a_memory_budget_is_exact():
+    """With a budget of three sequences the c2 batch runs in slices of 3, 3
+    and 2 sequences (two captured graphs) and reproduces the whole-batch
+    forward bit for bit (no op mixes batch elements)."""
+    w = WORKLOADS["c2"]
+    cfg = w.cfg
+    sd = make_state_dict(cfg, 0)
+    x, mask = generate_case(cfg, 0, w.padding_ratio)
+    x, mask = x.cuda(), mask.cuda()
+    whole = _model(cfg, sd)(x, mask)
+    m = FusedTransformer(cfg, memory_budget_bytes=None)
+    m.load_state_dict(sd, strict=True)
+    m = m.cuda().eval()
+    m.memory_budget_bytes = 3 * m.bytes_per_sequence(cfg.seq_len) + 1
+    sliced = m(x, mask)
+    torch.cuda.synchronize()
+    assert m.slice_rows(cfg.batch_size, cfg.seq_len, x.device) == 3
+    assert len(m._graphs) == 2
+    assert torch.equal(sliced, whole)
