@@ -63,7 +63,62 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--batch-size", type=int, default=None,
                    help="rows per rank (default: the workload's batch); for bounded profiling")
+    p.add_argument("--protocol", default="contract", choices=("contract", "organiser"),
+                   help="organiser: time the public module the way the organiser's harness "
+                        "does (fixed device input, per-call events, 3 rounds x 100, median)")
+    p.add_argument("--seed", type=int, default=1234, help="organiser protocol seed")
     return p.parse_args()
+
+
+def run_organiser_protocol(args, rank, world):
+    """The organiser harness's timing, restated (torch_transformer_benchmark.py
+    :477-583, defaults :617-624): the input is drawn once with seed+100000,
+    the module is called `warmup` (20) times, then `rounds` (3) batches of
+    `repeats` (100) calls, each call bracketed by CUDA events on the current
+    stream with no cache flush and no synchronisation in between; the result
+    is the median call latency. The module is the public drop-in
+    (`submission.UserOptimizedTransformer`). Its accuracy trials (seeds
+    seed..seed+4 against the fp32 reference layer) are the GPU test
+    `test_organiser_accuracy_trials`. Each rank times its own GPU."""
+    import submission
+    torch.cuda.set_device(rank if world > 1 else 0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    w = WORKLOADS[args.config]
+    cfg = w.cfg
+    api = submission.UserOptimizedTransformer(cfg)
+    api.load_state_dict(make_state_dict(cfg, 0), strict=True)
+    api = api.to(dev).eval()
+    x_cpu, mask_cpu = generate_case(cfg, args.seed + 100000, w.padding_ratio, w.input_scale)
+    x, mask = x_cpu.to(dev), mask_cpu.to(dev)
+    warmup, repeats, rounds = 20, 100, 3
+    samples = []
+    with torch.inference_mode():
+        for _ in range(warmup):
+            api(x, mask)
+        torch.cuda.synchronize(dev)
+        for _ in range(rounds):
+            starts = [torch.cuda.Event(enable_timing=True) for _ in range(repeats)]
+            ends = [torch.cuda.Event(enable_timing=True) for _ in range(repeats)]
+            torch.cuda.synchronize(dev)
+            for i in range(repeats):
+                starts[i].record()
+                api(x, mask)
+                ends[i].record()
+            torch.cuda.synchronize(dev)
+            samples.extend(a.elapsed_time(b) for a, b in zip(starts, ends))
+    assert api._impl is not None, "public API fell back: nothing of ours was timed"
+    med = statistics.median(samples)
+    flops = useful_flops(cfg, lengths_of(mask_cpu, cfg.batch_size, cfg.seq_len))
+    line = {"metric": METRIC, "protocol": "organiser", "value": round(flops / (med / 1e3) / 1e12, 3),
+            "unit": "TFLOP/s", "median_ms": round(med, 4),
+            "min_ms": round(min(samples), 4), "samples": len(samples),
+            "tokens_per_s": round(cfg.batch_size * cfg.seq_len * 1000.0 / med, 1),
+            "n_gpus": world, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.config, "signature": sig(cfg), "seed": args.seed + 100000,
+                       "warmup": warmup, "repeats": repeats, "rounds": rounds}}
+    if rank == 0:
+        print(json.dumps(line))
+    return 0
 
 
 def dist_env():
@@ -302,6 +357,8 @@ def main():
         args.gpus = world if world > 1 else args.gpus
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.protocol == "organiser":
+        return run_organiser_protocol(args, rank, world)
 
     import torch.distributed as dist
     from techjam2026_b200 import _lib

@@ -213,3 +213,24 @@ def test_batch_streaming_under_a_memory_budget_is_exact():
     assert m.slice_rows(cfg.batch_size, cfg.seq_len, x.device) == 3
     assert len(m._graphs) == 2
     assert torch.equal(sliced, whole)
+
+
+def test_organiser_accuracy_trials():
+    """The organiser harness's accuracy gate on c2: five trials with seeds
+    1234..1238 (its default seed), each drawn by generate_random_case and
+    compared elementwise with the fp32 reference layer, through the public
+    drop-in module."""
+    import submission
+    w = WORKLOADS["c2"]
+    cfg = w.cfg
+    sd = make_state_dict(cfg, 0)
+    ours = submission.UserOptimizedTransformer(cfg)
+    ours.load_state_dict(sd, strict=True)
+    ours = ours.cuda().eval()
+    for trial in range(5):
+        x, mask = generate_case(cfg, 1234 + trial, w.padding_ratio, w.input_scale)
+        with torch.inference_mode():
+            out = ours(x.cuda(), mask.cuda())
+        assert ours._impl is not None and not ours._failed
+        ref = _oracle(cfg, sd, x, mask, query_chunk=256)
+        _assert_gate(ref, out, f"organiser trial {trial + 1}/5 (seed {1234 + trial})")
