@@ -116,7 +116,8 @@ int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t ldw, const
  * planes [2][M][ldc] in the same split format (to feed another
  * kf_gemm_bf16x3). Needs K, lda, ldw % 8 == 0 and 16-byte aligned pointers.
  * head_dim/head_stride (fp32 output only) and live_tiles/live_count as
- * kf_gemm_tf32. Replaces the same F.linear calls
+ * kf_gemm_tf32; `bn` as kf_gemm_tf32 plus 96 (fewer partial waves when
+ * N / 128 tiles leave the last wave nearly empty). Replaces the same F.linear calls
  * as kf_gemm_tf32, at fp32-class accuracy. */
 int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t ldw,
                    const float* bias, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K,

@@ -61,14 +61,15 @@ struct GemmCfg {
   static constexpr int EPI_WARPS = 8;       // two per TMEM lane quarter
   static constexpr int CONV_WARP0 = 2 + EPI_WARPS;
   static constexpr int THREADS = 32 * CONV_WARP0 + (CONVERTS ? CONV_THREADS : 0);
-  static constexpr int TMEM_COLS = 2 * BN;
+  // Two accumulators of BN columns, allocated as a power of two.
+  static constexpr int TMEM_COLS = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
   static constexpr int EPI_BUF_BYTES = BM * 32 * 4;  // one 128x32 fp32 output chunk
   // Two buffers: one per epilogue half (each half stages its own chunks).
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = EPI_OFF + 2 * EPI_BUF_BYTES;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = BAR_OFF + BAR_BYTES + 1024;
-  static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(BN == 64 || BN == 96 || BN == 128 || BN == 256, "BN");
   static_assert(STAGES >= 2 && STAGES <= 8, "stages");
   static_assert(SMEM_BYTES <= 232448, "smem");
 };
@@ -809,8 +810,8 @@ extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W
     return KF_E_INVALID;
   }
   if (bn == 0) bn = choose_bn(M, N);
-  if (bn != 64 && bn != 128 && bn != 256) {
-    set_last_error("kf_gemm_bf16x3: bn must be 0, 64, 128 or 256");
+  if (bn != 64 && bn != 96 && bn != 128 && bn != 256) {
+    set_last_error("kf_gemm_bf16x3: bn must be 0, 64, 96, 128 or 256");
     return KF_E_INVALID;
   }
   CUtensorMap ta, tb, tcm;
@@ -868,6 +869,7 @@ extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W
                                                  live_count, st);                              \
   }
   KF_GEMM_PRE_CASE(64)
+  KF_GEMM_PRE_CASE(96)
   KF_GEMM_PRE_CASE(128)
   KF_GEMM_PRE_CASE(256)
 #undef KF_GEMM_PRE_CASE

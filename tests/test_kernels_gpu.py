@@ -355,7 +355,7 @@ def from_planes(p: torch.Tensor) -> torch.Tensor:
 
 @pytest.mark.parametrize("M,N,K", [(128, 64, 64), (517, 384, 512), (4096, 2048, 512),
                                    (300, 200, 136), (2048, 512, 2048)])
-@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("bn", [64, 96, 128, 256])
 @pytest.mark.parametrize("gelu", [False, True])
 @pytest.mark.parametrize("out_split", [False, True])
 def test_gemm_bf16x3_presplit(M, N, K, bn, gelu, out_split):
