@@ -1,0 +1,155 @@
+"""Populate the sm_100 dispatch table by measurement (gate, then time).
+
+    python -m techjam2026_b200.tune --config c4 [--write]
+
+For one BASELINE configuration, on the current GPU:
+
+1. Build the forward with the table's current plan for that shape and keep
+   its output on a seeded input as the reference.
+2. For each GEMM of the layer (qkv, out, ffn1, ffn2) and each N tile the
+   kernels offer, build the forward with only that tile changed. The gate:
+   its output must be bit-identical to the reference (an N tile only decides
+   which CTA computes an output element, never the order of its
+   accumulation), so a candidate that changes any bit is rejected as a bug.
+3. Time every surviving candidate as a CUDA-graph replay (median of
+   `--repeats`, L2 flushed before each), keep the fastest tile per GEMM, and
+   confirm the combined plan against the reference and the current plan.
+4. With --write, store the combined plan as the exact entry for the shape
+   when it is faster than the current one.
+
+This is the sm_100 counterpart of the reference's plan search and
+`verify --demote` (kernelforge/search.py:131-351, cli.py:149-260), limited
+to the choices that cannot change numerics.
+"""
+from __future__ import annotations
+
+import argparse
+import dataclasses
+import gc
+import json
+import statistics
+import sys
+from typing import Dict, List, Tuple
+
+import torch
+
+from .configs import WORKLOADS, generate_case, make_state_dict, signature
+from .dispatch import DispatchTable, Entry, Plan, probe
+from .fused import FusedTransformer
+
+GEMMS = ("qkv", "out", "ffn1", "ffn2")
+TILES = {"bf16x3": (64, 96, 128, 256), "3xtf32": (64, 128, 256), "tf32": (64, 128, 256)}
+
+
+def _forward(cfg, sd, plan: Plan, x, mask) -> Tuple[FusedTransformer, torch.Tensor]:
+    m = FusedTransformer(cfg, plan)
+    m.load_state_dict(sd, strict=True)
+    m = m.to(x.device).eval()
+    runner = m.graph_runner(x, mask)
+    runner.load_inputs(x, mask)
+    runner.replay()
+    torch.cuda.synchronize()
+    return m, runner.static_out.clone()
+
+
+def _time(model: FusedTransformer, x, mask, repeats: int, flush: torch.Tensor) -> float:
+    runner = model.graph_runner(x, mask)
+    runner.load_inputs(x, mask)
+    for _ in range(3):
+        runner.replay()
+    times = []
+    for _ in range(repeats):
+        flush.zero_()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        runner.replay()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    return statistics.median(times)
+
+
+def tune(name: str, repeats: int = 10, seed: int = 0, log=print) -> Dict:
+    w = WORKLOADS[name]
+    cfg = w.cfg
+    spec = probe()
+    table = DispatchTable.load_for(spec)
+    base, source = table.lookup(spec.arch, torch.float32, cfg)
+    sd = make_state_dict(cfg, seed)
+    x_cpu, m_cpu = generate_case(cfg, seed, w.padding_ratio, w.input_scale)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    x, mask = x_cpu.to(dev), m_cpu.to(dev)
+    flush = torch.empty(64 * 1024 * 1024, device=dev)
+
+    model, ref = _forward(cfg, sd, base, x, mask)
+    t_base = _time(model, x, mask, repeats, flush)
+    model.release_buffers()
+    del model
+    gc.collect()
+    torch.cuda.empty_cache()
+    log(f"{name} {signature(cfg)}: current plan ({source}) {base.describe()}: {t_base:.3f} ms")
+    best = {}
+    results: List[dict] = []
+    for g in GEMMS:
+        field = f"bn_{g}"
+        prec = getattr(base, f"prec_{g}")
+        timed = []
+        for bn in TILES[prec]:
+            cand = dataclasses.replace(base, **{field: bn})
+            model, out = _forward(cfg, sd, cand, x, mask)
+            exact = torch.equal(out, ref)
+            t = _time(model, x, mask, repeats, flush) if exact else float("inf")
+            model.release_buffers()  # the captured graph holds its memory pool
+            del model, out
+            gc.collect()
+            torch.cuda.empty_cache()
+            results.append({"gemm": g, "bn": bn, "ms": t, "bit_exact": exact})
+            log(f"  {g:5s} bn={bn:3d}: {'%.3f ms' % t if exact else 'REJECTED (output differs)'}")
+            if exact:
+                timed.append((t, bn))
+        best[field] = min(timed)[1] if timed else getattr(base, field)
+    tuned = dataclasses.replace(base, **best)
+    model, out = _forward(cfg, sd, tuned, x, mask)
+    exact = torch.equal(out, ref)
+    t_tuned = _time(model, x, mask, repeats, flush) if exact else float("inf")
+    log(f"  combined {tuned.describe()}: {t_tuned:.3f} ms, bit-exact {exact}")
+    return {"config": name, "signature": signature(cfg), "base_ms": t_base,
+            "tuned_ms": t_tuned, "bit_exact": exact, "plan": tuned, "base": base,
+            "candidates": results}
+
+
+def write_entry(result: Dict, arch: str = "sm_100") -> str:
+    table = DispatchTable.load(arch)
+    sig = result["signature"]
+    tuned: Plan = result["plan"]
+    note = (f"tiles tuned by measurement: {result['tuned_ms']:.3f} ms "
+            f"(was {result['base_ms']:.3f} ms); all candidates bit-exact")
+    for e in table.entries:
+        if e.signature == sig and e.dtype == "float32":
+            keep = e.note.split(";")[0]
+            e.plan = dataclasses.replace(tuned, name=e.plan.name)
+            e.note = f"{keep}; {note}"
+            break
+    else:
+        table.entries.append(Entry(sig, "float32", "sm_100", tuned, note))
+    return table.save(arch)
+
+
+def main(argv=None) -> int:
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--config", action="append", choices=sorted(WORKLOADS), required=True)
+    p.add_argument("--repeats", type=int, default=10)
+    p.add_argument("--write", action="store_true", help="store faster plans in the table")
+    args = p.parse_args(argv)
+    for name in args.config:
+        r = tune(name, args.repeats)
+        if args.write and r["bit_exact"] and r["tuned_ms"] < r["base_ms"]:
+            print(f"  written to {write_entry(r)}")
+        print(json.dumps({k: (dataclasses.asdict(v) if isinstance(v, Plan) else v)
+                          for k, v in r.items() if k != "candidates"}))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

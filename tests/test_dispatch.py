@@ -82,3 +82,28 @@ def test_batch_streaming_slice_rows_follow_the_budget():
         m.memory_budget_bytes = budget
         m._slice_rows.clear()
         assert m.slice_rows(8, cfg.seq_len, cpu) == rows
+
+
+def test_tune_write_entry_updates_exact_signature(tmp_path, monkeypatch):
+    """tune.write_entry replaces the exact entry's tiles (keeping its name and
+    the first part of its note) or appends a new entry; lookup then returns
+    it as "exact"."""
+    import dataclasses
+    import shutil
+    from techjam2026_b200 import dispatch, tune
+    from techjam2026_b200.configs import WORKLOADS, signature
+    shutil.copy(dispatch.DispatchTable.path_for("sm_100"), tmp_path / "dispatch_sm_100.json")
+    monkeypatch.setattr(dispatch, "TABLE_DIR", str(tmp_path))
+    cfg = WORKLOADS["c4"].cfg
+    base, _ = dispatch.DispatchTable.load().lookup("sm_100", torch.float32, cfg)
+    tuned = dataclasses.replace(base, bn_ffn1=96, bn_ffn2=64)
+    tune.write_entry({"signature": signature(cfg), "plan": tuned, "tuned_ms": 1.0,
+                      "base_ms": 2.0})
+    plan, src = dispatch.DispatchTable.load().lookup("sm_100", torch.float32, cfg)
+    assert src == "exact" and plan.bn_ffn1 == 96 and plan.bn_ffn2 == 64
+    assert plan.name == base.name
+    odd = dataclasses.replace(cfg, batch_size=3)
+    tune.write_entry({"signature": signature(odd), "plan": tuned, "tuned_ms": 1.0,
+                      "base_ms": 2.0})
+    plan, src = dispatch.DispatchTable.load().lookup("sm_100", torch.float32, odd)
+    assert src == "exact" and plan.bn_ffn2 == 64
