@@ -124,6 +124,26 @@ int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t 
                    int epilogue, int flags, int bn, int head_dim, int head_stride,
                    const int32_t* live_tiles, const int32_t* live_count, void* stream);
 
+/* kf_gemm_bf16x3 (bias epilogue) followed by kf_ln_add_mask in one kernel:
+ * y = A.W^T + bias stays on chip; s = keep ? res + y : 0 is written to s_out
+ * (may equal res, or be null) and h = LayerNorm(s) * gamma + beta to h_out,
+ * with kf_ln_add_mask's ln_flags (KF_LN_*: mask_out, TF32 rounding, skipping
+ * padded rows, bf16 hi/lo planes [2][M][ldh]). s is bit-identical to the
+ * two-kernel sequence; h differs only by the order of the row reductions.
+ * N (= the LayerNorm width) must be a multiple of 128 and at most 1024: a
+ * cluster of N/128 CTAs computes the N/128 column tiles of a row tile and
+ * exchanges the row sums through distributed shared memory. Needs the
+ * alignments of kf_gemm_bf16x3 and 16-byte aligned res, s_out, gamma, beta,
+ * h_out. Replaces the out_proj / FFN2 F.linear plus the next
+ * add_mask_layernorm (kernelforge/optimized.py:573-574, 441-446 with
+ * :460-476; kernelforge/ops/layernorm.py:101-156). */
+int kf_gemm_bf16x3_add_ln(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t ldw,
+                          const float* bias, const float* res, int64_t ldr, const uint8_t* keep,
+                          const float* gamma, const float* beta, float eps, float* s_out,
+                          int64_t lds, void* h_out, int64_t ldh, int64_t M, int64_t N, int64_t K,
+                          int ln_flags, const int32_t* live_tiles, const int32_t* live_count,
+                          void* stream);
+
 /* ----------------------------------------------------------- attention */
 
 /* Words of the packed key-validity workspace for a [B, S] keep mask. */

@@ -33,6 +33,10 @@ SIGNATURES = {
     "kf_gemm_bf16x3": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
                                 _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int,
                                 _c_ptr, _c_ptr, _c_ptr]),
+    "kf_gemm_bf16x3_add_ln": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
+                                       _c_ptr, _c_ptr, _c_ptr, _c_float, _c_ptr, _c_i64,
+                                       _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
+                                       _c_ptr, _c_ptr, _c_ptr]),
     "kf_split_bf16x2": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_i64, _c_ptr]),
     "kf_keep_bits_words": (ctypes.c_size_t, [_c_i64, _c_i64]),
     "kf_keep_bits": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr]),

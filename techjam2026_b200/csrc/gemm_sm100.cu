@@ -200,12 +200,31 @@ __device__ __forceinline__ void gemm_store_chunk(const float (&v)[32], float* __
   }
 }
 
-template <int BN, int EPI, int SPLIT>
+// Arguments of the residual-add + mask + LayerNorm epilogue (LNF kernels):
+// the GEMM output y never reaches memory; s = keep ? res + y : 0 and
+// h = LayerNorm(s) (gamma, beta, eps) are written as kf_ln_add_mask writes
+// them (flags KF_LN_*).
+struct LnArgs {
+  const float* res;
+  int64_t ldr;
+  const uint8_t* keep;
+  const float* gamma;
+  const float* beta;
+  float* s_out;
+  int64_t lds;
+  void* h_out;
+  int64_t ldh;
+  float eps;
+  int flags;
+};
+
+template <int BN, int EPI, int SPLIT, bool LNF = false>
 __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int M,
                      int N, int K, int flags, int head_dim, int head_stride,
-                     const int32_t* __restrict__ live_tiles, const int32_t* __restrict__ live_count) {
+                     const int32_t* __restrict__ live_tiles, const int32_t* __restrict__ live_count,
+                     const __grid_constant__ LnArgs ln) {
   using Cfg = GemmCfg<BN, SPLIT>;
   constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -217,9 +236,14 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   uint64_t* acc_full = conv + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  // LNF: cluster exchanges of row statistics, [sum | centred sum of squares]
+  // x [tile parity]; other kernels keep the old barrier layout.
+  uint64_t* xbar = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(LNF ? xbar + 4 : drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* epi_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [2], per half
+  static_assert(!LNF || (3 * STAGES + 9) * 8 + 16 <= Cfg::BAR_BYTES, "LN barriers");
+  static_assert(!LNF || (BN == 128 && SPLIT == 3 && EPI == KF_EPI_BIAS), "LN epilogue shape");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -237,6 +261,8 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
       mbar_init(&acc_empty[a], Cfg::EPI_WARPS);
     }
     mbar_init(drain, 1);
+    if (LNF)
+      for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 128 * num_n);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -251,6 +277,12 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // LNF: every CTA of the cluster has initialised its exchange barriers
+  // before any CTA arrives on them remotely (warp-aligned: reconverge first).
+  if (LNF) {
+    __syncwarp();
+    cluster_sync_all();
+  }
 
   // The next kernel is released only once every CTA of this one holds its
   // TMEM (a CTA of the next kernel may allocate before its own wait, and must
@@ -448,6 +480,171 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
         }
       }
     }
+  } else if constexpr (LNF) {
+    // ------------------------------ epilogue: residual add + mask + LayerNorm
+    // The cluster's num_n CTAs hold the num_n 128-column tiles of the same
+    // 128 rows. Thread r of each half owns row r of its tile: pass 1 forms
+    // s = keep ? res + (acc + bias) : 0 (y rounded exactly as the GEMM would
+    // store it), writes s back over the accumulator and sums its 64 columns;
+    // the two halves and then the cluster's CTAs (through distributed shared
+    // memory) complete the row sum; pass 2 the centred sum of squares; pass 3
+    // writes s and h. Summation order is fixed, so results are deterministic.
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;
+    const bool leader = threadIdx.x == 64;
+    const int csize = num_n;
+    const uint32_t rank = static_cast<uint32_t>(blockIdx.x % csize);
+    float* xs = reinterpret_cast<float*>(smem + Cfg::EPI_OFF);  // [2 kinds][2 parities][8][128]
+    float* red = xs + 2 * 2 * 8 * 128;                          // [2 halves][128]
+    const float inv_n = 1.f / static_cast<float>(N);
+    const bool split_h = (ln.flags & KF_LN_OUT_BF16X2) != 0;
+    const bool rnd_h = (ln.flags & KF_LN_ROUND_TF32) != 0;
+    const bool skip_padded = (ln.flags & KF_LN_SKIP_PADDED) != 0;
+    const bool mask_out = (ln.flags & KF_LN_MASK_OUT) != 0;
+    // One bounded wait by the leader, shared through named barrier 1 (all 256
+    // epilogue threads), so every thread takes the same exits.
+    auto shared_wait = [&](uint64_t* bar, uint32_t parity, bool cluster_scope) -> bool {
+      if (leader)
+        epi_ok[0] = (cluster_scope ? mbar_wait_cluster(bar, parity, abort_flag, KF_DEV_WAIT_TIMEOUT_EPI)
+                                   : mbar_wait(bar, parity, abort_flag, KF_DEV_WAIT_TIMEOUT_EPI))
+                        ? 1 : 0;
+      named_bar_sync(1, 256);
+      const bool ok = epi_ok[0] != 0;
+      // completed phase: this re-test returns at once and acquires for this thread
+      if (ok && cluster_scope) mbar_try_wait_cluster(bar, parity, 0u);
+      return ok;
+    };
+    // Exchange one value per row with every CTA of the cluster; returns the
+    // sum over the cluster's CTAs in rank order.
+    auto exchange = [&](int kind, int tc, float part, bool& ok) -> float {
+      const int buf = tc & 1;
+      float* x = xs + (kind * 2 + buf) * 8 * 128;
+      uint64_t* bar = &xbar[kind * 2 + buf];
+      if (half == 0) {
+        const uint32_t slot = smem_u32(x + rank * 128 + r);
+        const uint32_t b = smem_u32(bar);
+        for (int q = 0; q < csize; ++q) {
+          st_cluster_f32(mapa_shared(slot, static_cast<uint32_t>(q)), part);
+          mbar_arrive_cluster(mapa_shared(b, static_cast<uint32_t>(q)));
+        }
+      }
+      ok = shared_wait(bar, static_cast<uint32_t>((tc >> 1) & 1), true);
+      float tot = 0.f;
+      if (ok)
+        for (int q = 0; q < csize; ++q) tot += x[q * 128 + r];
+      return tot;
+    };
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int tc = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tc) {
+      const int m0 = row0(tile);
+      const int n0 = (tile % num_n) * BN;
+      if (!shared_wait(&acc_full[acc], acc_phase, false)) break;
+      tc_fence_after();
+      const int row = m0 + r;
+      const bool in_range = row < M;
+      const bool kept = in_range && (ln.keep ? (__ldg(ln.keep + row) != 0) : true);
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      // pass 1
+      float part = 0.f;
+#pragma unroll 1
+      for (int c = 32 * half; c < BN; c += 64) {
+        float v[32];
+        tmem_ld32(tbase + static_cast<uint32_t>(c), v);
+        const float* xrow = ln.res + static_cast<int64_t>(row) * ln.ldr + n0 + c;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (bias) bb = __ldg(reinterpret_cast<const float4*>(bias + n0 + c) + j);
+          float4 xx = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (kept) xx = *reinterpret_cast<const float4*>(xrow + 4 * j);
+          const float y0 = v[4 * j] + bb.x, y1 = v[4 * j + 1] + bb.y;
+          const float y2 = v[4 * j + 2] + bb.z, y3 = v[4 * j + 3] + bb.w;
+          v[4 * j] = kept ? xx.x + y0 : 0.f;
+          v[4 * j + 1] = kept ? xx.y + y1 : 0.f;
+          v[4 * j + 2] = kept ? xx.z + y2 : 0.f;
+          v[4 * j + 3] = kept ? xx.w + y3 : 0.f;
+          part += (v[4 * j] + v[4 * j + 1]) + (v[4 * j + 2] + v[4 * j + 3]);
+        }
+        tmem_st32(tbase + static_cast<uint32_t>(c), v);
+      }
+      red[half * 128 + r] = part;
+      named_bar_sync(1, 256);
+      bool ok = true;
+      const float mean = exchange(0, tc, red[r] + red[128 + r], ok) * inv_n;
+      if (!ok) break;
+      // pass 2 (every thread has read red: the exchange's barrier is behind it)
+      float sq = 0.f;
+#pragma unroll 1
+      for (int c = 32 * half; c < BN; c += 64) {
+        float v[32];
+        tmem_ld32(tbase + static_cast<uint32_t>(c), v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float a = v[4 * j] - mean, b = v[4 * j + 1] - mean;
+          const float cc = v[4 * j + 2] - mean, dd = v[4 * j + 3] - mean;
+          sq += (a * a + b * b) + (cc * cc + dd * dd);
+        }
+      }
+      red[half * 128 + r] = sq;
+      named_bar_sync(1, 256);
+      const float var = exchange(1, tc, red[r] + red[128 + r], ok) * inv_n;
+      if (!ok) break;
+      const float rstd = 1.f / sqrtf(var + ln.eps);
+      // pass 3 (tcgen05.ld is warp-aligned: every lane loads, only the
+      // stores depend on the row)
+      {
+        const bool write_row = in_range && (kept || !skip_padded);
+        const bool zero_h = mask_out && !kept;
+        uint16_t* h_hi = reinterpret_cast<uint16_t*>(ln.h_out) + static_cast<int64_t>(row) * ln.ldh;
+        uint16_t* h_lo = h_hi + static_cast<int64_t>(M) * ln.ldh;
+        float* h_f = reinterpret_cast<float*>(ln.h_out) + static_cast<int64_t>(row) * ln.ldh;
+#pragma unroll 1
+        for (int c = 32 * half; c < BN; c += 64) {
+          float v[32];
+          tmem_ld32(tbase + static_cast<uint32_t>(c), v);
+          const int col0 = n0 + c;
+          if (!write_row) continue;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int col = col0 + 4 * j;
+            const float4 sv = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            if (ln.s_out)
+              *reinterpret_cast<float4*>(ln.s_out + static_cast<int64_t>(row) * ln.lds + col) = sv;
+            float4 hv = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (!zero_h) {
+              const float4 ww = __ldg(reinterpret_cast<const float4*>(ln.gamma + col));
+              const float4 bb = __ldg(reinterpret_cast<const float4*>(ln.beta + col));
+              hv.x = (sv.x - mean) * rstd * ww.x + bb.x;
+              hv.y = (sv.y - mean) * rstd * ww.y + bb.y;
+              hv.z = (sv.z - mean) * rstd * ww.z + bb.z;
+              hv.w = (sv.w - mean) * rstd * ww.w + bb.w;
+              if (rnd_h) {
+                hv.x = round_tf32(hv.x);
+                hv.y = round_tf32(hv.y);
+                hv.z = round_tf32(hv.z);
+                hv.w = round_tf32(hv.w);
+              }
+            }
+            if (split_h)
+              store_split4(h_hi + col, h_lo + col, hv);
+            else
+              *reinterpret_cast<float4*>(h_f + col) = hv;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      named_bar_sync(1, 256);  // epi_ok and red are rewritten for the next tile
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
   } else {
     // ------------------------------------------ epilogue (warps 2..9, two halves)
     // Warps 2-5 and 6-9 each cover all four TMEM lane quarters (warp w reads
@@ -597,6 +794,11 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // LNF: no CTA leaves while a peer may still write into its shared memory.
+  if (LNF) {
+    __syncwarp();
+    cluster_sync_all();
+  }
   if (warp == 1) {
     __syncwarp();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
@@ -626,8 +828,60 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   const int grid = tiles < sm_count() ? tiles : sm_count();
   return cuda_status(launch_chained(kern, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM_BYTES, st, ta,
                                     tb, tc, C, ldc, bias, M, N, K, flags, hd, hs, live_tiles,
-                                    live_count),
+                                    live_count, LnArgs{}),
                      "kf_gemm_tf32 launch");
+}
+
+// The LayerNorm-fused GEMM: clusters of N/128 CTAs, one row tile per cluster
+// at a time, as many clusters as can be resident at once.
+static int launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tb, const float* bias,
+                          int M, int N, int K, const LnArgs& ln, const int32_t* live_tiles,
+                          const int32_t* live_count, cudaStream_t st) {
+  using Cfg = GemmCfg<128, 3>;
+  auto kern = gemm_tf32_kernel<128, KF_EPI_BIAS, 3, true>;
+  static int attr_set[64] = {0};
+  static int max_clusters[64][9] = {{0}};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!attr_set[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return cuda_status(e, "kf_gemm_bf16x3_add_ln: set attributes");
+    attr_set[dev] = 1;
+  }
+  const int csize = N / 128;
+  if (!max_clusters[dev][csize]) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(csize * 8));
+    cfg.blockDim = dim3(Cfg::THREADS);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(csize);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / csize;
+    }
+    max_clusters[dev][csize] = n > 0 ? n : 1;
+  }
+  const int row_tiles = (M + Cfg::BM - 1) / Cfg::BM;
+  const int clusters = row_tiles < max_clusters[dev][csize] ? row_tiles : max_clusters[dev][csize];
+  CUtensorMap tc;
+  memset(&tc, 0, sizeof(tc));
+  return cuda_status(
+      launch_chained_cluster(kern, dim3(static_cast<unsigned>(clusters * csize)),
+                             dim3(Cfg::THREADS), Cfg::SMEM_BYTES, st,
+                             static_cast<unsigned>(csize), ta, tb, tc, static_cast<float*>(nullptr),
+                             static_cast<int64_t>(0), bias, M, N, K, 0, 0, 0, live_tiles,
+                             live_count, ln),
+      "kf_gemm_bf16x3_add_ln launch");
 }
 
 // Pick the N tile that minimises (waves x per-tile cost) on this GPU.
@@ -874,4 +1128,76 @@ extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W
   KF_GEMM_PRE_CASE(256)
 #undef KF_GEMM_PRE_CASE
   return KF_E_INVALID;
+}
+
+extern "C" int kf_gemm_bf16x3_add_ln(const uint16_t* A2, int64_t lda, const uint16_t* W2,
+                                     int64_t ldw, const float* bias, const float* res, int64_t ldr,
+                                     const uint8_t* keep, const float* gamma, const float* beta,
+                                     float eps, float* s_out, int64_t lds, void* h_out,
+                                     int64_t ldh, int64_t M, int64_t N, int64_t K, int ln_flags,
+                                     const int32_t* live_tiles, const int32_t* live_count,
+                                     void* stream) {
+  if (!A2 || !W2 || !res || !gamma || !beta || !h_out || M < 0 || N < 0 || K < 0) {
+    set_last_error("kf_gemm_bf16x3_add_ln: invalid arguments");
+    return KF_E_INVALID;
+  }
+  if (M == 0 || N == 0) return KF_OK;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (N % 128 || N / 128 > 8 || K == 0 || K % 8 || lda % 8 || ldw % 8 || lda < K || ldw < K ||
+      ldr % 4 || ldr < N || ldh < N || (s_out && (lds % 4 || lds < N || !a16(s_out))) ||
+      !a16(A2) || !a16(W2) || !a16(res) || !a16(gamma) || !a16(beta) || !a16(h_out) ||
+      (bias && !a16(bias)) || ((ln_flags & KF_LN_OUT_BF16X2) ? ldh % 8 : ldh % 4)) {
+    set_last_error(
+        "kf_gemm_bf16x3_add_ln: needs N %% 128 == 0 and N <= 1024, K, lda, ldw %% 8 == 0, "
+        "ldr, lds %% 4 == 0, ldh %% %d == 0 and 16-byte aligned pointers (N=%lld K=%lld)",
+        (ln_flags & KF_LN_OUT_BF16X2) ? 8 : 4, (long long)N, (long long)K);
+    return KF_E_UNSUPPORTED;
+  }
+  if (M > INT32_MAX / 2 || K > INT32_MAX) {
+    set_last_error("kf_gemm_bf16x3_add_ln: dimensions beyond 2^30");
+    return KF_E_UNSUPPORTED;
+  }
+  if ((ln_flags & KF_LN_OUT_BF16X2) && (ln_flags & KF_LN_ROUND_TF32)) {
+    set_last_error("kf_gemm_bf16x3_add_ln: KF_LN_OUT_BF16X2 and KF_LN_ROUND_TF32 are exclusive");
+    return KF_E_INVALID;
+  }
+  if ((live_tiles == nullptr) != (live_count == nullptr)) {
+    set_last_error("kf_gemm_bf16x3_add_ln: live_tiles and live_count go together");
+    return KF_E_INVALID;
+  }
+  CUtensorMap ta, tb;
+  int rc;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M), 2};
+    const uint64_t strides[2] = {static_cast<uint64_t>(lda) * 2,
+                                 static_cast<uint64_t>(M) * static_cast<uint64_t>(lda) * 2};
+    const uint32_t box[3] = {64, 128, 1};
+    rc = encode_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, A2, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N), 2};
+    const uint64_t strides[2] = {static_cast<uint64_t>(ldw) * 2,
+                                 static_cast<uint64_t>(N) * static_cast<uint64_t>(ldw) * 2};
+    const uint32_t box[3] = {64, 128, 1};
+    rc = encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, W2, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  LnArgs ln;
+  ln.res = res;
+  ln.ldr = ldr;
+  ln.keep = keep;
+  ln.gamma = gamma;
+  ln.beta = beta;
+  ln.s_out = s_out;
+  ln.lds = lds;
+  ln.h_out = h_out;
+  ln.ldh = ldh;
+  ln.eps = eps;
+  ln.flags = ln_flags & (KF_LN_MASK_OUT | KF_LN_ROUND_TF32 | KF_LN_SKIP_PADDED | KF_LN_OUT_BF16X2);
+  return launch_gemm_ln(ta, tb, bias, static_cast<int>(M), static_cast<int>(N),
+                        static_cast<int>(K), ln, live_tiles, live_count,
+                        static_cast<cudaStream_t>(stream));
 }

@@ -52,6 +52,12 @@ class Plan:
     # GEMMs compute only 128-row tiles holding a real token and the non-final
     # norms leave padded rows untouched (every consumer masks those rows).
     skip_padded_rows: bool = True
+    # Residual add + mask + LayerNorm in the epilogue of out_proj and FFN2
+    # (bf16x3 GEMMs, d a multiple of 128 up to 1024): one kernel fewer per
+    # norm, and y never reaches memory. Off unless the table turns it on for
+    # a shape: with one row tile per cluster (c2) the fused epilogue is
+    # exposed and the forward is slower (0.850 vs 0.731 ms).
+    fuse_ln: bool = False
     # N tile of each GEMM (0 = pick by wave quantisation at launch).
     bn_qkv: int = 0
     bn_out: int = 0
@@ -75,6 +81,8 @@ class Plan:
             bits.append("skip-empty-q")
         if self.skip_padded_rows:
             bits.append("skip-padded-rows")
+        if self.fuse_ln:
+            bits.append("ln-in-gemm")
         if self.cuda_graph:
             bits.append("cuda-graph")
         tiles = (self.bn_qkv, self.bn_out, self.bn_ffn1, self.bn_ffn2)

@@ -77,3 +77,18 @@ def test_empty_problems_are_no_ops(lib):
     assert lib.kf_gemm_tf32(fake, 8, fake, 8, None, fake, 8, 0, 8, 8, 0, 0, 0, 0, 0, None, None, None) == 0
     assert lib.kf_ln_add_mask(fake, 8, None, 0, None, fake, fake, None, 0, fake, 8, 0, 8, 1e-5,
                               0, None) == 0
+
+
+def test_fused_gemm_layernorm_entry_rejects_before_any_launch():
+    """kf_gemm_bf16x3_add_ln validates its arguments on the host: null
+    operands, and widths that are not a multiple of 128 (or above 1024), are
+    refused with an error code before any CUDA call."""
+    lib = _lib.lib()
+    args = lambda N: (16, 64, 16, 64, None, 16, N, None, 16, 16, 1e-5, None, 0, 16, N, 128, N,
+                      64, 0, None, None, None)
+    assert lib.kf_gemm_bf16x3_add_ln(None, 64, None, 64, None, None, 128, None, None, None, 1e-5,
+                                     None, 0, None, 128, 128, 128, 64, 0, None, None, None) == \
+        _lib.KF_E_INVALID
+    assert lib.kf_gemm_bf16x3_add_ln(*args(100)) == _lib.KF_E_UNSUPPORTED
+    assert b"128" in lib.kf_last_error()
+    assert lib.kf_gemm_bf16x3_add_ln(*args(2048)) == _lib.KF_E_UNSUPPORTED

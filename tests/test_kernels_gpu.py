@@ -569,3 +569,73 @@ def test_gemm_gelu_epilogue_error_bound(out_split):
     assert bool((err <= bound).all()), f"max err {err.max().item()}"
     # and against the fp32 erf GELU that torch computes on the GPU
     assert (got - F.gelu(x).double()).abs().max().item() < 2e-5
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (300, 512, 512), (4096, 512, 2048),
+                                   (1000, 768, 256), (517, 1024, 512)])
+@pytest.mark.parametrize("mode", ["planes_skip", "final_mask_out", "fp32_round"])
+def test_gemm_layernorm_fusion_matches_two_kernels(M, N, K, mode):
+    """kf_gemm_bf16x3_add_ln == kf_gemm_bf16x3 (bias) then kf_ln_add_mask:
+    s bit-identical (the same fp32 additions), h within 2e-5 (only the
+    order of the row reductions differs; for bf16 hi/lo planes plus the
+    pairs' own 2^-16), padded rows handled as the flags say. Widths
+    128..1024 use clusters of 1..8 CTAs."""
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    torch.manual_seed(M + N + K)
+    a = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / math.sqrt(K)
+    bias = torch.randn(N, device="cuda")
+    res0 = torch.randn(M, N, device="cuda")
+    gamma, beta = torch.randn(N, device="cuda"), torch.randn(N, device="cuda")
+    keep = (torch.rand(M, device="cuda") > 0.3).to(torch.uint8)
+    keep[:7] = 1
+    a2, w2 = to_planes(a).contiguous(), to_planes(w).contiguous()
+    flags = {"planes_skip": _lib.KF_LN_OUT_BF16X2 | _lib.KF_LN_SKIP_PADDED,
+             "final_mask_out": _lib.KF_LN_MASK_OUT,
+             "fp32_round": _lib.KF_LN_ROUND_TF32}[mode]
+    planes = mode == "planes_skip"
+    with_s = mode != "final_mask_out"
+
+    def new_h():
+        if planes:
+            return torch.full((2, M, N), 0x1357, dtype=torch.int16, device="cuda")
+        return torch.full((M, N), 3.0, device="cuda")
+
+    # two kernels
+    y = torch.empty(M, N, device="cuda")
+    _lib.check(L.kf_gemm_bf16x3(a2.data_ptr(), K, w2.data_ptr(), K, bias.data_ptr(), y.data_ptr(),
+                                N, M, N, K, _lib.KF_EPI_BIAS, 0, 0, 0, 0, None, None,
+                                _lib.stream_ptr()), "gemm")
+    res_a, h_a = res0.clone(), new_h()
+    _lib.check(L.kf_ln_add_mask(res_a.data_ptr(), N, y.data_ptr(), N, keep.data_ptr(),
+                                gamma.data_ptr(), beta.data_ptr(),
+                                res_a.data_ptr() if with_s else None, N, h_a.data_ptr(), N, M, N,
+                                1e-5, flags, _lib.stream_ptr()), "ln")
+    # one kernel
+    res_b, h_b = res0.clone(), new_h()
+    _lib.check(L.kf_gemm_bf16x3_add_ln(a2.data_ptr(), K, w2.data_ptr(), K, bias.data_ptr(),
+                                       res_b.data_ptr(), N, keep.data_ptr(), gamma.data_ptr(),
+                                       beta.data_ptr(), 1e-5,
+                                       res_b.data_ptr() if with_s else None, N, h_b.data_ptr(),
+                                       N, M, N, K, flags, None, None, _lib.stream_ptr()),
+               "gemm+ln")
+    torch.cuda.synchronize()
+    assert L.kf_device_status(0) == 0
+    assert torch.equal(res_a, res_b)
+    if planes:
+        kept = keep.bool()
+        assert torch.equal(h_a[:, ~kept], h_b[:, ~kept])        # untouched padded rows
+        ha, hb = from_planes(h_a)[kept], from_planes(h_b)[kept]
+        # a last-bit change of mean or rstd may move the hi/lo split: each
+        # pair carries ~2^-17 relative error, so two pairs differ by <= 2^-16
+        bound = 2e-5 + 2.0 ** -16 * ha.abs()
+    elif mode == "fp32_round":
+        # rounding to TF32 turns a last-bit difference into at most one
+        # TF32 unit (2^-10 relative)
+        ha, hb = h_a, h_b
+        bound = 2e-5 + 2.0 ** -10 * ha.abs()
+    else:
+        ha, hb = h_a, h_b
+        bound = 2e-5 + 0 * ha
+    assert bool(((ha - hb).abs() <= bound).all()), (ha - hb).abs().max().item()
