@@ -44,7 +44,7 @@ sys.path.insert(0, ROOT)
 import torch  # noqa: E402
 
 from techjam2026_b200.configs import WORKLOADS, generate_case, make_state_dict  # noqa: E402
-from techjam2026_b200.roofline import (lengths_of, measured_peaks, useful_flops,  # noqa: E402
+from techjam2026_b200.roofline import (lengths_of, measured_peaks, profiled_traffic, useful_flops,  # noqa: E402
                                        dense_causal_flops)
 
 METRIC = "layer-stack fwd latency ms & TFLOP/s (% tcgen05 peak) at 1/2/4/8 B200 vs CPU ref"
@@ -508,9 +508,14 @@ def main():
         achieved = amount / (dom_ms / 1e3) / 1e9
         peak = peaks["hbm_gbs"]
         r_unit = "GB/s"
+    # DRAM bytes of one launch of the dominant kernel, from the committed ncu
+    # capture of this workload (null when no capture covers it).
+    prof = profiled_traffic(w.name, dom)
     roofline = {"kernel": dom, "bound": bound, "achieved": round(achieved, 2),
                 "peak": round(peak, 1), "unit": r_unit, "frac": round(achieved / peak, 4),
-                "traffic": None,
+                "traffic": prof["bytes"] if prof else None,
+                "traffic_source": (f"{prof['source']} (ncu dram__bytes_read.sum + "
+                                   "dram__bytes_write.sum, one launch)") if prof else None,
                 "peak_source": f"{peaks['source']} (TF32 = measured dense BF16 / 2)"
                 if bound == "tensor" else peaks["source"],
                 "launch_ms": round(dom_ms, 5),

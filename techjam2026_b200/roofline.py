@@ -89,3 +89,28 @@ def measured_peaks(path: Optional[str] = None) -> dict:
     out["tf32_tflops"] = out["bf16_tflops"] / 2.0
     out["tf32_tflops_sustained"] = out["bf16_tflops_sustained"] / 2.0
     return out
+
+
+def profiled_traffic(workload: str, kind: str, folder: Optional[str] = None) -> Optional[dict]:
+    """DRAM bytes per launch of `kind` on `workload`, from an ncu capture.
+
+    Reads the `traffic <workload> <kind> <bytes>` lines of the committed
+    capture summaries (profiles/traffic_*.md: dram__bytes_read.sum +
+    dram__bytes_write.sum per launch, one ncu pass over one forward).
+    Returns {"bytes": N, "source": file name} or None when no capture covers
+    the pair."""
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    folder = folder or os.path.join(here, "profiles")
+    try:
+        names = sorted(n for n in os.listdir(folder)
+                       if n.startswith("traffic_") and n.endswith(".md"))
+    except OSError:
+        return None
+    for name in names:
+        with open(os.path.join(folder, name), encoding="utf-8") as f:
+            for line in f:
+                parts = line.split()
+                if (len(parts) == 4 and parts[0] == "traffic" and parts[1] == workload
+                        and parts[2] == kind):
+                    return {"bytes": int(parts[3]), "source": f"profiles/{name}"}
+    return None
