@@ -329,17 +329,22 @@ def kernel_breakdown(model, x, keep, ws, weights, repeats: int = 5):
 
 
 def kernel_work(kind: str, cfg, B: int, S: int, lengths) -> tuple:
-    """Algorithmic work of ONE launch of `kind`: (amount, unit, bound)."""
+    """Algorithmic work of ONE launch of `kind`: (amount, unit, bound).
+
+    GEMMs count the valid tokens T only (2*T*N*K): padded rows are not
+    algorithmic work, so skipping them cannot raise the fraction. Attention
+    counts valid causal pairs; the norm counts 16*d bytes per row."""
     d, F, H = cfg.d_model, cfg.ffn_dim, cfg.num_heads
     M = B * S
+    T = float(sum(lengths))
     if kind == "qkv":
-        return 2.0 * M * 3 * d * d, "flop", "tensor"
+        return 2.0 * T * 3 * d * d, "flop", "tensor"
     if kind == "out_proj":
-        return 2.0 * M * d * d, "flop", "tensor"
+        return 2.0 * T * d * d, "flop", "tensor"
     if kind == "ffn1":
-        return 2.0 * M * F * d, "flop", "tensor"
+        return 2.0 * T * F * d, "flop", "tensor"
     if kind == "ffn2":
-        return 2.0 * M * d * F, "flop", "tensor"
+        return 2.0 * T * d * F, "flop", "tensor"
     if kind == "attention":
         pairs = sum(n * (n + 1) // 2 for n in lengths) if cfg.causal else sum(n * n for n in lengths)
         return 4.0 * d * pairs, "flop", "tensor"

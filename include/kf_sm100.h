@@ -107,6 +107,14 @@ int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t ldw, const
                  const int32_t* live_count, void* stream);
 
 #define KF_GEMM_OUT_BF16X2 8 /* kf_gemm_bf16x3: write C as bf16 hi/lo planes */
+#define KF_GEMM_K32 16       /* kf_gemm_bf16x3: stream k blocks of 32 instead of 64
+                                (twice as many half-size stages in flight; same
+                                MMA order, so C is bit-identical) */
+#define KF_GEMM_PAIR 32      /* kf_gemm_bf16x3: 256 x bn tiles on CTA pairs
+                                (tcgen05 cta_group::2; bn 128 or 256): each SM
+                                stages its 128 A rows and half of the B rows, so
+                                shared-memory operand traffic per product drops
+                                by a third (bn 256); same accumulation order */
 
 /* Error-compensated GEMM on operands already split into bf16 planes:
  * A2 = [2][M][lda] (hi plane, then lo plane, with hi + lo = the fp32 value to

@@ -77,6 +77,8 @@ KF_ATTN_SKIP_EMPTY_Q = 2
 KF_ATTN_ROUND_TF32 = 4
 KF_ATTN_OUT_BF16X2 = 8
 KF_GEMM_OUT_BF16X2 = 8
+KF_GEMM_K32 = 16
+KF_GEMM_PAIR = 32
 KF_NOALLOC_KEEP_WORDS_MAX = 262144
 
 _lib = None

@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(192, MINB)
             }
           }
           bulk_commit_group();
-          bulk_wait_group_all();
+          bulk_wait_group_read<0>();  // the zero box is read; the writes finish with the grid
         }
       }
     } else {
@@ -596,7 +596,7 @@ __global__ void __launch_bounds__(192, MINB)
                                  c * 64, rows0, h, b + pl * nb);
               }
               bulk_commit_group();
-              bulk_wait_group_all();
+              bulk_wait_group_read<0>();  // staging read; the writes finish with the grid
             }
           } else {
 #pragma unroll 1

@@ -43,15 +43,31 @@ namespace kf {
 enum : int { KF_GEMM_VEC_OK = 1 << 8, KF_GEMM_TMA_OUT = 1 << 9, KF_GEMM_OUT_SPLIT = 1 << 10 };
 // SPLIT_BF16X3_PRE: operands arrive already split into bf16 hi/lo planes
 // (kf_gemm_bf16x3); TMA loads the four planes, no converter warps.
-enum : int { SPLIT_NONE = 0, SPLIT_TF32X3 = 1, SPLIT_BF16X3 = 2, SPLIT_BF16X3_PRE = 3 };
+// SPLIT_BF16X3_PRE32: the same with 32-wide k blocks (64-byte rows, 64-byte
+// swizzle): stages of half the size, so twice as many are in flight in the
+// same shared memory. The MMAs run in the same order, so C is bit-identical.
+enum : int {
+  SPLIT_NONE = 0,
+  SPLIT_TF32X3 = 1,
+  SPLIT_BF16X3 = 2,
+  SPLIT_BF16X3_PRE = 3,
+  SPLIT_BF16X3_PRE32 = 4
+};
 
-template <int BN, int SPLIT>
+// PAIR: cta_group::2 tiles of 256 x BN computed by a cluster of two CTAs;
+// each CTA stages its own 128 A rows and half of the BN B rows, and holds
+// the accumulator of its 128 rows (BN columns) in its own TMEM.
+template <int BN, int SPLIT, bool PAIR = false>
 struct GemmCfg {
   static constexpr int BM = 128;
-  // One 128-byte swizzle row per k block: 32 fp32 or (pre-split) 64 bf16.
-  static constexpr int BK = SPLIT == 3 ? 64 : 32;
-  static constexpr int A_BYTES = BM * 128;  // one plane
-  static constexpr int B_BYTES = BN * 128;
+  // One swizzle row per k block and plane: 128 bytes (32 fp32 or, pre-split,
+  // 64 bf16), or 64 bytes (32 bf16) for SPLIT_BF16X3_PRE32.
+  static constexpr int ROW_BYTES = SPLIT == SPLIT_BF16X3_PRE32 ? 64 : 128;
+  static constexpr int BK = SPLIT == SPLIT_BF16X3_PRE ? 64 : 32;
+  static constexpr bool PRESPLIT = SPLIT == SPLIT_BF16X3_PRE || SPLIT == SPLIT_BF16X3_PRE32;
+  static constexpr int A_BYTES = BM * ROW_BYTES;  // one plane
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B rows staged by this CTA
+  static constexpr int B_BYTES = B_ROWS * ROW_BYTES;
   // stage layout: A | B [| lo(A) | lo(B)]
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (SPLIT ? 2 : 1);
   static constexpr int STAGES_FIT = 196608 / STAGE_BYTES;
@@ -72,6 +88,7 @@ struct GemmCfg {
   static_assert(BN == 64 || BN == 96 || BN == 128 || BN == 256, "BN");
   static_assert(STAGES >= 2 && STAGES <= 8, "stages");
   static_assert(SMEM_BYTES <= 232448, "smem");
+  static_assert(!PAIR || (SPLIT == SPLIT_BF16X3_PRE && (BN == 128 || BN == 256)), "pair shape");
 };
 
 // Low part of a TF32 split: x - trunc_tf32(x), exact in fp32.
@@ -116,6 +133,18 @@ __device__ __forceinline__ void split_bf16_chunk(const uint8_t* f32_tile, uint8_
   *reinterpret_cast<uint4*>(lo_tile + dst) =
       make_uint4(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]), pack_bf16x2(l[4], l[5]),
                  pack_bf16x2(l[6], l[7]));
+}
+
+// cta_group::2: issued by the pair's first CTA, A rows from both CTAs, B
+// columns split between them, D in both CTAs' TMEM.
+__device__ __forceinline__ void mma_bf16_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
@@ -218,15 +247,16 @@ struct LnArgs {
   int flags;
 };
 
-template <int BN, int EPI, int SPLIT, bool LNF = false>
+template <int BN, int EPI, int SPLIT, bool LNF = false, bool PAIR = false>
 __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int M,
                      int N, int K, int flags, int head_dim, int head_stride,
                      const int32_t* __restrict__ live_tiles, const int32_t* __restrict__ live_count,
                      const __grid_constant__ LnArgs ln) {
-  using Cfg = GemmCfg<BN, SPLIT>;
+  using Cfg = GemmCfg<BN, SPLIT, PAIR>;
   constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
+  static_assert(!(LNF && PAIR), "pair kernels have the plain epilogues");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -249,6 +279,8 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   const int lane = threadIdx.x & 31;
   const int num_n = (N + BN - 1) / BN;
   const int num_kb = (K + BK - 1) / BK;
+  // PAIR: rank in the CTA pair; rank 0 issues the MMAs for both.
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -258,7 +290,8 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], Cfg::EPI_WARPS);
+      // PAIR: rank 0's barrier counts the epilogue warps of both CTAs.
+      mbar_init(&acc_empty[a], PAIR ? 2 * Cfg::EPI_WARPS : Cfg::EPI_WARPS);
     }
     mbar_init(drain, 1);
     if (LNF)
@@ -270,16 +303,22 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
     if (flags & KF_GEMM_TMA_OUT) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // LNF: every CTA of the cluster has initialised its exchange barriers
-  // before any CTA arrives on them remotely (warp-aligned: reconverge first).
-  if (LNF) {
+  // LNF / PAIR: every CTA of the cluster has initialised its barriers (and
+  // holds its TMEM) before any CTA signals them remotely (warp-aligned:
+  // reconverge first).
+  if (LNF || PAIR) {
     __syncwarp();
     cluster_sync_all();
   }
@@ -295,10 +334,26 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   // (kf_live_row_tiles); other row tiles are not computed and keep their
   // contents. Every role reads the same list, so they agree on the schedule.
   const int num_m = live_tiles ? __ldg(live_count) : (M + BM - 1) / BM;
-  const int num_tiles = num_m * num_n;
-  auto row0 = [&](int tile) -> int {
-    const int mi = tile / num_n;
+  // Work units: 128 x BN tiles, or (PAIR) 256 x BN tiles made of the row
+  // tiles 2i and 2i+1 of the list (the two need not be adjacent rows). With an
+  // odd count the last pair's second CTA repeats the first's rows and stores
+  // nothing. Units go round-robin over CTAs (pairs), N fastest.
+  const int num_tiles = (PAIR ? (num_m + 1) / 2 : num_m) * num_n;
+  const int unit0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int ustride = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  auto row_tile = [&](int tile, bool& own) -> int {
+    int mi = tile / num_n;
+    own = true;
+    if (PAIR) {
+      const int j = 2 * mi + static_cast<int>(crank);
+      own = j < num_m;
+      mi = own ? j : 2 * mi;
+    }
     return (live_tiles ? __ldg(live_tiles + mi) : mi) * BM;
+  };
+  auto row0 = [&](int tile) -> int {
+    bool own;
+    return row_tile(tile, own);
   };
 
   if (warp == 0) {
@@ -308,16 +363,27 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = unit0; tile < num_tiles && ok; tile += ustride) {
         const int m0 = row0(tile);
-        const int n0 = (tile % num_n) * BN;
+        // PAIR: this CTA stages B rows [n0 + rank * BN/2, + BN/2) of the tile.
+        const int n0 = (tile % num_n) * BN + static_cast<int>(crank) * (PAIR ? Cfg::B_ROWS : 0);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, KF_DEV_WAIT_TIMEOUT_TMA)) {
             ok = false;
             break;
           }
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
-          if (SPLIT == SPLIT_BF16X3_PRE) {
+          if constexpr (PAIR) {
+            // Both CTAs' loads complete on rank 0's barrier, which rank 0 arms
+            // with the bytes of the pair (the other CTA's bytes may land
+            // first: the phase cannot end before rank 0's arrival).
+            if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_3d_pair(sa, &tmA, fb, kb * BK, m0, 0);
+            tma_load_3d_pair(sa + Cfg::A_BYTES, &tmB, fb, kb * BK, n0, 0);
+            tma_load_3d_pair(sa + Cfg::A_BYTES + Cfg::B_BYTES, &tmA, fb, kb * BK, m0, 1);
+            tma_load_3d_pair(sa + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &tmB, fb, kb * BK, n0, 1);
+          } else if (Cfg::PRESPLIT) {
             // planes: A_hi | B_hi | A_lo | B_lo (3-D maps, plane = coordinate 2)
             mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
             tma_load_3d(sa, &tmA, &full[stage], kb * BK, m0, 0);
@@ -337,7 +403,15 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
           }
         }
       }
-      if (!ok) {
+      if (PAIR) {
+        // Rank 0's MMA thread releases the stages of both CTAs (its commits
+        // arrive in this CTA's shared memory, and its products read this
+        // CTA's tiles): wait for the release of the last ones before leaving.
+        const long long first = issued > STAGES ? issued - STAGES : 0;
+        for (long long i = first; i < issued; ++i)
+          mbar_wait_drain(&empty[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1),
+                          KF_DEV_WAIT_TIMEOUT_TMA);
+      } else if (!ok) {
         // Drain: wait for the loads still in flight (the last <= STAGES).
         const long long first = issued > STAGES ? issued - STAGES : 0;
         for (long long i = first; i < issued; ++i)
@@ -346,17 +420,23 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && crank == 0) {
       // ------------------------------------------------ MMA issuer
+      // (PAIR: rank 0 only; each cta_group::2 product covers both CTAs' rows)
       constexpr uint32_t idesc = make_idesc_tf32(BM, BN, 0, 0);
-      constexpr uint32_t idesc_bf = make_idesc_bf16(BM, BN);
+      constexpr uint32_t idesc_bf = make_idesc_bf16(PAIR ? 2 * BM : BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA)) {
+      for (int tile = unit0; tile < num_tiles && ok; tile += ustride) {
+        // PAIR: the other CTA's epilogue warps arrive remotely (release at
+        // cluster scope), so the wait acquires at cluster scope.
+        if (!(PAIR ? mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, abort_flag,
+                                       KF_DEV_WAIT_TIMEOUT_MMA)
+                   : mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag,
+                               KF_DEV_WAIT_TIMEOUT_MMA))) {
           ok = false;
           break;
         }
@@ -373,7 +453,20 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
           const uint32_t b_addr = a_addr + Cfg::A_BYTES;
           const uint32_t alo_addr = b_addr + Cfg::B_BYTES;
           const uint32_t blo_addr = alo_addr + Cfg::A_BYTES;
-          if (SPLIT == SPLIT_BF16X3_PRE) {
+          if (PAIR) {
+            // As below, one cta_group::2 product per step: M = 256 rows (A
+            // from both CTAs), B's BN rows split between the CTAs.
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint64_t ah = make_smem_desc(a_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+              const uint64_t bh = make_smem_desc(b_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+              const uint64_t al = make_smem_desc(alo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+              const uint64_t bl = make_smem_desc(blo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+              mma_bf16_ss_pair(d_tmem, al, bh, idesc_bf, (kb | k) != 0 ? 1u : 0u);
+              mma_bf16_ss_pair(d_tmem, ah, bl, idesc_bf, 1u);
+              mma_bf16_ss_pair(d_tmem, ah, bh, idesc_bf, 1u);
+            }
+          } else if (SPLIT == SPLIT_BF16X3_PRE) {
             // TMA-loaded bf16 planes, 128-byte rows (SW128): 4 k steps of 16.
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
@@ -381,6 +474,18 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
               const uint64_t bh = make_smem_desc(b_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
               const uint64_t al = make_smem_desc(alo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
               const uint64_t bl = make_smem_desc(blo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
+              mma_bf16_ss(d_tmem, al, bh, idesc_bf, (kb | k) != 0 ? 1u : 0u);
+              mma_bf16_ss(d_tmem, ah, bl, idesc_bf, 1u);
+              mma_bf16_ss(d_tmem, ah, bh, idesc_bf, 1u);
+            }
+          } else if (SPLIT == SPLIT_BF16X3_PRE32) {
+            // TMA-loaded bf16 planes, 64-byte rows (SW64): 2 k steps of 16.
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint64_t ah = make_smem_desc(a_addr + k * 32, 16, 512, KF_SWIZZLE_64B);
+              const uint64_t bh = make_smem_desc(b_addr + k * 32, 16, 512, KF_SWIZZLE_64B);
+              const uint64_t al = make_smem_desc(alo_addr + k * 32, 16, 512, KF_SWIZZLE_64B);
+              const uint64_t bl = make_smem_desc(blo_addr + k * 32, 16, 512, KF_SWIZZLE_64B);
               mma_bf16_ss(d_tmem, al, bh, idesc_bf, (kb | k) != 0 ? 1u : 0u);
               mma_bf16_ss(d_tmem, ah, bl, idesc_bf, 1u);
               mma_bf16_ss(d_tmem, ah, bh, idesc_bf, 1u);
@@ -413,21 +518,36 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
             mma_tf32_ss(d_tmem, ad, bd, idesc, (SPLIT || (kb | k) != 0) ? 1u : 0u);
             (void)idesc_bf;
           }
-          mma_commit(&empty[stage]);
+          if constexpr (PAIR) {
+            // The stage is free in both CTAs once these products complete.
+            mma_commit_pair(&empty[stage]);
+            mma_commit_pair_at(mapa_shared(smem_u32(&empty[stage]), 1));
+          } else {
+            mma_commit(&empty[stage]);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(&acc_full[acc]);
+        if constexpr (PAIR) {
+          mma_commit_pair(&acc_full[acc]);
+          mma_commit_pair_at(mapa_shared(smem_u32(&acc_full[acc]), 1));
+        } else {
+          mma_commit(&acc_full[acc]);
+        }
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
       // Every MMA this thread issued completes before TMEM is released.
-      mma_commit(drain);
+      if constexpr (PAIR) {
+        mma_commit_pair(drain);
+      } else {
+        mma_commit(drain);
+      }
       mbar_wait_drain(drain, 0, KF_DEV_WAIT_TIMEOUT_MMA);
     }
   } else if (Cfg::CONVERTS && warp >= Cfg::CONV_WARP0) {
@@ -436,7 +556,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+    for (int tile = unit0; tile < num_tiles && ok; tile += ustride) {
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA)) {
           ok = false;
@@ -458,7 +578,8 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
           const uint4* src = reinterpret_cast<const uint4*>(st_base);
           uint4* dst = reinterpret_cast<uint4*>(st_base + Cfg::A_BYTES + Cfg::B_BYTES);
           constexpr int NV = (Cfg::A_BYTES + Cfg::B_BYTES) / 16 / Cfg::CONV_THREADS;
-          static_assert(NV * 16 * Cfg::CONV_THREADS == Cfg::A_BYTES + Cfg::B_BYTES, "split");
+          static_assert(!Cfg::CONVERTS || NV * 16 * Cfg::CONV_THREADS == Cfg::A_BYTES + Cfg::B_BYTES,
+                        "split");
           uint4 v[NV];
 #pragma unroll
           for (int t = 0; t < NV; ++t) v[t] = src[ct + t * Cfg::CONV_THREADS];  // all loads in flight
@@ -660,8 +781,9 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
     uint8_t* buf = smem + Cfg::EPI_OFF + half * Cfg::EPI_BUF_BYTES;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int m0 = row0(tile);
+    for (int tile = unit0; tile < num_tiles; tile += ustride) {
+      bool own;  // PAIR: false for a repeated row tile (nothing stored)
+      const int m0 = row_tile(tile, own);
       const int n0 = (tile % num_n) * BN;
       // One bounded wait by the half's leader, shared through the half's
       // named barrier, so all four warps of a half always reach the same
@@ -678,7 +800,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
       float* crow = C + static_cast<int64_t>(row) * ldc;
 #pragma unroll 1
       for (int c = 32 * half; c < BN; c += 64) {
-        if (n0 + c >= N) break;  // uniform over the half
+        if (n0 + c >= N || !own) break;  // uniform over the half
         float v[32];
         tmem_ld32(tbase + static_cast<uint32_t>(c), v);
         if (tma_out && (flags & KF_GEMM_OUT_SPLIT)) {
@@ -781,27 +903,40 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (lane == 0) {
+        // PAIR: the accumulator is handed back to rank 0's MMA thread.
+        if (PAIR)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+        else
+          mbar_arrive(&acc_empty[acc]);
+      }
       named_bar_sync(bar_id, 128);  // the half has read epi_ok before it is rewritten
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
-    if (tma_out && leader) bulk_wait_group_all();
+    // Shared memory must outlive the stores' reads of it; the writes
+    // themselves complete before the grid does (a dependent kernel's
+    // griddepcontrol.wait sees them).
+    if (tma_out && leader) bulk_wait_group_read<0>();
   }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // LNF: no CTA leaves while a peer may still write into its shared memory.
-  if (LNF) {
+  // LNF / PAIR: no CTA leaves while a peer may still write into its shared
+  // memory or arrive on its barriers; PAIR frees TMEM as a pair.
+  if (LNF || PAIR) {
     __syncwarp();
     cluster_sync_all();
   }
   if (warp == 1) {
     __syncwarp();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
@@ -830,6 +965,56 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
                                     tb, tc, C, ldc, bias, M, N, K, flags, hd, hs, live_tiles,
                                     live_count, LnArgs{}),
                      "kf_gemm_tf32 launch");
+}
+
+// cta_group::2 GEMM: clusters of two CTAs (one 256 x BN tile per pair at a
+// time), as many pairs as can be resident at once.
+template <int BN, int EPI>
+static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                            float* C, int64_t ldc, const float* bias, int M, int N, int K,
+                            int flags, int hd, int hs, const int32_t* live_tiles,
+                            const int32_t* live_count, cudaStream_t st) {
+  using Cfg = GemmCfg<BN, SPLIT_BF16X3_PRE, true>;
+  auto kern = gemm_tf32_kernel<BN, EPI, SPLIT_BF16X3_PRE, false, true>;
+  static int attr_set[64] = {0};
+  static int max_pairs[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!attr_set[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_status(e, "kf_gemm_bf16x3 (pair): set smem attribute");
+    attr_set[dev] = 1;
+  }
+  if (!max_pairs[dev]) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 8);
+    cfg.blockDim = dim3(Cfg::THREADS);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / 2;
+    }
+    max_pairs[dev] = n > 0 ? n : 1;
+  }
+  // Units of 256 x BN over all row tiles (the live count is only known on
+  // the device; pairs without work exit).
+  const int units = (((M + Cfg::BM - 1) / Cfg::BM + 1) / 2) * ((N + BN - 1) / BN);
+  const int pairs = units < max_pairs[dev] ? units : max_pairs[dev];
+  return cuda_status(
+      launch_chained_cluster(kern, dim3(static_cast<unsigned>(2 * pairs)), dim3(Cfg::THREADS),
+                             Cfg::SMEM_BYTES, st, 2u, ta, tb, tc, C, ldc, bias, M, N, K, flags, hd,
+                             hs, live_tiles, live_count, LnArgs{}),
+      "kf_gemm_bf16x3 (pair) launch");
 }
 
 // The LayerNorm-fused GEMM: clusters of N/128 CTAs, one row tile per cluster
@@ -1068,6 +1253,17 @@ extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W
     set_last_error("kf_gemm_bf16x3: bn must be 0, 64, 96, 128 or 256");
     return KF_E_INVALID;
   }
+  // k blocks of 64 bf16 (128-byte rows) or, with KF_GEMM_K32, of 32 (64-byte
+  // rows): the x coordinate of every load is a multiple of 32 elements.
+  const bool k32 = (flags & KF_GEMM_K32) != 0;
+  // KF_GEMM_PAIR: cta_group::2 tiles of 256 x bn; each CTA stages bn/2 B rows.
+  const bool pair = (flags & KF_GEMM_PAIR) != 0;
+  if (pair && (k32 || (bn != 128 && bn != 256))) {
+    set_last_error("kf_gemm_bf16x3: KF_GEMM_PAIR needs bn 128 or 256 and no KF_GEMM_K32");
+    return KF_E_INVALID;
+  }
+  const uint32_t kbox = k32 ? 32 : 64;
+  const CUtensorMapSwizzle ksw = k32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   CUtensorMap ta, tb, tcm;
   memset(&tcm, 0, sizeof(tcm));
   int rc;
@@ -1075,18 +1271,16 @@ extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W
     const uint64_t dims[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M), 2};
     const uint64_t strides[2] = {static_cast<uint64_t>(lda) * 2,
                                  static_cast<uint64_t>(M) * static_cast<uint64_t>(lda) * 2};
-    const uint32_t box[3] = {64, 128, 1};
-    rc = encode_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, A2, dims, strides, box,
-                           CU_TENSOR_MAP_SWIZZLE_128B);
+    const uint32_t box[3] = {kbox, 128, 1};
+    rc = encode_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, A2, dims, strides, box, ksw);
     if (rc) return rc;
   }
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N), 2};
     const uint64_t strides[2] = {static_cast<uint64_t>(ldw) * 2,
                                  static_cast<uint64_t>(N) * static_cast<uint64_t>(ldw) * 2};
-    const uint32_t box[3] = {64, static_cast<uint32_t>(bn), 1};
-    rc = encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, W2, dims, strides, box,
-                           CU_TENSOR_MAP_SWIZZLE_128B);
+    const uint32_t box[3] = {kbox, static_cast<uint32_t>(pair ? bn / 2 : bn), 1};
+    rc = encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, W2, dims, strides, box, ksw);
     if (rc) return rc;
   }
   int f = (flags & KF_GEMM_ROUND_TF32) | KF_GEMM_TMA_OUT;
@@ -1112,7 +1306,33 @@ extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
   float* Cf = static_cast<float*>(C);
+  if (pair) {
+    if (bn == 128)
+      return epilogue == KF_EPI_BIAS
+                 ? launch_gemm_pair<128, KF_EPI_BIAS>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,
+                                                      head_dim, head_stride, live_tiles,
+                                                      live_count, st)
+                 : launch_gemm_pair<128, KF_EPI_BIAS_GELU>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,
+                                                           head_dim, head_stride, live_tiles,
+                                                           live_count, st);
+    return epilogue == KF_EPI_BIAS
+               ? launch_gemm_pair<256, KF_EPI_BIAS>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,
+                                                    head_dim, head_stride, live_tiles, live_count,
+                                                    st)
+               : launch_gemm_pair<256, KF_EPI_BIAS_GELU>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,
+                                                         head_dim, head_stride, live_tiles,
+                                                         live_count, st);
+  }
 #define KF_GEMM_PRE_CASE(BNV)                                                                  \
+  if (bn == BNV && k32) {                                                                      \
+    if (epilogue == KF_EPI_BIAS)                                                               \
+      return launch_gemm<BNV, KF_EPI_BIAS, 4>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,          \
+                                              head_dim, head_stride, live_tiles, live_count,   \
+                                              st);                                             \
+    return launch_gemm<BNV, KF_EPI_BIAS_GELU, 4>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,       \
+                                                 head_dim, head_stride, live_tiles,            \
+                                                 live_count, st);                              \
+  }                                                                                            \
   if (bn == BNV) {                                                                             \
     if (epilogue == KF_EPI_BIAS)                                                               \
       return launch_gemm<BNV, KF_EPI_BIAS, 3>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,          \

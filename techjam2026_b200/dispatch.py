@@ -63,6 +63,21 @@ class Plan:
     bn_out: int = 0
     bn_ffn1: int = 0
     bn_ffn2: int = 0
+    # k block of each bf16x3 GEMM's shared-memory stages: 64 bf16 (128-byte
+    # rows) or 32 (64-byte rows, twice as many half-size stages in flight).
+    # Same MMA order either way, so the output is bit-identical.
+    kb_qkv: int = 64
+    kb_out: int = 64
+    kb_ffn1: int = 64
+    kb_ffn2: int = 64
+    # bf16x3 GEMM on CTA pairs (tcgen05 cta_group::2, 256 x bn tiles, bn 128
+    # or 256): each SM stages half of B, which relieves shared-memory
+    # bandwidth on large GEMMs (c3b/c4: 9-18% faster per GEMM at bn 256);
+    # on small ones (c2) the coarser tiles lose. Bit-identical output.
+    pair_qkv: bool = False
+    pair_out: bool = False
+    pair_ffn1: bool = False
+    pair_ffn2: bool = False
 
     def gemm_precisions(self) -> dict:
         return {"qkv": self.prec_qkv, "out": self.prec_out, "ffn1": self.prec_ffn1,
@@ -88,6 +103,12 @@ class Plan:
         tiles = (self.bn_qkv, self.bn_out, self.bn_ffn1, self.bn_ffn2)
         if any(tiles):
             bits.append("bn=" + "/".join(str(t or "auto") for t in tiles))
+        kbs = (self.kb_qkv, self.kb_out, self.kb_ffn1, self.kb_ffn2)
+        if any(k != 64 for k in kbs):
+            bits.append("kb=" + "/".join(str(k) for k in kbs))
+        pairs = (self.pair_qkv, self.pair_out, self.pair_ffn1, self.pair_ffn2)
+        if any(pairs):
+            bits.append("cta-pair=" + "/".join("y" if p else "n" for p in pairs))
         return " ".join(bits)
 
 

@@ -264,6 +264,10 @@ class FusedTransformer(LayerStack):
 
         def gemm(kind, g, A, lda, W, bias, C, ldc, N, K, epi, flags, bn, hd_=0, hs_=0):
             if split[g]:
+                if getattr(plan, f"kb_{g}") == 32:
+                    flags |= _lib.KF_GEMM_K32
+                if getattr(plan, f"pair_{g}") and bn in (128, 256):
+                    flags |= _lib.KF_GEMM_PAIR
                 run(kind, L.kf_gemm_bf16x3, A, lda, W.data_ptr(), K, bias.data_ptr(), C, ldc,
                     M, N, K, epi, flags, bn, hd_, hs_, lt, lc, st)
             else:

@@ -7,10 +7,11 @@ For one BASELINE configuration, on the current GPU:
 1. Build the forward with the table's current plan for that shape and keep
    its output on a seeded input as the reference.
 2. For each GEMM of the layer (qkv, out, ffn1, ffn2) and each N tile the
-   kernels offer, build the forward with only that tile changed. The gate:
-   its output must be bit-identical to the reference (an N tile only decides
-   which CTA computes an output element, never the order of its
-   accumulation), so a candidate that changes any bit is rejected as a bug.
+   kernels offer (one CTA, or a CTA pair for bf16x3 at 128/256), build the
+   forward with only that choice changed. The gate: its output must be
+   bit-identical to the reference (a tile only decides which CTA computes an
+   output element, never the order of its accumulation), so a candidate
+   that changes any bit is rejected as a bug.
 3. Time every surviving candidate as a CUDA-graph replay (median of
    `--repeats`, L2 flushed before each), keep the fastest tile per GEMM, and
    confirm the combined plan against the reference and the current plan.
@@ -39,6 +40,16 @@ from .fused import FusedTransformer
 
 GEMMS = ("qkv", "out", "ffn1", "ffn2")
 TILES = {"bf16x3": (64, 96, 128, 256), "3xtf32": (64, 128, 256), "tf32": (64, 128, 256)}
+# bf16x3 GEMMs also run as 256 x bn tiles on CTA pairs for these N tiles.
+PAIR_TILES = (128, 256)
+
+
+def candidates(prec: str) -> List[Tuple[int, bool]]:
+    """(N tile, CTA pair) choices of one GEMM; none of them changes a bit."""
+    out = [(bn, False) for bn in TILES[prec]]
+    if prec == "bf16x3":
+        out += [(bn, True) for bn in PAIR_TILES]
+    return out
 
 
 def _forward(cfg, sd, plan: Plan, x, mask) -> Tuple[FusedTransformer, torch.Tensor]:
@@ -92,11 +103,11 @@ def tune(name: str, repeats: int = 10, seed: int = 0, log=print) -> Dict:
     best = {}
     results: List[dict] = []
     for g in GEMMS:
-        field = f"bn_{g}"
+        field, pfield = f"bn_{g}", f"pair_{g}"
         prec = getattr(base, f"prec_{g}")
         timed = []
-        for bn in TILES[prec]:
-            cand = dataclasses.replace(base, **{field: bn})
+        for bn, pair in candidates(prec):
+            cand = dataclasses.replace(base, **{field: bn, pfield: pair})
             model, out = _forward(cfg, sd, cand, x, mask)
             exact = torch.equal(out, ref)
             t = _time(model, x, mask, repeats, flush) if exact else float("inf")
@@ -104,11 +115,16 @@ def tune(name: str, repeats: int = 10, seed: int = 0, log=print) -> Dict:
             del model, out
             gc.collect()
             torch.cuda.empty_cache()
-            results.append({"gemm": g, "bn": bn, "ms": t, "bit_exact": exact})
-            log(f"  {g:5s} bn={bn:3d}: {'%.3f ms' % t if exact else 'REJECTED (output differs)'}")
+            results.append({"gemm": g, "bn": bn, "pair": pair, "ms": t, "bit_exact": exact})
+            tag = f"bn={bn:3d}{' pair' if pair else '     '}"
+            log(f"  {g:5s} {tag}: {'%.3f ms' % t if exact else 'REJECTED (output differs)'}")
             if exact:
-                timed.append((t, bn))
-        best[field] = min(timed)[1] if timed else getattr(base, field)
+                timed.append((t, bn, pair))
+        if timed:
+            _, bn_best, pair_best = min(timed)
+            best[field], best[pfield] = bn_best, pair_best
+        else:
+            best[field], best[pfield] = getattr(base, field), getattr(base, pfield)
     tuned = dataclasses.replace(base, **best)
     model, out = _forward(cfg, sd, tuned, x, mask)
     exact = torch.equal(out, ref)

@@ -107,3 +107,25 @@ def test_tune_write_entry_updates_exact_signature(tmp_path, monkeypatch):
                       "base_ms": 2.0})
     plan, src = dispatch.DispatchTable.load().lookup("sm_100", torch.float32, odd)
     assert src == "exact" and plan.bn_ffn2 == 64
+
+
+def test_tune_candidates_include_cta_pairs_for_bf16x3_only():
+    from techjam2026_b200 import tune
+    bf = tune.candidates("bf16x3")
+    assert (256, True) in bf and (128, True) in bf and (96, False) in bf
+    assert all(not pair for _, pair in tune.candidates("tf32"))
+    assert all(bn in (128, 256) for bn, pair in bf if pair)
+
+
+def test_plan_pair_fields_round_trip_and_describe():
+    import dataclasses
+    from techjam2026_b200.dispatch import DEFAULT_PLAN, Entry, Plan
+    p = dataclasses.replace(DEFAULT_PLAN, bn_qkv=256, pair_qkv=True)
+    e = Entry("sig", "float32", "sm_100", p, "note")
+    assert Entry.from_json(e.to_json()).plan == p
+    assert "cta-pair=y/n/n/n" in p.describe()
+    # entries written before the pair fields existed still load
+    d = dataclasses.asdict(DEFAULT_PLAN)
+    for k in ("pair_qkv", "pair_out", "pair_ffn1", "pair_ffn2"):
+        d.pop(k)
+    assert Plan(**d).pair_qkv is False

@@ -382,6 +382,104 @@ def test_gemm_bf16x3_presplit(M, N, K, bn, gelu, out_split):
     assert err < 6e-4, f"max abs err {err}"
 
 
+@pytest.mark.parametrize("M,N,K", [(128, 64, 64), (517, 384, 512), (300, 200, 136),
+                                   (256, 256, 24), (2048, 512, 2048), (1000, 1024, 1000)])
+@pytest.mark.parametrize("bn", [64, 96, 128, 256])
+@pytest.mark.parametrize("gelu,out_split", [(False, False), (True, True)])
+def test_gemm_bf16x3_k32_bit_identical(M, N, K, bn, gelu, out_split):
+    """KF_GEMM_K32 (32-wide k blocks, 64-byte swizzle) issues the same MMAs in
+    the same order as the 64-wide blocks: every output bit agrees, including
+    a ragged last k block (K % 32 != 0) and K below one block."""
+    from techjam2026_b200 import _lib
+    torch.manual_seed(M * 7 + N + K + bn)
+    a = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / math.sqrt(K)
+    bias = torch.randn(N, device="cuda")
+    a2, w2 = to_planes(a).contiguous(), to_planes(w).contiguous()
+    outs = []
+    for k32 in (False, True):
+        shape = (2, M, N) if out_split else (M, N)
+        c = torch.full(shape, 3, dtype=torch.int16 if out_split else torch.float32, device="cuda")
+        flags = (_lib.KF_GEMM_OUT_BF16X2 if out_split else 0) | (_lib.KF_GEMM_K32 if k32 else 0)
+        rc = _lib.lib().kf_gemm_bf16x3(a2.data_ptr(), K, w2.data_ptr(), K, bias.data_ptr(),
+                                       c.data_ptr(), N, M, N, K, 1 if gelu else 0, flags, bn, 0,
+                                       0, None, None, _lib.stream_ptr())
+        _lib.check(rc, "kf_gemm_bf16x3")
+        outs.append(c)
+    assert torch.equal(outs[0], outs[1])
+    got = from_planes(outs[1]) if out_split else outs[1]
+    ref = a.double() @ w.double().t() + bias.double()
+    if gelu:
+        ref = F.gelu(ref, approximate="none")
+    assert (got.double() - ref).abs().max().item() < 6e-4
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (517, 384, 512), (300, 200, 136),
+                                   (1000, 1024, 1000), (4096, 2048, 512), (2048, 512, 2048)])
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("gelu,out_split", [(False, False), (True, True)])
+@pytest.mark.parametrize("live", [False, True])
+def test_gemm_bf16x3_pair_bit_identical(M, N, K, bn, gelu, out_split, live):
+    """KF_GEMM_PAIR (256 x bn tiles on CTA pairs, cta_group::2) gives the same
+    bits as the one-CTA kernel: same products, same order. Covers an odd
+    number of row tiles (the last pair's second CTA stores nothing), N and K
+    not multiples of the tile, and a live-tile list with gaps (rows of the
+    other tiles keep their contents)."""
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    torch.manual_seed(M * 3 + N + K + bn)
+    a = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / math.sqrt(K)
+    bias = torch.randn(N, device="cuda")
+    a2, w2 = to_planes(a).contiguous(), to_planes(w).contiguous()
+    lt = lc = None
+    n_rt = (M + 127) // 128
+    if live:
+        keep = torch.zeros(M, dtype=torch.uint8, device="cuda")
+        for t in range(0, n_rt, 3):  # tiles 0, 3, 6, ... live
+            keep[t * 128] = 1
+        lt = torch.empty(n_rt, dtype=torch.int32, device="cuda")
+        lc = torch.zeros(1, dtype=torch.int32, device="cuda")
+        _lib.check(L.kf_live_row_tiles(keep.data_ptr(), M, lt.data_ptr(), lc.data_ptr(),
+                                       _lib.stream_ptr()), "live tiles")
+    outs = []
+    for pair in (False, True):
+        shape = (2, M, N) if out_split else (M, N)
+        c = torch.full(shape, 3, dtype=torch.int16 if out_split else torch.float32, device="cuda")
+        flags = (_lib.KF_GEMM_OUT_BF16X2 if out_split else 0) | (_lib.KF_GEMM_PAIR if pair else 0)
+        rc = L.kf_gemm_bf16x3(a2.data_ptr(), K, w2.data_ptr(), K, bias.data_ptr(), c.data_ptr(), N,
+                              M, N, K, 1 if gelu else 0, flags, bn, 0, 0,
+                              lt.data_ptr() if live else None, lc.data_ptr() if live else None,
+                              _lib.stream_ptr())
+        _lib.check(rc, "kf_gemm_bf16x3")
+        outs.append(c)
+    assert torch.equal(outs[0], outs[1])
+    assert L.kf_device_status(0) == 0
+    got = from_planes(outs[1]) if out_split else outs[1]
+    ref = a.double() @ w.double().t() + bias.double()
+    if gelu:
+        ref = F.gelu(ref, approximate="none")
+    rows = torch.arange(M, device="cuda")
+    computed = ((rows // 128) % 3 == 0) if live else torch.ones(M, dtype=torch.bool, device="cuda")
+    assert (got[computed].double() - ref[computed]).abs().max().item() < 6e-4
+    if live:
+        untouched = outs[1][:, ~computed] if out_split else outs[1][~computed]
+        assert torch.all(untouched == 3)
+
+
+def test_gemm_bf16x3_pair_rejects_bad_tiles():
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    a2 = torch.zeros(2, 128, 64, dtype=torch.int16, device="cuda")
+    w2 = torch.zeros(2, 64, 64, dtype=torch.int16, device="cuda")
+    c = torch.zeros(128, 64, device="cuda")
+    for bn, extra in ((64, 0), (96, 0), (128, _lib.KF_GEMM_K32)):
+        rc = L.kf_gemm_bf16x3(a2.data_ptr(), 64, w2.data_ptr(), 64, None, c.data_ptr(), 64, 128,
+                              64, 64, 0, _lib.KF_GEMM_PAIR | extra, bn, 0, 0, None, None,
+                              _lib.stream_ptr())
+        assert rc == _lib.KF_E_INVALID
+
+
 def test_gemm_bf16x3_head_padded_output():
     from techjam2026_b200 import _lib
     torch.manual_seed(11)
