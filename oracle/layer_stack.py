@@ -72,7 +72,7 @@ def attention(h: torch.Tensor, params: Params, prefix: str, num_heads: int,
     k = k.view(B, S, num_heads, Dh).transpose(1, 2)
     v = v.view(B, S, num_heads, Dh).transpose(1, 2)
     chunk = query_chunk or S
-    ctx = torch.empty(B, num_heads, S, Dh, dtype=dtype)
+    ctx = torch.empty(B, num_heads, S, Dh, dtype=dtype, device=h.device)
     for b in range(B):
         kb, vb = k[b], v[b]
         key_ok = None if valid_token_mask is None else valid_token_mask[b]
@@ -80,13 +80,13 @@ def attention(h: torch.Tensor, params: Params, prefix: str, num_heads: int,
             i1 = min(S, i0 + chunk)
             scores = torch.matmul(q[b, :, i0:i1], kb.transpose(-2, -1)) * scale
             if causal:
-                qi = torch.arange(i0, i1)[:, None]
-                kj = torch.arange(S)[None, :]
+                qi = torch.arange(i0, i1, device=h.device)[:, None]
+                kj = torch.arange(S, device=h.device)[None, :]
                 scores = scores.masked_fill(kj > qi, float("-inf"))
             if key_ok is not None:
                 scores = scores.masked_fill(~key_ok[None, None, :], float("-inf"))
-            probs = torch.softmax(scores.to(torch.float32 if dtype == torch.float32 else dtype),
-                                  dim=-1).to(dtype)
+            # softmax in fp32 whatever the I/O dtype (torch_transformer_benchmark.py:110-111)
+            probs = torch.softmax(scores.float(), dim=-1).to(dtype)
             ctx[b, :, i0:i1] = torch.matmul(probs, vb)
     ctx = ctx.transpose(1, 2).reshape(B, S, d)
     out = _linear(ctx, params, prefix + ".out_proj", dtype)

@@ -6,6 +6,9 @@ Same contract as the reference's submission.py:40-106:
   * picks a plan from the sm_100 dispatch table on the first forward (which
     falls inside the harness's warm-up) and runs the CUDA path
     (techjam2026_b200.fused.FusedTransformer, whole forward in one CUDA graph);
+    at float16/bfloat16 I/O the plan is the organiser's own layer captured
+    whole into one CUDA graph (techjam2026_b200.exact: the gate admits only
+    its exact arithmetic there, as the reference's own table records);
   * if choosing or running the CUDA path raises, it says so on stdout and
     returns the organiser's baseline answer from then on (sticky), because the
     harness's accuracy gate is a hard failure. Nothing is silent.
@@ -35,6 +38,7 @@ except Exception:  # standalone: parameter container with the same tree
     HAS_ORGANISER_BASELINE = False
 
 from techjam2026_b200.dispatch import DispatchTable, Plan, probe
+from techjam2026_b200.exact import ExactGraphForward
 from techjam2026_b200.fused import FusedTransformer
 
 _VERBOSE = os.environ.get("KF_VERBOSE", "") not in ("", "0")
@@ -45,7 +49,7 @@ class UserOptimizedTransformer(BaselineTransformer):
 
     def __init__(self, config) -> None:
         super().__init__(config)
-        self._impl: Optional[FusedTransformer] = None
+        self._impl = None  # FusedTransformer, or ExactGraphForward (fp16/bf16)
         self._plan: Optional[Plan] = None
         self._source = "uninitialized"
         self._failed = False
@@ -59,9 +63,19 @@ class UserOptimizedTransformer(BaselineTransformer):
             spec = probe(x.device.index)
             plan, source = DispatchTable.load_for(spec).lookup(
                 spec.arch, x.dtype, self.config, spec.shared_mem_per_block_kb)
-            impl = FusedTransformer(self.config, plan)
-            impl.load_state_dict(self.state_dict(), strict=True)
-            impl.eval()
+            if plan.exact_reference:
+                # float16 / bfloat16: the organiser's own layer, whole forward
+                # in one CUDA graph (bit-identical to its eager forward).
+                if not HAS_ORGANISER_BASELINE:
+                    raise RuntimeError(
+                        f"{x.dtype} I/O runs the organiser's exact layer, and "
+                        "torch_transformer_benchmark is not importable")
+                base_forward = super().forward
+                impl = ExactGraphForward(lambda xx, mm: base_forward(xx, mm))
+            else:
+                impl = FusedTransformer(self.config, plan)
+                impl.load_state_dict(self.state_dict(), strict=True)
+                impl.eval()
             self._impl, self._plan, self._source = impl, plan, source
             if _VERBOSE:
                 print(f"[kf-b200] {spec.arch} {x.dtype} -> {plan.name} ({source}): "

@@ -7,8 +7,9 @@
 //               frees (K once S = QK^T is done, V after O += PV);
 //   warp 1      MMA issuer and TMEM owner. TMEM holds three S buffers (BN fp32
 //               columns each) and the O accumulator (DH columns). S_j = Q K_j^T
-//               is issued right after O += P_{j-2} V_{j-2}, a whole softmax
-//               pass before it is needed, and O += P_j V_j
+//               is issued as soon as O += P_{j-3} V_{j-3} has been (its buffer
+//               is then free), two softmax passes before it is needed; then
+//               O += P_{j-2} V_{j-2}, which waits for that softmax. O += P_j V_j
 //               reads P straight from TMEM (tcgen05.mma A operand in TMEM), so
 //               P never touches shared memory;
 //   warps 2-5   softmax: one thread per query row (TMEM lane). Reads its S row,
@@ -378,14 +379,11 @@ __global__ void __launch_bounds__(192, MINB)
       };
       for (int j = 0; j < kv_end && ok; ++j) {
         if (!kv_tile_live<BN>(kb, words, j, S)) continue;
-        // P V of tile it - (NSB - 1) first: it waits only for that tile's
-        // softmax, never for the K load of tile it, and it frees the S buffer
-        // that S_it overwrites (the pipe runs in issue order). S_it is then
-        // issued a whole softmax pass before it is needed.
-        if (it >= Cfg::NSB - 1 && !issue_pv(it - (Cfg::NSB - 1))) {
-          ok = false;
-          break;
-        }
+        // S_it first: its buffer (it % NSB) last held P of tile it - NSB,
+        // whose P V was issued in an earlier iteration, and the pipe runs in
+        // issue order, so S_it needs no wait on any softmax. It goes out as
+        // soon as P V of tile it - NSB has, i.e. NSB - 1 softmax passes
+        // before the softmax needs it.
         if (!mbar_wait(&k_full[ks], kph, abort_flag, KF_DEV_WAIT_TIMEOUT_MMA)) {
           ok = false;
           break;
@@ -409,8 +407,14 @@ __global__ void __launch_bounds__(192, MINB)
           kph ^= 1u;
         }
         ++it;
+        // Then P V of tile it - NSB (counting the S just issued): it waits
+        // for that tile's softmax only.
+        if (it >= Cfg::NSB && !issue_pv(it - Cfg::NSB)) {
+          ok = false;
+          break;
+        }
       }
-      for (int i = (it > Cfg::NSB - 1 ? it - (Cfg::NSB - 1) : 0); ok && i < it; ++i)
+      for (int i = (it >= Cfg::NSB ? it - Cfg::NSB + 1 : 0); ok && i < it; ++i)
         ok = issue_pv(i);
       if (ok && it > 0) mma_commit(o_final);
       mma_commit(drain);
@@ -437,9 +441,14 @@ __global__ void __launch_bounds__(192, MINB)
       }
       tc_fence_after();
       float s[BN];
+      // One TMEM round trip for the row's BN scores (x64 form when BN == 64).
+      if constexpr (BN == 64) {
+        tmem_ld64(t_row + sb * BN, s);
+      } else {
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c)
-        tmem_ld32(t_row + sb * BN + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+        for (int c = 0; c < BN / 32; ++c)
+          tmem_ld32(t_row + sb * BN + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+      }
 
       const int k0 = j * BN;
       uint32_t kw[BN / 32];
@@ -498,10 +507,11 @@ __global__ void __launch_bounds__(192, MINB)
       l_run += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       if (__any_sync(0xffffffffu, rescale_o)) {
         // O += P_{it-1} V_{it-1} must have landed before this row is rescaled.
-        // The s_full arrival just observed implies PV_{it-2} is complete (the
+        // The s_full arrival just observed implies PV_{it-3} is complete (the
         // MMA pipe completes in issue order and S_it was issued after it).
-        // o_done[(it-1) & 1] counts the products of that parity, so it is at
-        // most one phase (PV_{it-1} itself) behind and the parity wait is exact.
+        // o_done[(it-1) & 1] counts the products of that parity (PV_{it-3},
+        // PV_{it-1}, ...), so it is at most one phase (PV_{it-1} itself)
+        // behind and the parity wait is exact.
         if (!mbar_wait(&o_done[(it - 1) & 1], static_cast<uint32_t>(((it - 1) >> 1) & 1),
                        abort_flag, KF_DEV_WAIT_TIMEOUT_SOFTMAX)) {
           ok = false;
@@ -519,9 +529,13 @@ __global__ void __launch_bounds__(192, MINB)
           tmem_st32(t_row + Cfg::O_COL + c * 32, o);
         }
       }
+      if constexpr (BN == 64) {
+        tmem_st64(t_row + sb * BN, s);
+      } else {
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c)
-        tmem_st32(t_row + sb * BN + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+        for (int c = 0; c < BN / 32; ++c)
+          tmem_st32(t_row + sb * BN + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);

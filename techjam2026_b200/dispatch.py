@@ -79,6 +79,12 @@ class Plan:
     pair_ffn1: bool = False
     pair_ffn2: bool = False
 
+    # Narrow I/O dtypes (float16/bfloat16): run the organiser's own layer,
+    # captured whole into one CUDA graph, instead of these kernels. At those
+    # dtypes the gate only admits the reference's exact arithmetic
+    # (techjam2026_b200/exact.py); never set for float32.
+    exact_reference: bool = False
+
     def gemm_precisions(self) -> dict:
         return {"qkv": self.prec_qkv, "out": self.prec_out, "ffn1": self.prec_ffn1,
                 "ffn2": self.prec_ffn2}
@@ -98,6 +104,8 @@ class Plan:
             bits.append("skip-padded-rows")
         if self.fuse_ln:
             bits.append("ln-in-gemm")
+        if self.exact_reference:
+            return "exact-reference+cuda-graph"
         if self.cuda_graph:
             bits.append("cuda-graph")
         tiles = (self.bn_qkv, self.bn_out, self.bn_ffn1, self.bn_ffn2)
@@ -113,6 +121,8 @@ class Plan:
 
 
 DEFAULT_PLAN = Plan()
+# float16 / bfloat16 I/O: the reference's own forward in one CUDA graph.
+EXACT_PLAN = Plan(name="exact-reference+graph", exact_reference=True)
 # For shapes never measured: same arithmetic, automatic tiles.
 CONSERVATIVE_PLAN = dataclasses.replace(DEFAULT_PLAN, name=DEFAULT_PLAN.name + "(auto-tiles)")
 
@@ -176,8 +186,12 @@ class DispatchTable:
         if a != "sm_100":
             raise RuntimeError(f"no kernels for {arch}: this build targets sm_100a only")
         dt = str(dtype).replace("torch.", "")
+        if dt in ("float16", "bfloat16"):
+            # The gate admits only the reference's exact arithmetic there
+            # (the reference's own table ships exact plans for these dtypes).
+            return EXACT_PLAN, "exact-dtype"
         if dt != "float32":
-            raise RuntimeError(f"I/O dtype {dt} is not implemented (float32 only)")
+            raise RuntimeError(f"I/O dtype {dt} is not implemented")
         hit = self._index.get((a, dt, signature(cfg)))
         if hit is not None:
             return hit.plan, "exact"

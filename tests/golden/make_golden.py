@@ -37,7 +37,11 @@ CASES = {
     "mini_s333": (2, 333, 64, 4, 128, 2, True, 0.5, 7),
     "mini_dh8_noncausal": (3, 40, 32, 4, 64, 2, False, 0.6, 5),
     "mini_nopad": (2, 96, 64, 2, 128, 2, True, 0.0, 11),
+    # bfloat16 I/O: the reference module cast to bf16, inputs drawn in bf16
+    # (the harness's --dtype bfloat16), output in bf16.
+    "mini_bf16": (2, 96, 64, 2, 128, 2, True, 0.5, 13),
 }
+DTYPES = {"mini_bf16": torch.bfloat16}
 
 
 def x_checksum(x: torch.Tensor) -> str:
@@ -50,20 +54,27 @@ def main() -> None:
     import torch_transformer_benchmark as ref
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    only = set(sys.argv[1:])  # optional case names: regenerate just those
     for name, (B, S, d, H, F, L, causal, pad, seed) in CASES.items():
+        if only and name not in only:
+            continue
+        dtype = DTYPES.get(name, torch.float32)
         cfg = ref.TransformerConfig(B, S, d, H, F, L, causal)
-        model = init_params_(ref.BaselineTransformer(cfg), seed).eval()
-        x, mask = ref.generate_random_case(cfg, torch.device("cpu"), torch.float32, seed,
-                                           pad, 1.0)
+        model = init_params_(ref.BaselineTransformer(cfg), seed).eval().to(dtype)
+        x, mask = ref.generate_random_case(cfg, torch.device("cpu"), dtype, seed, pad, 1.0)
         with torch.inference_mode():
             out = model(x, mask)
         blob = {"config": [B, S, d, H, F, L, causal], "seed": seed, "padding_ratio": pad,
                 "state_dict": {k: v.clone() for k, v in model.state_dict().items()},
                 "x": x.clone(), "mask": mask.clone(), "out": out.clone()}
+        if dtype != torch.float32:
+            blob["dtype"] = str(dtype).replace("torch.", "")
         path = os.path.join(HERE, f"golden_{name}.pt")
         torch.save(blob, path)
         print(f"{name}: out[{tuple(out.shape)}] -> {path} ({os.path.getsize(path)} bytes)")
 
+    if only:
+        return
     inputs = {}
     for wname, w in WORKLOADS.items():
         cfg = ref.TransformerConfig(**{f: getattr(w.cfg, f) for f in (

@@ -40,7 +40,20 @@ def test_other_arches_and_dtypes_are_refused():
     with pytest.raises(RuntimeError):
         DispatchTable([]).lookup("sm_90", torch.float32, cfg)
     with pytest.raises(RuntimeError):
-        DispatchTable([]).lookup("sm_100", torch.float16, cfg)
+        DispatchTable([]).lookup("sm_100", torch.float64, cfg)
+
+
+def test_narrow_dtypes_get_the_exact_reference_plan():
+    """fp16/bf16 I/O: only the reference's exact arithmetic passes the gate,
+    so every shape maps to the exact-reference graph plan."""
+    from techjam2026_b200.dispatch import EXACT_PLAN
+    cfg = TransformerConfig(2, 64, 128, 4, 512, 1, True)
+    for dt in (torch.float16, torch.bfloat16):
+        plan, src = DispatchTable.load().lookup("sm_100", dt, cfg)
+        assert plan is EXACT_PLAN and src == "exact-dtype" and plan.exact_reference
+        assert plan.describe() == "exact-reference+cuda-graph"
+    plan, _ = DispatchTable.load().lookup("sm_100", torch.float32, cfg)
+    assert not plan.exact_reference
 
 
 def test_table_round_trips(tmp_path, monkeypatch):

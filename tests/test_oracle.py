@@ -102,3 +102,19 @@ def test_mask_is_a_prefix_and_padded_x_is_zero():
         n = int(mask[b].sum())
         assert bool(mask[b, :n].all()) and not bool(mask[b, n:].any())
         assert torch.count_nonzero(x[b, n:]) == 0
+
+
+def test_oracle_matches_reference_at_bfloat16_io():
+    """bf16 I/O (the harness's --dtype bfloat16): the reference module cast to
+    bf16 on bf16 inputs. The oracle restates the same ops in the same order
+    (softmax in fp32, every other result rounded to bf16)."""
+    case = load_case("mini_bf16")
+    cfg = case["cfg"]
+    assert case["dtype"] == "bfloat16" and case["x"].dtype == torch.bfloat16
+    out = oracle.forward(case["state_dict"], cfg.num_layers, cfg.num_heads, case["x"],
+                         case["mask"], causal=cfg.causal, dtype=torch.bfloat16)
+    assert out.dtype == torch.bfloat16
+    diff = (out.float() - case["out"].float()).abs().max().item()
+    # Same CPU ops in the same order; a bf16 ulp at |x| ~ 4 is 2^-5.
+    assert diff <= 2 ** -5, diff
+    assert torch.count_nonzero(out[~case["mask"]]) == 0
