@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import dataclasses
 import json
+import math
 import os
 from typing import Dict, List, Optional, Tuple
 
@@ -192,10 +193,24 @@ class DispatchTable:
             return EXACT_PLAN, "exact-dtype"
         if dt != "float32":
             raise RuntimeError(f"I/O dtype {dt} is not implemented")
-        hit = self._index.get((a, dt, signature(cfg)))
+        sig = signature(cfg)
+        hit = self._index.get((a, dt, sig))
         if hit is not None:
             return hit.plan, "exact"
-        if any(_norm_arch(e.arch) == a and e.dtype == dt for e in self.entries):
+        same_arch = [e for e in self.entries if _norm_arch(e.arch) == a and e.dtype == dt]
+        if same_arch:
+            # Nearest: the same layer shape at another batch size (a batch
+            # slice, or one rank's shard of a multi-GPU batch) keeps the
+            # measured plan of the closest batch; any other shape gets the
+            # same arithmetic with tiles chosen at launch.
+            rest = sig.split("-", 1)[1]
+            same_layer = [e for e in same_arch if e.signature.split("-", 1)[1] == rest]
+            if same_layer:
+                B = max(1, cfg.batch_size)
+                best = min(same_layer,
+                           key=lambda e: abs(math.log(max(1, int(e.signature.split("-", 1)[0][1:]))) -
+                                             math.log(B)))
+                return best.plan, "nearest"
             return CONSERVATIVE_PLAN, "nearest"
         return DEFAULT_PLAN, "default"
 

@@ -35,6 +35,29 @@ def test_lookup_order():
     assert DispatchTable([]).lookup("sm_100", torch.float32, other) == (DEFAULT_PLAN, "default")
 
 
+def test_nearest_keeps_the_plan_of_the_same_layer_at_the_closest_batch():
+    """A batch slice or one rank's shard of a configuration keeps that
+    configuration's measured plan; another layer shape does not."""
+    big = Plan(name="b16", bn_qkv=256, pair_qkv=True)
+    small = Plan(name="b2", bn_qkv=128)
+    t = DispatchTable([
+        Entry(signature(TransformerConfig(16, 1024, 1024, 4, 4096, 2, True)), "float32", "sm_100", big),
+        Entry(signature(TransformerConfig(2, 1024, 1024, 4, 4096, 2, True)), "float32", "sm_100", small),
+    ])
+    for B, want in ((8, big), (32, big), (4, small), (1, small)):
+        cfg = TransformerConfig(B, 1024, 1024, 4, 4096, 2, True)
+        assert t.lookup("sm_100", torch.float32, cfg) == (want, "nearest"), B
+    other = TransformerConfig(8, 1024, 1024, 4, 4096, 2, False)      # not causal
+    assert t.lookup("sm_100", torch.float32, other) == (CONSERVATIVE_PLAN, "nearest")
+    # the shipped table: one c5 shard (2 sequences) keeps the c5 plan
+    from techjam2026_b200.configs import WORKLOADS
+    import dataclasses
+    c5 = WORKLOADS["c5"].cfg
+    shipped = DispatchTable.load()
+    assert shipped.lookup("sm_100", torch.float32, dataclasses.replace(c5, batch_size=2))[0] == \
+        shipped.lookup("sm_100", torch.float32, c5)[0]
+
+
 def test_other_arches_and_dtypes_are_refused():
     cfg = TransformerConfig(2, 64, 128, 4, 512, 1, True)
     with pytest.raises(RuntimeError):
