@@ -84,7 +84,10 @@ struct GemmCfg {
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = EPI_OFF + 2 * EPI_BUF_BYTES;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = BAR_OFF + BAR_BYTES + 1024;
+  // The tile's bias columns, staged by the epilogue before it waits for the
+  // accumulator (off the critical path of the tile's epilogue).
+  static constexpr int BIAS_OFF = BAR_OFF + BAR_BYTES;
+  static constexpr int SMEM_BYTES = BIAS_OFF + BN * 4 + 1024;
   static_assert(BN == 64 || BN == 96 || BN == 128 || BN == 256, "BN");
   static_assert(STAGES >= 2 && STAGES <= 8, "stages");
   static_assert(SMEM_BYTES <= 232448, "smem");
@@ -779,12 +782,22 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
     const bool leader = threadIdx.x == 64 + 128 * half;
     const bool rnd = (flags & KF_GEMM_ROUND_TF32) != 0;
     uint8_t* buf = smem + Cfg::EPI_OFF + half * Cfg::EPI_BUF_BYTES;
+    float* sbias = reinterpret_cast<float*>(smem + Cfg::BIAS_OFF);  // [BN], per tile
+    const int ht = threadIdx.x - (64 + 128 * half);                 // 0..127 in the half
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = unit0; tile < num_tiles; tile += ustride) {
       bool own;  // PAIR: false for a repeated row tile (nothing stored)
       const int m0 = row_tile(tile, own);
       const int n0 = (tile % num_n) * BN;
+      // Stage the bias of this half's chunks (columns 32*half + 64*j + 0..31)
+      // while the MMAs of the tile run; 0 past N or without a bias. The
+      // previous tile's readers are past the end-of-tile barrier, and the
+      // barrier after the accumulator wait publishes these writes.
+      if (ht < 32) {
+        for (int c = 32 * half; c < BN; c += 64)
+          sbias[c + ht] = (bias && n0 + c + ht < N) ? __ldg(bias + n0 + c + ht) : 0.f;
+      }
       // One bounded wait by the half's leader, shared through the half's
       // named barrier, so all four warps of a half always reach the same
       // barriers (no warp can be left waiting for one that gave up).
@@ -810,19 +823,14 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
           uint4 hu[4], lu[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {  // 8 columns -> one 16-byte unit per plane
-            const int col = n0 + c + 8 * j;
             float o[8];
-            if (bias && col + 8 <= N) {
-              const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + col));
-              const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + col + 4));
+            {
+              const float4 b0 = *reinterpret_cast<const float4*>(sbias + c + 8 * j);
+              const float4 b1 = *reinterpret_cast<const float4*>(sbias + c + 8 * j + 4);
               o[0] = v[8 * j] + b0.x, o[1] = v[8 * j + 1] + b0.y;
               o[2] = v[8 * j + 2] + b0.z, o[3] = v[8 * j + 3] + b0.w;
               o[4] = v[8 * j + 4] + b1.x, o[5] = v[8 * j + 5] + b1.y;
               o[6] = v[8 * j + 6] + b1.z, o[7] = v[8 * j + 7] + b1.w;
-            } else {
-#pragma unroll
-              for (int t = 0; t < 8; ++t)
-                o[t] = v[8 * j + t] + ((bias && col + t < N) ? __ldg(bias + col + t) : 0.f);
             }
             if (EPI == KF_EPI_BIAS_GELU) {
 #pragma unroll
@@ -860,15 +868,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
           float4 ov[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const int col = n0 + c + 4 * j;
-            float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (bias && col + 4 <= N) {
-              bb = __ldg(reinterpret_cast<const float4*>(bias + col));
-            } else if (bias) {
-              float tb[4] = {0.f, 0.f, 0.f, 0.f};
-              for (int t = 0; t < 4 && col + t < N; ++t) tb[t] = __ldg(bias + col + t);
-              bb = make_float4(tb[0], tb[1], tb[2], tb[3]);
-            }
+            const float4 bb = *reinterpret_cast<const float4*>(sbias + c + 4 * j);
             float4 o = make_float4(v[4 * j] + bb.x, v[4 * j + 1] + bb.y, v[4 * j + 2] + bb.z,
                                    v[4 * j + 3] + bb.w);
             if (EPI == KF_EPI_BIAS_GELU) {
