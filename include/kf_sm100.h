@@ -110,6 +110,10 @@ int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t ldw, const
 #define KF_GEMM_K32 16       /* kf_gemm_bf16x3: stream k blocks of 32 instead of 64
                                 (twice as many half-size stages in flight; same
                                 MMA order, so C is bit-identical) */
+#define KF_GEMM_W_STATIC 64  /* kf_gemm_bf16x3: W was written before the kernel that
+                                precedes this call in the stream started (weights
+                                prepared once), so the first W tiles may be loaded
+                                before waiting for that kernel; one-CTA tiles only */
 #define KF_GEMM_PAIR 32      /* kf_gemm_bf16x3: 256 x bn tiles on CTA pairs
                                 (tcgen05 cta_group::2; bn 128 or 256): each SM
                                 stages its 128 A rows and half of the B rows, so

@@ -79,6 +79,7 @@ KF_ATTN_OUT_BF16X2 = 8
 KF_GEMM_OUT_BF16X2 = 8
 KF_GEMM_K32 = 16
 KF_GEMM_PAIR = 32
+KF_GEMM_W_STATIC = 64
 KF_NOALLOC_KEEP_WORDS_MAX = 262144
 
 _lib = None

@@ -330,6 +330,24 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   // TMEM (a CTA of the next kernel may allocate before its own wait, and must
   // then only ever wait for columns that a running CTA will free).
   pdl_launch_dependents();
+  // KF_GEMM_W_STATIC (the caller guarantees W was written before the
+  // previous kernel in the stream started): the W tiles of the first stages
+  // of this CTA's first tile are loaded before the wait, so they overlap the
+  // previous kernel's tail. Their barriers expect those bytes now and the A
+  // bytes and the arrival later (the phase cannot end in between).
+  int pre_w = 0;
+  if constexpr (Cfg::PRESPLIT && !PAIR && !LNF) {
+    if ((flags & KF_GEMM_W_STATIC) && warp == 0 && lane == 0) {
+      const int nw0 = (static_cast<int>(blockIdx.x) % num_n) * BN;
+      pre_w = num_kb < STAGES ? num_kb : STAGES;
+      for (int s2 = 0; s2 < pre_w; ++s2) {
+        uint8_t* sa = smem + s2 * Cfg::STAGE_BYTES;
+        mbar_expect_tx(&full[s2], 2 * Cfg::B_BYTES);
+        tma_load_3d(sa + Cfg::A_BYTES, &tmB, &full[s2], s2 * BK, nw0, 0);
+        tma_load_3d(sa + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &tmB, &full[s2], s2 * BK, nw0, 1);
+      }
+    }
+  }
   // Everything above overlaps the previous kernel; from here on we read its
   // outputs (the A operand and the live-tile list).
   pdl_wait();
@@ -386,6 +404,11 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
             tma_load_3d_pair(sa + Cfg::A_BYTES, &tmB, fb, kb * BK, n0, 0);
             tma_load_3d_pair(sa + Cfg::A_BYTES + Cfg::B_BYTES, &tmA, fb, kb * BK, m0, 1);
             tma_load_3d_pair(sa + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &tmB, fb, kb * BK, n0, 1);
+          } else if (Cfg::PRESPLIT && issued < pre_w) {
+            // W of this stage went out before the wait: A only, and arrive.
+            mbar_arrive_expect_tx(&full[stage], 2 * Cfg::A_BYTES);
+            tma_load_3d(sa, &tmA, &full[stage], kb * BK, m0, 0);
+            tma_load_3d(sa + Cfg::A_BYTES + Cfg::B_BYTES, &tmA, &full[stage], kb * BK, m0, 1);
           } else if (Cfg::PRESPLIT) {
             // planes: A_hi | B_hi | A_lo | B_lo (3-D maps, plane = coordinate 2)
             mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
@@ -405,6 +428,13 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
             phase ^= 1u;
           }
         }
+      }
+      // Prefetched W stages that never got their A loads (no tile for this
+      // CTA, or an abort): arrive, so the phase ends once the W bytes land,
+      // and wait for that before the shared memory can be released.
+      for (long long s2 = issued; s2 < pre_w; ++s2) {
+        mbar_arrive(&full[s2]);
+        mbar_wait_drain(&full[s2], 0, KF_DEV_WAIT_TIMEOUT_TMA);
       }
       if (PAIR) {
         // Rank 0's MMA thread releases the stages of both CTAs (its commits
@@ -1283,7 +1313,7 @@ extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W
     rc = encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, W2, dims, strides, box, ksw);
     if (rc) return rc;
   }
-  int f = (flags & KF_GEMM_ROUND_TF32) | KF_GEMM_TMA_OUT;
+  int f = (flags & (KF_GEMM_ROUND_TF32 | KF_GEMM_W_STATIC)) | KF_GEMM_TMA_OUT;
   if (head_dim == 0 || (head_dim % 4 == 0 && head_stride % 4 == 0)) f |= KF_GEMM_VEC_OK;
   if (head_dim > 0) {
     f &= ~KF_GEMM_TMA_OUT;  // scatter into head-padded slots: direct stores

@@ -77,6 +77,12 @@ class _Weights:
         self.finw = prep_b(model.final_norm.weight)
         self.finb = prep_b(model.final_norm.bias)
         self.fin_eps = float(model.final_norm.eps)
+        # Once every prepared weight is written, later GEMMs may load their
+        # first W tiles before waiting for the previous kernel
+        # (KF_GEMM_W_STATIC). Not inside a stream capture (no sync there).
+        self.static = not torch.cuda.is_current_stream_capturing()
+        if self.static:
+            torch.cuda.current_stream(device).synchronize()
 
 
 class _Workspace:
@@ -268,6 +274,8 @@ class FusedTransformer(LayerStack):
                     flags |= _lib.KF_GEMM_K32
                 if getattr(plan, f"pair_{g}") and bn in (128, 256):
                     flags |= _lib.KF_GEMM_PAIR
+                elif w.static:
+                    flags |= _lib.KF_GEMM_W_STATIC
                 run(kind, L.kf_gemm_bf16x3, A, lda, W.data_ptr(), K, bias.data_ptr(), C, ldc,
                     M, N, K, epi, flags, bn, hd_, hs_, lt, lc, st)
             else:

@@ -467,6 +467,45 @@ def test_gemm_bf16x3_pair_bit_identical(M, N, K, bn, gelu, out_split, live):
         assert torch.all(untouched == 3)
 
 
+@pytest.mark.parametrize("M,N,K", [(517, 384, 512), (300, 200, 136), (2048, 512, 2048),
+                                   (256, 256, 24)])
+@pytest.mark.parametrize("bn", [64, 96, 128, 256])
+@pytest.mark.parametrize("k32", [False, True])
+@pytest.mark.parametrize("live", [False, True])
+def test_gemm_bf16x3_static_w_prefetch_bit_identical(M, N, K, bn, k32, live):
+    """KF_GEMM_W_STATIC loads the first W stages before waiting for the
+    previous kernel: same bits, including CTAs that end up with no tile (a
+    sparse live-tile list) and so must drain their prefetched stages."""
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    torch.manual_seed(M + 5 * N + K + bn)
+    a = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / math.sqrt(K)
+    bias = torch.randn(N, device="cuda")
+    a2, w2 = to_planes(a).contiguous(), to_planes(w).contiguous()
+    torch.cuda.synchronize()  # W is written before the GEMM's predecessor starts
+    lt = lc = None
+    if live:
+        n_rt = (M + 127) // 128
+        keep = torch.zeros(M, dtype=torch.uint8, device="cuda")
+        keep[(n_rt - 1) * 128] = 1  # only the last row tile is live
+        lt = torch.empty(n_rt, dtype=torch.int32, device="cuda")
+        lc = torch.zeros(1, dtype=torch.int32, device="cuda")
+        _lib.check(L.kf_live_row_tiles(keep.data_ptr(), M, lt.data_ptr(), lc.data_ptr(),
+                                       _lib.stream_ptr()), "live tiles")
+    outs = []
+    for static in (False, True):
+        c = torch.full((M, N), 3.0, device="cuda")
+        flags = (_lib.KF_GEMM_K32 if k32 else 0) | (_lib.KF_GEMM_W_STATIC if static else 0)
+        rc = L.kf_gemm_bf16x3(a2.data_ptr(), K, w2.data_ptr(), K, bias.data_ptr(), c.data_ptr(), N,
+                              M, N, K, 0, flags, bn, 0, 0, lt.data_ptr() if live else None,
+                              lc.data_ptr() if live else None, _lib.stream_ptr())
+        _lib.check(rc, "kf_gemm_bf16x3")
+        outs.append(c)
+    assert torch.equal(outs[0], outs[1])
+    assert L.kf_device_status(0) == 0
+
+
 def test_gemm_bf16x3_pair_rejects_bad_tiles():
     from techjam2026_b200 import _lib
     L = _lib.lib()
