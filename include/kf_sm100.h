@@ -56,6 +56,9 @@ int kf_device_status(int reset);
                                only when every consumer masks those rows) */
 #define KF_LN_OUT_BF16X2 8  /* write h as bf16 hi/lo planes: h_out is then a
                                uint16 [2][M][ldh] buffer (kf_gemm_bf16x3 input) */
+#define KF_LN_STATIC_PARAMS 16 /* keep, w and b were written before the kernel that
+                                  precedes this call in the stream started: they are
+                                  loaded before waiting for that kernel */
 
 /* Fused residual-add + row mask + LayerNorm over rows of width d:
  *     s = keep[r] ? x[r] + y[r] : 0          (y optional, keep optional)

@@ -65,6 +65,7 @@ KF_LN_MASK_OUT = 1
 KF_LN_ROUND_TF32 = 2
 KF_LN_SKIP_PADDED = 4
 KF_LN_OUT_BF16X2 = 8
+KF_LN_STATIC_PARAMS = 16
 KF_EPI_BIAS = 0
 KF_EPI_BIAS_GELU = 1
 KF_GEMM_ROUND_TF32 = 1

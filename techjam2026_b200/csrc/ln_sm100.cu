@@ -34,7 +34,6 @@ __global__ void __launch_bounds__(256) ln_add_mask_vec_kernel(
     float* __restrict__ h_out, int64_t ldh, int64_t M,
     int d, float eps, int flags) {
   pdl_launch_dependents();
-  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= M) return;
@@ -42,13 +41,38 @@ __global__ void __launch_bounds__(256) ln_add_mask_vec_kernel(
   // The kernel is latency-bound (one short row per warp), so every load it
   // needs -- the row's keep byte, x, y and, for rows of up to 1024 floats,
   // gamma and beta -- is issued up front instead of one dependent round trip
-  // after another; a padded row's loads are simply not used.
+  // after another; a padded row's loads are simply not used. With
+  // KF_LN_STATIC_PARAMS (keep, gamma and beta were written before the
+  // previous kernel in the stream started) those go out before the wait on
+  // the previous kernel, and a skipped padded row leaves without waiting.
   constexpr bool PREFETCH_WB = NV <= 8;
   constexpr int NW = PREFETCH_WB ? NV : 1;
-  const bool kept = keep ? (__ldg(keep + row) != 0) : true;
+  const bool early = (flags & KF_LN_STATIC_PARAMS) != 0;
+  float4 gw[NW], gb[NW];
+  bool kept = true;
+  auto load_params = [&]() {
+    kept = keep ? (__ldg(keep + row) != 0) : true;
+    if (PREFETCH_WB) {
+#pragma unroll
+      for (int i = 0; i < NW; ++i) {
+        const int c = lane + 32 * i;
+        gw[i] = gb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c < nv4) {
+          gw[i] = __ldg(reinterpret_cast<const float4*>(w) + c);
+          gb[i] = __ldg(reinterpret_cast<const float4*>(b) + c);
+        }
+      }
+    }
+  };
+  if (early) {
+    load_params();
+    if (!kept && (flags & KF_LN_SKIP_PADDED)) return;  // reads and writes nothing
+  }
+  pdl_wait();
+  if (!early) load_params();
   // Long rows add y as it arrives (registers for two copies would spill).
   constexpr int NT = PREFETCH_WB ? NV : 1;
-  float4 v[NV], t[NT], gw[NW], gb[NW];
+  float4 v[NV], t[NT];
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int c = lane + 32 * i;
@@ -66,17 +90,6 @@ __global__ void __launch_bounds__(256) ln_add_mask_vec_kernel(
           v[i].z += yy.z;
           v[i].w += yy.w;
         }
-      }
-    }
-  }
-  if (PREFETCH_WB) {
-#pragma unroll
-    for (int i = 0; i < NW; ++i) {
-      const int c = lane + 32 * i;
-      gw[i] = gb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (c < nv4) {
-        gw[i] = __ldg(reinterpret_cast<const float4*>(w) + c);
-        gb[i] = __ldg(reinterpret_cast<const float4*>(b) + c);
       }
     }
   }
@@ -156,7 +169,7 @@ __global__ void __launch_bounds__(256) ln_add_mask_scalar_kernel(
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= M) return;
-  const bool kept = keep ? (keep[row] != 0) : true;
+  const bool kept = keep ? (keep[row] != 0) : true;  // (KF_LN_STATIC_PARAMS unused here)
   if (!kept && (flags & KF_LN_SKIP_PADDED)) return;
   auto val = [&](int c) -> float {
     if (!kept) return 0.f;

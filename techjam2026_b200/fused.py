@@ -232,7 +232,11 @@ class FusedTransformer(LayerStack):
         skip_rows = keep_u8 is not None and plan.skip_padded_rows
         lt = ws.live_tiles.data_ptr() if skip_rows else None
         lc = ws.live_count.data_ptr() if skip_rows else None
-        ln_skip = _lib.KF_LN_SKIP_PADDED if skip_rows else 0
+        # keep, gamma and beta are static for the forward (inputs copied and
+        # weights synchronised before it starts): the norms load them before
+        # waiting for the previous kernel.
+        ln_static = _lib.KF_LN_STATIC_PARAMS if w.static else 0
+        ln_skip = (_lib.KF_LN_SKIP_PADDED if skip_rows else 0) | ln_static
 
         # Producer output formats follow their consumer's precision: bf16
         # hi/lo planes for "bf16x3", TF32-rounded fp32 for "tf32" (the tensor
@@ -319,7 +323,7 @@ class FusedTransformer(LayerStack):
             # FFN2, then the next layer's LN1 (or the final norm).
             if i == nl - 1:
                 nw, nb, ne = w.finw.data_ptr(), w.finb.data_ptr(), w.fin_eps
-                s_out, h_out, f_next = None, out.data_ptr(), _lib.KF_LN_MASK_OUT
+                s_out, h_out, f_next = None, out.data_ptr(), _lib.KF_LN_MASK_OUT | ln_static
             else:
                 nx = w.layers[i + 1]
                 nw, nb, ne = nx["ln1w"].data_ptr(), nx["ln1b"].data_ptr(), nx["eps1"]

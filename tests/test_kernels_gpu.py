@@ -76,6 +76,34 @@ def test_layernorm_mask_is_a_select_not_a_multiply():
     assert torch.isfinite(h).all()
 
 
+@pytest.mark.parametrize("d", [128, 512, 1024, 4096])
+@pytest.mark.parametrize("skip", [False, True])
+def test_layernorm_static_params_identical(d, skip):
+    """KF_LN_STATIC_PARAMS loads keep, gamma and beta before the wait on the
+    previous kernel (and lets skipped padded rows leave early): same bits."""
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    torch.manual_seed(d)
+    M = 517
+    x, y = torch.randn(M, d, device="cuda"), torch.randn(M, d, device="cuda")
+    keep = (torch.rand(M, device="cuda") > 0.3).to(torch.uint8)
+    w, b = torch.randn(d, device="cuda"), torch.randn(d, device="cuda")
+    torch.cuda.synchronize()
+    outs = []
+    for static in (False, True):
+        s = torch.full((M, d), 5.0, device="cuda")
+        h = torch.full((M, d), 7.0, device="cuda")
+        flags = (_lib.KF_LN_SKIP_PADDED if skip else 0) | (_lib.KF_LN_STATIC_PARAMS if static else 0)
+        _lib.check(L.kf_ln_add_mask(x.data_ptr(), d, y.data_ptr(), d, keep.data_ptr(),
+                                    w.data_ptr(), b.data_ptr(), s.data_ptr(), d, h.data_ptr(), d,
+                                    M, d, 1e-5, flags, _lib.stream_ptr()), "kf_ln_add_mask")
+        outs.append((s, h))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    if skip:
+        dead = keep == 0
+        assert torch.all(outs[1][0][dead] == 5.0) and torch.all(outs[1][1][dead] == 7.0)
+
+
 def test_layernorm_in_place_residual():
     """The stack updates its residual stream in place (x is s_out)."""
     from techjam2026_b200 import _lib

@@ -67,7 +67,9 @@ def _worker(rank, world, port, q):
                                    x[mine], mask[mine], causal=cfg.causal)
         full = gather_rows(out_local, rows)
         if rank == 0:
-            q.put(full)
+            # By value (a numpy array is pickled whole): a tensor would travel
+            # as a shared-memory handle that dies with this process.
+            q.put(full.numpy().copy())
     finally:
         dist.destroy_process_group()
 
@@ -81,7 +83,7 @@ def test_two_rank_gloo_gather_matches_single_process():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    got = q.get(timeout=300)
+    got = torch.from_numpy(q.get(timeout=300))
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
