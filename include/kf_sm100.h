@@ -139,6 +139,26 @@ int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t 
                    int epilogue, int flags, int bn, int head_dim, int head_stride,
                    const int32_t* live_tiles, const int32_t* live_count, void* stream);
 
+/* kf_gemm_bf16x3 with stream-K scheduling: one CTA per SM, each computing an
+ * even share of all (tile, k block) pairs, so a GEMM with fewer tiles than
+ * SMs (or a ragged last wave) still keeps every SM busy for a share of the
+ * K loop. A tile split between CTAs is finished by the CTA holding its first
+ * k blocks, which adds the other parts (fp32, in a fixed order: results are
+ * deterministic, not bit-identical to kf_gemm_bf16x3). `bn` 64, 128 or 256
+ * (0 = 128), no KF_GEMM_PAIR / KF_GEMM_K32. `workspace`: at least
+ * kf_gemm_sk_workspace_bytes(M, N, bn) bytes, 16-byte aligned, ZEROED before
+ * its first use (the kernel leaves its counters zero again); partials go at
+ * its start and the per-tile counters at its end, so GEMMs of several shapes
+ * can share one buffer of max(partial bytes) + max(counter bytes); calls
+ * sharing it must not overlap on the GPU. Replaces the same F.linear calls as kf_gemm_bf16x3
+ * (kernelforge/optimized.py:441-446, 573). */
+int kf_gemm_bf16x3_sk(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t ldw,
+                      const float* bias, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                      int epilogue, int flags, int bn, int head_dim, int head_stride,
+                      const int32_t* live_tiles, const int32_t* live_count, void* workspace,
+                      int64_t workspace_bytes, void* stream);
+int64_t kf_gemm_sk_workspace_bytes(int64_t M, int64_t N, int bn);
+
 /* kf_gemm_bf16x3 (bias epilogue) followed by kf_ln_add_mask in one kernel:
  * y = A.W^T + bias stays on chip; s = keep ? res + y : 0 is written to s_out
  * (may equal res, or be null) and h = LayerNorm(s) * gamma + beta to h_out,

@@ -33,6 +33,10 @@ SIGNATURES = {
     "kf_gemm_bf16x3": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
                                 _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int,
                                 _c_ptr, _c_ptr, _c_ptr]),
+    "kf_gemm_bf16x3_sk": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
+                                   _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int,
+                                   _c_int, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_ptr]),
+    "kf_gemm_sk_workspace_bytes": (_c_i64, [_c_i64, _c_i64, _c_int]),
     "kf_gemm_bf16x3_add_ln": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
                                        _c_ptr, _c_ptr, _c_ptr, _c_float, _c_ptr, _c_i64,
                                        _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,

@@ -88,7 +88,7 @@ struct GemmCfg {
   // accumulator (off the critical path of the tile's epilogue).
   static constexpr int BIAS_OFF = BAR_OFF + BAR_BYTES;
   static constexpr int SMEM_BYTES = BIAS_OFF + BN * 4 + 1024;
-  static_assert(BN == 64 || BN == 96 || BN == 128 || BN == 256, "BN");
+  static_assert(BN == 64 || BN == 96 || BN == 112 || BN == 128 || BN == 256, "BN");
   static_assert(STAGES >= 2 && STAGES <= 8, "stages");
   static_assert(SMEM_BYTES <= 232448, "smem");
   static_assert(!PAIR || (SPLIT == SPLIT_BF16X3_PRE && (BN == 128 || BN == 256)), "pair shape");
@@ -250,16 +250,25 @@ struct LnArgs {
   int flags;
 };
 
-template <int BN, int EPI, int SPLIT, bool LNF = false, bool PAIR = false>
+// Stream-K workspace (SK kernels): fp32 partial accumulators of tiles split
+// between CTAs, [tiles][2 parts][128 rows][BN], and per (tile, epilogue half)
+// arrival counters, zero between launches.
+struct SkArgs {
+  float* ws;
+  int* flags;
+};
+
+template <int BN, int EPI, int SPLIT, bool LNF = false, bool PAIR = false, bool SK = false>
 __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int M,
                      int N, int K, int flags, int head_dim, int head_stride,
                      const int32_t* __restrict__ live_tiles, const int32_t* __restrict__ live_count,
-                     const __grid_constant__ LnArgs ln) {
+                     const __grid_constant__ LnArgs ln, const __grid_constant__ SkArgs sk) {
   using Cfg = GemmCfg<BN, SPLIT, PAIR>;
   constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
   static_assert(!(LNF && PAIR), "pair kernels have the plain epilogues");
+  static_assert(!SK || (SPLIT == SPLIT_BF16X3_PRE && !PAIR && !LNF), "stream-K shape");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -336,7 +345,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   // previous kernel's tail. Their barriers expect those bytes now and the A
   // bytes and the arrival later (the phase cannot end in between).
   int pre_w = 0;
-  if constexpr (Cfg::PRESPLIT && !PAIR && !LNF) {
+  if constexpr (Cfg::PRESPLIT && !PAIR && !LNF && !SK) {
     if ((flags & KF_GEMM_W_STATIC) && warp == 0 && lane == 0) {
       const int nw0 = (static_cast<int>(blockIdx.x) % num_n) * BN;
       pre_w = num_kb < STAGES ? num_kb : STAGES;
@@ -376,6 +385,46 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
     bool own;
     return row_tile(tile, own);
   };
+  // Segments (tile, k blocks [kb_b, kb_e)) a CTA computes, the same sequence
+  // for every role. Round-robin whole tiles, or (SK, stream-K) an even share
+  // of the num_tiles * num_kb k blocks: CTA c takes [c W / G, (c+1) W / G),
+  // with G cut so that a share is at least half a tile (a tile then spans at
+  // most three CTAs). A tile's first part (kb_b = 0) is its owner: it adds
+  // the other parts, which their CTAs compute first in their ranges.
+  const long long sk_W = static_cast<long long>(num_tiles) * num_kb;
+  int sk_G = static_cast<int>(gridDim.x);
+  if (SK && 2LL * num_tiles < sk_G) sk_G = 2 * num_tiles;
+  auto sk_beg = [&](long long c) -> long long { return c * sk_W / sk_G; };
+  auto sk_cta_of = [&](long long u) -> int {  // the CTA whose share holds k block u
+    long long c = u * sk_G / (sk_W > 0 ? sk_W : 1);
+    while (c + 1 < sk_G && sk_beg(c + 1) <= u) ++c;
+    while (c > 0 && sk_beg(c) > u) --c;
+    return static_cast<int>(c);
+  };
+  struct SegIter {
+    long long u, u1;
+    int rr, rr_stride, n_tiles, n_kb;
+    __device__ bool next(int& tile, int& kb_b, int& kb_e) {
+      if (SK) {
+        if (u >= u1) return false;
+        tile = static_cast<int>(u / n_kb);
+        kb_b = static_cast<int>(u - static_cast<long long>(tile) * n_kb);
+        const long long rem = u1 - u;
+        kb_e = (kb_b + rem < n_kb) ? kb_b + static_cast<int>(rem) : n_kb;
+        u += kb_e - kb_b;
+        return true;
+      }
+      if (rr >= n_tiles) return false;
+      tile = rr;
+      kb_b = 0;
+      kb_e = n_kb;
+      rr += rr_stride;
+      return true;
+    }
+  };
+  const bool sk_active = SK && static_cast<int>(blockIdx.x) < sk_G;
+  const SegIter seg0{sk_active ? sk_beg(blockIdx.x) : 0, sk_active ? sk_beg(blockIdx.x + 1) : 0,
+                     unit0, ustride, num_tiles, num_kb};
 
   if (warp == 0) {
     if (lane == 0) {
@@ -384,11 +433,13 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      for (int tile = unit0; tile < num_tiles && ok; tile += ustride) {
+      SegIter it = seg0;
+      int tile, kb_b, kb_e;
+      while (ok && it.next(tile, kb_b, kb_e)) {
         const int m0 = row0(tile);
         // PAIR: this CTA stages B rows [n0 + rank * BN/2, + BN/2) of the tile.
         const int n0 = (tile % num_n) * BN + static_cast<int>(crank) * (PAIR ? Cfg::B_ROWS : 0);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb_b; kb < kb_e; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, KF_DEV_WAIT_TIMEOUT_TMA)) {
             ok = false;
             break;
@@ -463,7 +514,9 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = unit0; tile < num_tiles && ok; tile += ustride) {
+      SegIter it = seg0;
+      int tile, kb_b, kb_e;
+      while (ok && it.next(tile, kb_b, kb_e)) {
         // PAIR: the other CTA's epilogue warps arrive remotely (release at
         // cluster scope), so the wait acquires at cluster scope.
         if (!(PAIR ? mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, abort_flag,
@@ -475,7 +528,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb_b; kb < kb_e; ++kb) {
           if (!mbar_wait(Cfg::CONVERTS ? &conv[stage] : &full[stage], phase, abort_flag,
                          KF_DEV_WAIT_TIMEOUT_MMA)) {
             ok = false;
@@ -495,7 +548,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
               const uint64_t bh = make_smem_desc(b_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
               const uint64_t al = make_smem_desc(alo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
               const uint64_t bl = make_smem_desc(blo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
-              mma_bf16_ss_pair(d_tmem, al, bh, idesc_bf, (kb | k) != 0 ? 1u : 0u);
+              mma_bf16_ss_pair(d_tmem, al, bh, idesc_bf, (kb != kb_b || k != 0) ? 1u : 0u);
               mma_bf16_ss_pair(d_tmem, ah, bl, idesc_bf, 1u);
               mma_bf16_ss_pair(d_tmem, ah, bh, idesc_bf, 1u);
             }
@@ -507,7 +560,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
               const uint64_t bh = make_smem_desc(b_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
               const uint64_t al = make_smem_desc(alo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
               const uint64_t bl = make_smem_desc(blo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
-              mma_bf16_ss(d_tmem, al, bh, idesc_bf, (kb | k) != 0 ? 1u : 0u);
+              mma_bf16_ss(d_tmem, al, bh, idesc_bf, (kb != kb_b || k != 0) ? 1u : 0u);
               mma_bf16_ss(d_tmem, ah, bl, idesc_bf, 1u);
               mma_bf16_ss(d_tmem, ah, bh, idesc_bf, 1u);
             }
@@ -519,7 +572,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
               const uint64_t bh = make_smem_desc(b_addr + k * 32, 16, 512, KF_SWIZZLE_64B);
               const uint64_t al = make_smem_desc(alo_addr + k * 32, 16, 512, KF_SWIZZLE_64B);
               const uint64_t bl = make_smem_desc(blo_addr + k * 32, 16, 512, KF_SWIZZLE_64B);
-              mma_bf16_ss(d_tmem, al, bh, idesc_bf, (kb | k) != 0 ? 1u : 0u);
+              mma_bf16_ss(d_tmem, al, bh, idesc_bf, (kb != kb_b || k != 0) ? 1u : 0u);
               mma_bf16_ss(d_tmem, ah, bl, idesc_bf, 1u);
               mma_bf16_ss(d_tmem, ah, bh, idesc_bf, 1u);
             }
@@ -533,7 +586,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
               const uint64_t al = make_smem_desc(alo + k * 32, 16, 512, KF_SWIZZLE_64B);
               const uint64_t bh = make_smem_desc(bhi + k * 32, 16, 512, KF_SWIZZLE_64B);
               const uint64_t bl = make_smem_desc(blo + k * 32, 16, 512, KF_SWIZZLE_64B);
-              mma_bf16_ss(d_tmem, al, bh, idesc_bf, (kb | k) != 0 ? 1u : 0u);
+              mma_bf16_ss(d_tmem, al, bh, idesc_bf, (kb != kb_b || k != 0) ? 1u : 0u);
               mma_bf16_ss(d_tmem, ah, bl, idesc_bf, 1u);
               mma_bf16_ss(d_tmem, ah, bh, idesc_bf, 1u);
             }
@@ -545,10 +598,10 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
             if (SPLIT) {
               const uint64_t ald = make_smem_desc(alo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
               const uint64_t bld = make_smem_desc(blo_addr + k * 32, 16, 1024, KF_SWIZZLE_128B);
-              mma_tf32_ss(d_tmem, ald, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+              mma_tf32_ss(d_tmem, ald, bd, idesc, (kb != kb_b || k != 0) ? 1u : 0u);
               mma_tf32_ss(d_tmem, ad, bld, idesc, 1u);
             }
-            mma_tf32_ss(d_tmem, ad, bd, idesc, (SPLIT || (kb | k) != 0) ? 1u : 0u);
+            mma_tf32_ss(d_tmem, ad, bd, idesc, (SPLIT || kb != kb_b || k != 0) ? 1u : 0u);
             (void)idesc_bf;
           }
           if constexpr (PAIR) {
@@ -816,7 +869,9 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
     const int ht = threadIdx.x - (64 + 128 * half);                 // 0..127 in the half
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = unit0; tile < num_tiles; tile += ustride) {
+    SegIter it = seg0;
+    int tile, kb_b, kb_e;
+    while (it.next(tile, kb_b, kb_e)) {
       bool own;  // PAIR: false for a repeated row tile (nothing stored)
       const int m0 = row_tile(tile, own);
       const int n0 = (tile % num_n) * BN;
@@ -826,7 +881,8 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
       // barrier after the accumulator wait publishes these writes.
       if (ht < 32) {
         for (int c = 32 * half; c < BN; c += 64)
-          sbias[c + ht] = (bias && n0 + c + ht < N) ? __ldg(bias + n0 + c + ht) : 0.f;
+          if (c + ht < BN)
+            sbias[c + ht] = (bias && n0 + c + ht < N) ? __ldg(bias + n0 + c + ht) : 0.f;
       }
       // One bounded wait by the half's leader, shared through the half's
       // named barrier, so all four warps of a half always reach the same
@@ -836,6 +892,43 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
       named_bar_sync(bar_id, 128);
       if (!epi_ok[half]) break;
       tc_fence_after();
+      // Stream-K: a later part of a tile (kb_b > 0) leaves its partial
+      // accumulator in the workspace (slot = part - 1) and counts itself in
+      // the tile's per-half counter; the owner (kb_b == 0, the tile's first
+      // k blocks) waits for the other parts and adds them, in part order.
+      int sk_part = 0, sk_np = 0;
+      if constexpr (SK) {
+        const long long tu = static_cast<long long>(tile) * num_kb;
+        if (kb_b > 0)
+          sk_part = static_cast<int>(blockIdx.x) - sk_cta_of(tu);
+        else if (kb_e < num_kb)
+          sk_np = sk_cta_of(tu + num_kb - 1) - static_cast<int>(blockIdx.x);
+        if (sk_part > 2 || sk_np > 2) {  // the share cut makes this impossible
+          if (leader) record_device_status(KF_DEV_WAIT_TIMEOUT_EPI);
+          sk_part = sk_part > 2 ? 3 : sk_part;
+          sk_np = sk_np > 2 ? 2 : sk_np;
+        }
+        if (sk_np > 0) {
+          if (leader) {
+            volatile int* fl = sk.flags + 2 * tile + half;
+            int got = 1;
+            const long long t0 = clock64();
+            while (*fl < sk_np) {
+              if (*abort_flag || clock64() - t0 > KF_WAIT_CYCLES) {
+                *abort_flag = 1;
+                record_device_status(KF_DEV_WAIT_TIMEOUT_EPI);
+                got = 0;
+                break;
+              }
+              __nanosleep(64);
+            }
+            __threadfence();
+            epi_ok[half] = got;
+          }
+          named_bar_sync(bar_id, 128);
+          if (!epi_ok[half]) break;
+        }
+      }
       const int r = quarter * 32 + lane;
       const int row = m0 + r;
       const uint32_t tbase =
@@ -845,8 +938,40 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
       for (int c = 32 * half; c < BN; c += 64) {
         if (n0 + c >= N || !own) break;  // uniform over the half
         float v[32];
+        // BN = 112: the last chunk holds 16 columns. Its TMEM load also reads
+        // 16 columns past the accumulator (inside the allocation, unused), and
+        // it is stored directly, bounded by the tile's last column.
+        const bool part = (c + 32 > BN);
         tmem_ld32(tbase + static_cast<uint32_t>(c), v);
-        if (tma_out && (flags & KF_GEMM_OUT_SPLIT)) {
+        if constexpr (SK) {
+          if (sk_part > 0) {  // a later part: this thread's row of the chunk to the workspace
+            if (sk_part <= 2) {
+              float4* dst = reinterpret_cast<float4*>(
+                  sk.ws + ((static_cast<int64_t>(tile) * 2 + sk_part - 1) * BM + r) * BN + c);
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            }
+            continue;
+          }
+          for (int pp = 0; pp < sk_np; ++pp) {  // the owner adds the later parts in order
+            const float4* src = reinterpret_cast<const float4*>(
+                sk.ws + ((static_cast<int64_t>(tile) * 2 + pp) * BM + r) * BN + c);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 q = __ldcg(src + j);
+              v[4 * j] += q.x;
+              v[4 * j + 1] += q.y;
+              v[4 * j + 2] += q.z;
+              v[4 * j + 3] += q.w;
+            }
+          }
+        }
+        if (part) {
+          if (row < M)
+            gemm_store_chunk<EPI>(v, crow, bias, n0 + c, (n0 + BN < N ? n0 + BN : N), flags,
+                                  head_dim, head_stride);
+        } else if (tma_out && (flags & KF_GEMM_OUT_SPLIT)) {
           // bf16 hi/lo planes: two 128x32 bf16 tiles (64-byte rows, SW64).
           // The arithmetic runs before the wait for the staging buffer, so
           // it overlaps the previous chunk's TMA store.
@@ -931,6 +1056,16 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
           gemm_store_chunk<EPI>(v, crow, bias, n0 + c, N, flags, head_dim, head_stride);
         }
       }
+      if constexpr (SK) {
+        if (sk_part > 0 && sk_part <= 2) {
+          __threadfence();  // this thread's partial rows, at device scope
+          named_bar_sync(bar_id, 128);
+          if (leader) atomicAdd(sk.flags + 2 * tile + half, 1);
+        } else if (sk_np > 0) {
+          named_bar_sync(bar_id, 128);  // the half has read every part
+          if (leader) atomicExch(sk.flags + 2 * tile + half, 0);
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -993,8 +1128,34 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   const int grid = tiles < sm_count() ? tiles : sm_count();
   return cuda_status(launch_chained(kern, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM_BYTES, st, ta,
                                     tb, tc, C, ldc, bias, M, N, K, flags, hd, hs, live_tiles,
-                                    live_count, LnArgs{}),
+                                    live_count, LnArgs{}, SkArgs{}),
                      "kf_gemm_tf32 launch");
+}
+
+// Stream-K GEMM: one CTA per SM, each taking an even share of all k blocks
+// (the share cut on the device once the live tile count is known).
+template <int BN, int EPI>
+static int launch_gemm_sk(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                          float* C, int64_t ldc, const float* bias, int M, int N, int K, int flags,
+                          int hd, int hs, const int32_t* live_tiles, const int32_t* live_count,
+                          const SkArgs& sk, cudaStream_t st) {
+  using Cfg = GemmCfg<BN, SPLIT_BF16X3_PRE>;
+  auto kern = gemm_tf32_kernel<BN, EPI, SPLIT_BF16X3_PRE, false, false, true>;
+  static int attr_set[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!attr_set[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_status(e, "kf_gemm_bf16x3_sk: set smem attribute");
+    attr_set[dev] = 1;
+  }
+  return cuda_status(launch_chained(kern, dim3(static_cast<unsigned>(sm_count())),
+                                    dim3(Cfg::THREADS), Cfg::SMEM_BYTES, st, ta, tb, tc, C, ldc,
+                                    bias, M, N, K, flags, hd, hs, live_tiles, live_count, LnArgs{},
+                                    sk),
+                     "kf_gemm_bf16x3_sk launch");
 }
 
 // cta_group::2 GEMM: clusters of two CTAs (one 256 x BN tile per pair at a
@@ -1043,7 +1204,7 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
   return cuda_status(
       launch_chained_cluster(kern, dim3(static_cast<unsigned>(2 * pairs)), dim3(Cfg::THREADS),
                              Cfg::SMEM_BYTES, st, 2u, ta, tb, tc, C, ldc, bias, M, N, K, flags, hd,
-                             hs, live_tiles, live_count, LnArgs{}),
+                             hs, live_tiles, live_count, LnArgs{}, SkArgs{}),
       "kf_gemm_bf16x3 (pair) launch");
 }
 
@@ -1095,7 +1256,7 @@ static int launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tb, const fl
                              dim3(Cfg::THREADS), Cfg::SMEM_BYTES, st,
                              static_cast<unsigned>(csize), ta, tb, tc, static_cast<float*>(nullptr),
                              static_cast<int64_t>(0), bias, M, N, K, 0, 0, 0, live_tiles,
-                             live_count, ln),
+                             live_count, ln, SkArgs{}),
       "kf_gemm_bf16x3_add_ln launch");
 }
 
@@ -1241,11 +1402,18 @@ extern "C" int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t
   return KF_E_INVALID;
 }
 
-extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t ldw,
-                              const float* bias, void* C, int64_t ldc, int64_t M, int64_t N,
-                              int64_t K, int epilogue, int flags, int bn, int head_dim,
-                              int head_stride, const int32_t* live_tiles,
-                              const int32_t* live_count, void* stream) {
+// Stream-K workspace bytes for an M x N output in N tiles of bn: two fp32
+// partial tiles per 128 x bn tile, then two int counters per tile.
+static int64_t sk_workspace_bytes(int64_t M, int64_t N, int bn) {
+  const int64_t tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  return tiles * 2 * 128 * bn * 4 + tiles * 2 * 4;
+}
+
+static int gemm_bf16x3_impl(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t ldw,
+                            const float* bias, void* C, int64_t ldc, int64_t M, int64_t N,
+                            int64_t K, int epilogue, int flags, int bn, int head_dim,
+                            int head_stride, const int32_t* live_tiles,
+                            const int32_t* live_count, const SkArgs* sk, void* stream) {
   if (!A2 || !W2 || !C || M < 0 || N < 0 || K < 0) {
     set_last_error("kf_gemm_bf16x3: invalid arguments");
     return KF_E_INVALID;
@@ -1279,8 +1447,16 @@ extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W
     return KF_E_INVALID;
   }
   if (bn == 0) bn = choose_bn(M, N);
-  if (bn != 64 && bn != 96 && bn != 128 && bn != 256) {
-    set_last_error("kf_gemm_bf16x3: bn must be 0, 64, 96, 128 or 256");
+  if (bn != 64 && bn != 96 && bn != 112 && bn != 128 && bn != 256) {
+    set_last_error("kf_gemm_bf16x3: bn must be 0, 64, 96, 112, 128 or 256");
+    return KF_E_INVALID;
+  }
+  if (bn == 112 && (out_split || (flags & KF_GEMM_PAIR))) {
+    set_last_error("kf_gemm_bf16x3: bn 112 needs fp32 output and one-CTA tiles");
+    return KF_E_INVALID;
+  }
+  if (sk && (bn == 96 || bn == 112 || (flags & (KF_GEMM_PAIR | KF_GEMM_K32)))) {
+    set_last_error("kf_gemm_bf16x3_sk: bn must be 64, 128 or 256, without KF_GEMM_PAIR/K32");
     return KF_E_INVALID;
   }
   // k blocks of 64 bf16 (128-byte rows) or, with KF_GEMM_K32, of 32 (64-byte
@@ -1336,6 +1512,29 @@ extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
   float* Cf = static_cast<float*>(C);
+  if (sk) {
+    if (bn == 64)
+      return epilogue == KF_EPI_BIAS
+                 ? launch_gemm_sk<64, KF_EPI_BIAS>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f, head_dim,
+                                                   head_stride, live_tiles, live_count, *sk, st)
+                 : launch_gemm_sk<64, KF_EPI_BIAS_GELU>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,
+                                                        head_dim, head_stride, live_tiles,
+                                                        live_count, *sk, st);
+    if (bn == 128)
+      return epilogue == KF_EPI_BIAS
+                 ? launch_gemm_sk<128, KF_EPI_BIAS>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,
+                                                    head_dim, head_stride, live_tiles, live_count,
+                                                    *sk, st)
+                 : launch_gemm_sk<128, KF_EPI_BIAS_GELU>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,
+                                                         head_dim, head_stride, live_tiles,
+                                                         live_count, *sk, st);
+    return epilogue == KF_EPI_BIAS
+               ? launch_gemm_sk<256, KF_EPI_BIAS>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f, head_dim,
+                                                  head_stride, live_tiles, live_count, *sk, st)
+               : launch_gemm_sk<256, KF_EPI_BIAS_GELU>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,
+                                                       head_dim, head_stride, live_tiles,
+                                                       live_count, *sk, st);
+  }
   if (pair) {
     if (bn == 128)
       return epilogue == KF_EPI_BIAS
@@ -1374,10 +1573,50 @@ extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W
   }
   KF_GEMM_PRE_CASE(64)
   KF_GEMM_PRE_CASE(96)
+  KF_GEMM_PRE_CASE(112)
   KF_GEMM_PRE_CASE(128)
   KF_GEMM_PRE_CASE(256)
 #undef KF_GEMM_PRE_CASE
   return KF_E_INVALID;
+}
+
+extern "C" int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t ldw,
+                              const float* bias, void* C, int64_t ldc, int64_t M, int64_t N,
+                              int64_t K, int epilogue, int flags, int bn, int head_dim,
+                              int head_stride, const int32_t* live_tiles,
+                              const int32_t* live_count, void* stream) {
+  return gemm_bf16x3_impl(A2, lda, W2, ldw, bias, C, ldc, M, N, K, epilogue, flags, bn, head_dim,
+                          head_stride, live_tiles, live_count, nullptr, stream);
+}
+
+extern "C" int64_t kf_gemm_sk_workspace_bytes(int64_t M, int64_t N, int bn) {
+  if (M <= 0 || N <= 0 || (bn != 64 && bn != 128 && bn != 256)) return 0;
+  return sk_workspace_bytes(M, N, bn);
+}
+
+extern "C" int kf_gemm_bf16x3_sk(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t ldw,
+                                 const float* bias, void* C, int64_t ldc, int64_t M, int64_t N,
+                                 int64_t K, int epilogue, int flags, int bn, int head_dim,
+                                 int head_stride, const int32_t* live_tiles,
+                                 const int32_t* live_count, void* workspace,
+                                 int64_t workspace_bytes, void* stream) {
+  if (bn == 0) bn = 128;
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 15u) || bn <= 0 ||
+      workspace_bytes < sk_workspace_bytes(M > 0 ? M : 1, N > 0 ? N : 1, bn)) {
+    set_last_error("kf_gemm_bf16x3_sk: workspace missing, unaligned or below "
+                   "kf_gemm_sk_workspace_bytes");
+    return KF_E_INVALID;
+  }
+  const int64_t tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  // Partials at the start, counters at the END of the caller's buffer: GEMMs
+  // of different shapes can share one workspace sized max(partials) +
+  // max(counters) without one's partials landing on another's counters.
+  SkArgs sk;
+  sk.ws = static_cast<float*>(workspace);
+  sk.flags = reinterpret_cast<int*>(static_cast<char*>(workspace) +
+                                    ((workspace_bytes - tiles * 2 * 4) & ~static_cast<int64_t>(15)));
+  return gemm_bf16x3_impl(A2, lda, W2, ldw, bias, C, ldc, M, N, K, epilogue, flags, bn, head_dim,
+                          head_stride, live_tiles, live_count, &sk, stream);
 }
 
 extern "C" int kf_gemm_bf16x3_add_ln(const uint16_t* A2, int64_t lda, const uint16_t* W2,

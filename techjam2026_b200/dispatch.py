@@ -79,6 +79,14 @@ class Plan:
     pair_out: bool = False
     pair_ffn1: bool = False
     pair_ffn2: bool = False
+    # Stream-K scheduling of a bf16x3 GEMM (kf_gemm_bf16x3_sk): every SM takes
+    # an even share of the (tile, k block) pairs, for GEMMs whose tiles fill
+    # only part of one wave (c2's N = 512 GEMMs: 108 tiles on 148 SMs). Split
+    # tiles are summed in a fixed order: deterministic, not bit-identical.
+    sk_qkv: bool = False
+    sk_out: bool = False
+    sk_ffn1: bool = False
+    sk_ffn2: bool = False
 
     # Narrow I/O dtypes (float16/bfloat16): run the organiser's own layer,
     # captured whole into one CUDA graph, instead of these kernels. At those
@@ -118,6 +126,9 @@ class Plan:
         pairs = (self.pair_qkv, self.pair_out, self.pair_ffn1, self.pair_ffn2)
         if any(pairs):
             bits.append("cta-pair=" + "/".join("y" if p else "n" for p in pairs))
+        sks = (self.sk_qkv, self.sk_out, self.sk_ffn1, self.sk_ffn2)
+        if any(sks):
+            bits.append("stream-k=" + "/".join("y" if p else "n" for p in sks))
         return " ".join(bits)
 
 

@@ -116,11 +116,33 @@ class _Workspace:
         self.bits = torch.zeros(B * words, **i32)
         self.live_tiles = torch.zeros((M + 127) // 128, **i32)
         self.live_count = torch.zeros(1, **i32)
+        # Stream-K GEMMs share one zeroed workspace (partials + counters);
+        # the kernels leave its counters zero, and they run one after another.
+        sk_bytes = _Workspace.sk_bytes(cfg, M, plan)
+        self.sk = torch.zeros(sk_bytes // 4, **i32) if sk_bytes else None
+
+    @staticmethod
+    def sk_bytes(cfg, M: int, plan: Plan) -> int:
+        """One stream-K workspace for every stream-K GEMM of the plan: the
+        largest partial area plus the largest counter area."""
+        d, F = cfg.d_model, cfg.ffn_dim
+        widths = {"qkv": 3 * d, "out": d, "ffn1": F, "ffn2": d}
+        prec = plan.gemm_precisions()
+        partials = counters = 0
+        for g, n in widths.items():
+            if getattr(plan, f"sk_{g}") and prec[g] == "bf16x3":
+                bn = getattr(plan, f"bn_{g}") or 128
+                tiles = ((M + 127) // 128) * ((n + bn - 1) // bn)
+                partials = max(partials, tiles * 2 * 128 * bn * 4)
+                counters = max(counters, tiles * 2 * 4)
+        # partials at the start, counters at the end (kf_gemm_bf16x3_sk)
+        return partials + ((counters + 15) // 16) * 16 + (16 if counters else 0)
 
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size()
                    for t in (self.res, self.h, self.h2, self.qkv, self.ctx, self.y, self.ffn,
-                             self.bits, self.live_tiles, self.live_count) if t is not None)
+                             self.bits, self.live_tiles, self.live_count, self.sk)
+                   if t is not None)
 
     @staticmethod
     def estimate(cfg, B: int, S: int, plan: Plan) -> int:
@@ -134,7 +156,8 @@ class _Workspace:
         per_row += 4 * d if (split["qkv"] or split["ffn1"]) else 0    # h2 planes
         per_row += 4 * 3 * H * dh_store + 4 * d + 4 * d + 4 * F       # qkv, ctx, y, ffn
         words = (S + 31) // 32
-        return M * per_row + 4 * B * words + 4 * ((M + 127) // 128) + 4
+        return (M * per_row + 4 * B * words + 4 * ((M + 127) // 128) + 4
+                + _Workspace.sk_bytes(cfg, M, plan))
 
 
 class FusedTransformer(LayerStack):
@@ -276,6 +299,11 @@ class FusedTransformer(LayerStack):
             if split[g]:
                 if getattr(plan, f"kb_{g}") == 32:
                     flags |= _lib.KF_GEMM_K32
+                if getattr(plan, f"sk_{g}"):
+                    run(kind, L.kf_gemm_bf16x3_sk, A, lda, W.data_ptr(), K, bias.data_ptr(), C,
+                        ldc, M, N, K, epi, flags, bn or 128, hd_, hs_, lt, lc,
+                        ws.sk.data_ptr(), ws.sk.numel() * 4, st)
+                    return
                 if getattr(plan, f"pair_{g}") and bn in (128, 256):
                     flags |= _lib.KF_GEMM_PAIR
                 elif w.static:

@@ -165,3 +165,28 @@ def test_plan_pair_fields_round_trip_and_describe():
     for k in ("pair_qkv", "pair_out", "pair_ffn1", "pair_ffn2"):
         d.pop(k)
     assert Plan(**d).pair_qkv is False
+
+
+def test_stream_k_workspace_keeps_partials_and_counters_apart():
+    """One workspace serves stream-K GEMMs of several shapes: the largest
+    partial area comes first and the largest counter area last, so no GEMM's
+    partials overlap any GEMM's counters (placed at the buffer's end)."""
+    import dataclasses
+    from techjam2026_b200.configs import WORKLOADS
+    from techjam2026_b200.dispatch import DEFAULT_PLAN
+    from techjam2026_b200.fused import _Workspace
+    cfg = WORKLOADS["c2"].cfg
+    M = cfg.batch_size * cfg.seq_len
+    plan = dataclasses.replace(DEFAULT_PLAN, bn_qkv=128, bn_out=128, bn_ffn1=128, bn_ffn2=64,
+                               sk_qkv=True, sk_out=True, sk_ffn1=True, sk_ffn2=True)
+    size = _Workspace.sk_bytes(cfg, M, plan)
+    assert size % 4 == 0
+    ends, starts = [], []
+    for n, bn in ((3 * cfg.d_model, 128), (cfg.d_model, 128), (cfg.ffn_dim, 128),
+                  (cfg.d_model, 64)):
+        tiles = ((M + 127) // 128) * ((n + bn - 1) // bn)
+        ends.append(tiles * 2 * 128 * bn * 4)
+        starts.append((size - tiles * 2 * 4) & ~15)
+        assert starts[-1] + tiles * 8 <= size
+    assert max(ends) <= min(starts)
+    assert _Workspace.sk_bytes(cfg, M, DEFAULT_PLAN) == 0

@@ -534,6 +534,117 @@ def test_gemm_bf16x3_static_w_prefetch_bit_identical(M, N, K, bn, k32, live):
     assert L.kf_device_status(0) == 0
 
 
+@pytest.mark.parametrize("M,N,K", [(4096, 512, 512), (517, 384, 512), (300, 200, 136),
+                                   (1000, 1000, 1000), (256, 112, 64), (128, 16, 32)])
+@pytest.mark.parametrize("gelu", [False, True])
+@pytest.mark.parametrize("static", [False, True])
+def test_gemm_bf16x3_bn112_bit_identical(M, N, K, gelu, static):
+    """N tile 112 (one wave for N = 512 on 148 SMs: 5 column tiles): the last
+    16-column chunk of each tile is stored directly, bounded by the tile.
+    Same bits as N tile 128 (a tile only moves work between CTAs)."""
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    torch.manual_seed(M + 3 * N + K)
+    a = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / math.sqrt(K)
+    bias = torch.randn(N, device="cuda")
+    a2, w2 = to_planes(a).contiguous(), to_planes(w).contiguous()
+    torch.cuda.synchronize()
+    outs = []
+    for bn in (128, 112):
+        c = torch.full((M, N), 3.0, device="cuda")
+        rc = L.kf_gemm_bf16x3(a2.data_ptr(), K, w2.data_ptr(), K, bias.data_ptr(), c.data_ptr(), N,
+                              M, N, K, 1 if gelu else 0,
+                              _lib.KF_GEMM_W_STATIC if static else 0, bn, 0, 0, None, None,
+                              _lib.stream_ptr())
+        _lib.check(rc, "kf_gemm_bf16x3")
+        outs.append(c)
+    assert torch.equal(outs[0], outs[1])
+    assert L.kf_device_status(0) == 0
+
+
+def test_gemm_bf16x3_bn112_rejects_split_output_and_pairs():
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    a2 = torch.zeros(2, 128, 64, dtype=torch.int16, device="cuda")
+    w2 = torch.zeros(2, 112, 64, dtype=torch.int16, device="cuda")
+    c = torch.zeros(2, 128, 112, dtype=torch.int16, device="cuda")
+    for flags in (_lib.KF_GEMM_OUT_BF16X2, _lib.KF_GEMM_PAIR):
+        rc = L.kf_gemm_bf16x3(a2.data_ptr(), 64, w2.data_ptr(), 64, None, c.data_ptr(), 112, 128,
+                              112, 64, 0, flags, 112, 0, 0, None, None, _lib.stream_ptr())
+        assert rc == _lib.KF_E_INVALID
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 512, 512), (4096, 512, 2048), (300, 200, 136),
+                                   (128, 64, 64), (1000, 1000, 1000), (256, 256, 24),
+                                   (4096, 2048, 512)])
+@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("gelu", [False, True])
+@pytest.mark.parametrize("live", [False, True])
+def test_gemm_bf16x3_stream_k(M, N, K, bn, gelu, live):
+    """Stream-K: every SM takes an even share of the (tile, k block) pairs and
+    a split tile is finished by its first part. Deterministic (two runs agree
+    bit for bit), within fp32 reassociation of the one-CTA kernel, padded row
+    tiles untouched, and the workspace's counters are zero again afterwards."""
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    torch.manual_seed(M + N + 7 * K + bn)
+    a = torch.randn(M, K, device="cuda")
+    w = torch.randn(N, K, device="cuda") / math.sqrt(K)
+    bias = torch.randn(N, device="cuda")
+    a2, w2 = to_planes(a).contiguous(), to_planes(w).contiguous()
+    lt = lc = None
+    n_rt = (M + 127) // 128
+    computed = torch.ones(M, dtype=torch.bool, device="cuda")
+    if live:
+        keep = torch.zeros(M, dtype=torch.uint8, device="cuda")
+        for t in range(0, n_rt, 2):
+            keep[t * 128] = 1
+        lt = torch.empty(n_rt, dtype=torch.int32, device="cuda")
+        lc = torch.zeros(1, dtype=torch.int32, device="cuda")
+        _lib.check(L.kf_live_row_tiles(keep.data_ptr(), M, lt.data_ptr(), lc.data_ptr(),
+                                       _lib.stream_ptr()), "live tiles")
+        computed = (torch.arange(M, device="cuda") // 128) % 2 == 0
+    nbytes = int(L.kf_gemm_sk_workspace_bytes(M, N, bn))
+    ws = torch.zeros(nbytes // 4, dtype=torch.int32, device="cuda")
+    tiles = n_rt * ((N + bn - 1) // bn)
+    flags_view = ws[tiles * 2 * 128 * bn:]
+    args = lambda c: (a2.data_ptr(), K, w2.data_ptr(), K, bias.data_ptr(), c.data_ptr(), N, M, N,
+                      K, 1 if gelu else 0, 0, bn, 0, 0, lt.data_ptr() if live else None,
+                      lc.data_ptr() if live else None)
+    ref = torch.full((M, N), 3.0, device="cuda")
+    _lib.check(L.kf_gemm_bf16x3(*args(ref), _lib.stream_ptr()), "kf_gemm_bf16x3")
+    outs = []
+    for _ in range(2):
+        c = torch.full((M, N), 3.0, device="cuda")
+        _lib.check(L.kf_gemm_bf16x3_sk(*args(c), ws.data_ptr(), nbytes, _lib.stream_ptr()),
+                   "kf_gemm_bf16x3_sk")
+        outs.append(c)
+        torch.cuda.synchronize()
+        assert torch.count_nonzero(flags_view) == 0
+    assert L.kf_device_status(0) == 0
+    assert torch.equal(outs[0], outs[1])
+    err = (outs[0][computed] - ref[computed]).abs().max().item()
+    assert err <= 1e-5 * max(1.0, ref[computed].abs().max().item()), err
+    assert torch.all(outs[0][~computed] == 3.0)
+
+
+def test_gemm_bf16x3_stream_k_rejects_bad_workspace():
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    a2 = torch.zeros(2, 128, 64, dtype=torch.int16, device="cuda")
+    w2 = torch.zeros(2, 64, 64, dtype=torch.int16, device="cuda")
+    c = torch.zeros(128, 64, device="cuda")
+    need = int(L.kf_gemm_sk_workspace_bytes(128, 64, 64))
+    ws = torch.zeros(need // 4, dtype=torch.int32, device="cuda")
+    for wptr, wbytes, bn in ((None, need, 64), (ws.data_ptr(), need - 4, 64),
+                             (ws.data_ptr(), need, 96)):
+        rc = L.kf_gemm_bf16x3_sk(a2.data_ptr(), 64, w2.data_ptr(), 64, None, c.data_ptr(), 64, 128,
+                                 64, 64, 0, 0, bn, 0, 0, None, None, wptr, wbytes,
+                                 _lib.stream_ptr())
+        assert rc == _lib.KF_E_INVALID
+
+
 def test_gemm_bf16x3_pair_rejects_bad_tiles():
     from techjam2026_b200 import _lib
     L = _lib.lib()

@@ -234,3 +234,33 @@ def test_organiser_accuracy_trials():
         assert ours._impl is not None and not ours._failed
         ref = _oracle(cfg, sd, x, mask, query_chunk=256)
         _assert_gate(ref, out, f"organiser trial {trial + 1}/5 (seed {1234 + trial})")
+
+
+def test_stream_k_gemms_share_one_workspace_and_pass_the_gate():
+    """Every GEMM on stream-K scheduling (four shapes sharing one workspace:
+    partials at its start, counters at its end) through several forwards:
+    the gate holds, results repeat bit for bit, padded rows stay zero."""
+    import dataclasses
+    from techjam2026_b200.dispatch import DEFAULT_PLAN
+    w = WORKLOADS["c2"]
+    cfg = dataclasses.replace(w.cfg, batch_size=4, num_layers=2)
+    sd = make_state_dict(cfg, 3)
+    x, mask = generate_case(cfg, 3, w.padding_ratio, w.input_scale)
+    plan = dataclasses.replace(DEFAULT_PLAN, bn_qkv=128, bn_out=128, bn_ffn1=128, bn_ffn2=64,
+                               sk_qkv=True, sk_out=True, sk_ffn1=True, sk_ffn2=True)
+    m = _model(cfg, sd, plan)
+    xd, md = x.cuda(), mask.cuda()
+    first = m(xd, md)
+    again = [m(xd, md) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert _lib_status() == 0
+    for o in again:
+        assert torch.equal(o, first)
+    ref = _oracle(cfg, sd, x, mask)
+    _assert_gate(ref, first, "stream-K c2 (B=4, L=2)")
+    assert padded_rows_exactly_zero(first, mask)
+
+
+def _lib_status():
+    from techjam2026_b200 import _lib
+    return _lib.lib().kf_device_status(0)
