@@ -498,9 +498,12 @@ __global__ void __launch_bounds__(192, MINB)
       for (int u = 0; u < 8; ++u) sp[u] = 0.f;
 #pragma unroll
       for (int c = 0; c < BN; ++c) {
-        // P is rounded to the nearest TF32 value (the tensor core would
-        // otherwise truncate it), on the integer pipe.
-        const float p = round_tf32_nonneg(fast_exp2(fmaf(s[c], scale_log2, neg_m)));
+        // P is truncated to TF32 here (one AND, as the tensor core would
+        // truncate it) and l sums exactly the values the product uses, so
+        // the common relative shortfall cancels in O / l and the weights stay
+        // unbiased, with the error spread of rounding to nearest.
+        const float p = __uint_as_float(
+            __float_as_uint(fast_exp2(fmaf(s[c], scale_log2, neg_m))) & 0xffffe000u);
         s[c] = p;
         sp[c & 7] += p;
       }
