@@ -472,13 +472,17 @@ __global__ void __launch_bounds__(192, MINB)
           s[c] = valid ? s[c] : -INFINITY;
         }
       }
+      // Eight partial maxima, two new scores per three-input max.
       float mp[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mp[u] = s[u];
+      for (int u = 0; u < 8; ++u) mp[u] = fmaxf(s[u], s[u + 8]);
 #pragma unroll
-      for (int c = 8; c < BN; ++c) mp[c & 7] = fmaxf(mp[c & 7], s[c]);
-      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))) *
+      for (int c = 16; c + 16 <= BN; c += 16) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mp[u] = fmax3(mp[u], s[c + u], s[c + 8 + u]);
+      }
+      const float mx = fmax3(fmax3(mp[0], mp[1], mp[2]), fmax3(mp[3], mp[4], mp[5]),
+                             fmaxf(mp[6], mp[7])) *
                        scale_log2;
       // Running max with lazy rescale: keep the old reference unless the new
       // max exceeds it by more than 8 (P stays <= 256 in fp32).
@@ -493,20 +497,31 @@ __global__ void __launch_bounds__(192, MINB)
         m_run = mx;
       }
       const float neg_m = (m_run == -INFINITY) ? 0.f : -m_run;
-      float sp[8];
+      // Scores two at a time: one f32x2 FMA for s * scale - m and one f32x2
+      // add into four packed partial sums (the same eight sums, indexed by
+      // c mod 8, as scalar code would keep).
+      const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
+      const uint64_t nm2 = f2_pack(neg_m, neg_m);
+      uint64_t sp2[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) sp[u] = 0.f;
+      for (int u = 0; u < 4; ++u) sp2[u] = f2_pack(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
+      for (int c = 0; c < BN; c += 2) {
+        float t0, t1;
+        f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sc2, nm2), t0, t1);
         // P is truncated to TF32 here (one AND, as the tensor core would
         // truncate it) and l sums exactly the values the product uses, so
         // the common relative shortfall cancels in O / l and the weights stay
         // unbiased, with the error spread of rounding to nearest.
-        const float p = __uint_as_float(
-            __float_as_uint(fast_exp2(fmaf(s[c], scale_log2, neg_m))) & 0xffffe000u);
-        s[c] = p;
-        sp[c & 7] += p;
+        const float p0 = __uint_as_float(__float_as_uint(fast_exp2(t0)) & 0xffffe000u);
+        const float p1 = __uint_as_float(__float_as_uint(fast_exp2(t1)) & 0xffffe000u);
+        s[c] = p0;
+        s[c + 1] = p1;
+        sp2[(c >> 1) & 3] = f2_add(sp2[(c >> 1) & 3], f2_pack(p0, p1));
       }
+      float sp[8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) f2_unpack(sp2[u], sp[2 * u], sp[2 * u + 1]);
       l_run += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       if (__any_sync(0xffffffffu, rescale_o)) {
         // O += P_{it-1} V_{it-1} must have landed before this row is rescaled.
