@@ -188,6 +188,35 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return x >= 0.f ? x - h : h;
 }
 
+// gelu_erf on a pair, the polynomial and products on packed f32x2 FMAs and
+// multiplies (the same formula; the reciprocal and exp2 stay scalar).
+__device__ __forceinline__ void gelu_erf2(float& x0, float& x1) {
+  constexpr float kP = 0.3275911f;
+  constexpr float kA1 = 0.254829592f, kA2 = -0.284496736f, kA3 = 1.421413741f;
+  constexpr float kA4 = -1.453152027f, kA5 = 1.061405429f;
+  constexpr float kInvSqrt2 = 0.70710678118654752440f;
+  constexpr float kNegLog2e = -1.44269504088896340736f;
+  const uint64_t z = f2_mul(f2_pack(fabsf(x0), fabsf(x1)), f2_pack(kInvSqrt2, kInvSqrt2));
+  float u0, u1;
+  f2_unpack(f2_fma(f2_pack(kP, kP), z, f2_pack(1.f, 1.f)), u0, u1);
+  const uint64_t t = f2_pack(rcp_approx(u0), rcp_approx(u1));
+  uint64_t poly = f2_fma(t, f2_pack(kA5, kA5), f2_pack(kA4, kA4));
+  poly = f2_fma(t, poly, f2_pack(kA3, kA3));
+  poly = f2_fma(t, poly, f2_pack(kA2, kA2));
+  poly = f2_fma(t, poly, f2_pack(kA1, kA1));
+  poly = f2_mul(t, poly);
+  float e0, e1;
+  f2_unpack(f2_mul(f2_mul(z, z), f2_pack(kNegLog2e, kNegLog2e)), e0, e1);
+  const uint64_t q = f2_mul(poly, f2_pack(fast_exp2(e0), fast_exp2(e1)));
+  const uint64_t xx = f2_pack(x0, x1);
+  const uint64_t h = f2_mul(f2_mul(f2_pack(0.5f, 0.5f), xx), q);
+  float h0, h1, d0, d1;
+  f2_unpack(h, h0, h1);
+  f2_unpack(f2_fma(h, f2_pack(-1.f, -1.f), xx), d0, d1);  // x - h
+  x0 = x0 >= 0.f ? d0 : h0;
+  x1 = x1 >= 0.f ? d1 : h1;
+}
+
 template <int EPI>
 __device__ __forceinline__ void gemm_store_chunk(const float (&v)[32], float* __restrict__ crow,
                                                  const float* __restrict__ bias, int col0, int N,
@@ -989,7 +1018,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
             }
             if (EPI == KF_EPI_BIAS_GELU) {
 #pragma unroll
-              for (int t = 0; t < 8; ++t) o[t] = gelu_erf(o[t]);
+              for (int t = 0; t < 8; t += 2) gelu_erf2(o[t], o[t + 1]);
             }
             uint32_t hw[4], lw[4];
 #pragma unroll
