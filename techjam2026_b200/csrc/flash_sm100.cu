@@ -587,9 +587,9 @@ __global__ void __launch_bounds__(192, MINB)
             for (int c = 0; c < DH / 32; ++c) {
               float o[32];
               tmem_ld32(t_row + Cfg::O_COL + c * 32, o);
-#pragma unroll
-              for (int t = 0; t < 32; ++t) o[t] = rnd ? round_tf32(o[t] * inv_l) : o[t] * inv_l;
               if (!split) {
+#pragma unroll
+                for (int t = 0; t < 32; ++t) o[t] = rnd ? round_tf32(o[t] * inv_l) : o[t] * inv_l;
                 uint8_t* rowp = sQ + c * BM * 128 + quarter * 32 * 128 + lane * 128;
 #pragma unroll
                 for (int u = 0; u < 8; ++u)
@@ -603,11 +603,12 @@ __global__ void __launch_bounds__(192, MINB)
                   uint32_t hw[4], lw[4];
 #pragma unroll
                   for (int e = 0; e < 4; ++e) {
-                    uint16_t h0, h1, l0, l1;
-                    split_bf16(o[8 * u + 2 * e], h0, l0);
-                    split_bf16(o[8 * u + 2 * e + 1], h1, l1);
-                    hw[e] = h0 | (static_cast<uint32_t>(h1) << 16);
-                    lw[e] = l0 | (static_cast<uint32_t>(l1) << 16);
+                    // O / l and the hi/lo split, two columns per packed op
+                    float a, bb;
+                    f2_unpack(f2_mul(f2_pack(o[8 * u + 2 * e], o[8 * u + 2 * e + 1]),
+                                     f2_pack(inv_l, inv_l)),
+                              a, bb);
+                    split_bf16x2(a, bb, hw[e], lw[e]);
                   }
                   const uint32_t off = ((static_cast<uint32_t>((c & 1) * 4 + u)) ^ sw) << 4;
                   *reinterpret_cast<uint4*>(hrow + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);

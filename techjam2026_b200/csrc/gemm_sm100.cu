@@ -1011,10 +1011,12 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
             {
               const float4 b0 = *reinterpret_cast<const float4*>(sbias + c + 8 * j);
               const float4 b1 = *reinterpret_cast<const float4*>(sbias + c + 8 * j + 4);
-              o[0] = v[8 * j] + b0.x, o[1] = v[8 * j + 1] + b0.y;
-              o[2] = v[8 * j + 2] + b0.z, o[3] = v[8 * j + 3] + b0.w;
-              o[4] = v[8 * j + 4] + b1.x, o[5] = v[8 * j + 5] + b1.y;
-              o[6] = v[8 * j + 6] + b1.z, o[7] = v[8 * j + 7] + b1.w;
+              const float bs[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+              for (int t = 0; t < 8; t += 2)  // accumulator + bias, two columns per add
+                f2_unpack(f2_add(f2_pack(v[8 * j + t], v[8 * j + t + 1]),
+                                 f2_pack(bs[t], bs[t + 1])),
+                          o[t], o[t + 1]);
             }
             if (EPI == KF_EPI_BIAS_GELU) {
 #pragma unroll
@@ -1022,14 +1024,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
             }
             uint32_t hw[4], lw[4];
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const __nv_bfloat162 hi = __floats2bfloat162_rn(o[2 * t], o[2 * t + 1]);
-              const float2 hf = __bfloat1622float2(hi);
-              const __nv_bfloat162 lo =
-                  __floats2bfloat162_rn(o[2 * t] - hf.x, o[2 * t + 1] - hf.y);
-              hw[t] = *reinterpret_cast<const uint32_t*>(&hi);
-              lw[t] = *reinterpret_cast<const uint32_t*>(&lo);
-            }
+            for (int t = 0; t < 4; ++t) split_bf16x2(o[2 * t], o[2 * t + 1], hw[t], lw[t]);
             hu[j] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
             lu[j] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
           }
@@ -1053,8 +1048,9 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float4 bb = *reinterpret_cast<const float4*>(sbias + c + 4 * j);
-            float4 o = make_float4(v[4 * j] + bb.x, v[4 * j + 1] + bb.y, v[4 * j + 2] + bb.z,
-                                   v[4 * j + 3] + bb.w);
+            float4 o;
+            f2_unpack(f2_add(f2_pack(v[4 * j], v[4 * j + 1]), f2_pack(bb.x, bb.y)), o.x, o.y);
+            f2_unpack(f2_add(f2_pack(v[4 * j + 2], v[4 * j + 3]), f2_pack(bb.z, bb.w)), o.z, o.w);
             if (EPI == KF_EPI_BIAS_GELU) {
               o.x = gelu_erf(o.x);
               o.y = gelu_erf(o.y);

@@ -565,6 +565,19 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
+// split_bf16 on a pair, as packed words (a in the low half): hi = bf16(x),
+// lo = bf16(x - hi), with one paired conversion each and one f32x2 FMA for
+// the two differences (x - hi is exact-rounded as the scalar subtraction).
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hw, uint32_t& lw) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const float2 hf = __bfloat1622float2(h);
+  float d0, d1;
+  f2_unpack(f2_fma(f2_pack(hf.x, hf.y), f2_pack(-1.f, -1.f), f2_pack(a, b)), d0, d1);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(d0, d1);
+  hw = *reinterpret_cast<const uint32_t*>(&h);
+  lw = *reinterpret_cast<const uint32_t*>(&l);
+}
+
 // 2^x on the SFU (ex2.approx: max relative error 2^-22 over the full range).
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
