@@ -186,14 +186,6 @@ __global__ void __launch_bounds__(192, MINB)
   pdl_launch_dependents();
   pdl_wait();  // Q/K/V and the key bits come from earlier kernels
 
-  // Optional skip of a query tile without any valid query (rows later masked).
-  bool skip = false;
-  if ((flags & KF_ATTN_SKIP_EMPTY_Q) && bits_b) {
-    uint32_t any = 0;
-    for (int w = q0 >> 5; w < ((q0 + BM) >> 5) && w < words; ++w) any |= __ldg(bits_b + w);
-    skip = (any == 0);
-  }
-
   const int n_kv_all = (S + BN - 1) / BN;
   int kv_end = n_kv_all;
   if (causal) {
@@ -203,18 +195,31 @@ __global__ void __launch_bounds__(192, MINB)
   }
 
   // Stage the key bits of keys [0, kv_end * BN) once; every role then tests
-  // tiles and masks keys from shared memory.
+  // tiles and masks keys from shared memory. The staged range holds the
+  // query tile's own words (kv_end * BN > its last query), so the same loads
+  // tell whether the tile has a valid query and the optional skip of a tile
+  // without one (rows later masked) costs no second round trip to memory.
   const uint32_t* kb = bits_b;
-  if (bits_b && !skip) {
+  int any_q = 0;
+  if (bits_b) {
+    const int qw0 = q0 >> 5;
+    const int qw1 = ((q0 + BM) >> 5) < words ? ((q0 + BM) >> 5) : words;
     const int need = (kv_end * BN + 31) >> 5;
     const int nw = need < words ? need : words;
     if (nw <= Cfg::BITS_WORDS) {
       uint32_t* sbits = reinterpret_cast<uint32_t*>(smem + Cfg::BITS_OFF);
-      for (int w = threadIdx.x; w < nw; w += blockDim.x) sbits[w] = __ldg(bits_b + w);
+      for (int w = threadIdx.x; w < nw; w += blockDim.x) {
+        const uint32_t v = __ldg(bits_b + w);
+        sbits[w] = v;
+        if (w >= qw0 && w < qw1 && v) any_q = 1;
+      }
       kb = sbits;
+    } else {
+      for (int w = qw0 + threadIdx.x; w < qw1; w += blockDim.x)
+        if (__ldg(bits_b + w)) any_q = 1;
     }
   }
-  __syncthreads();
+  const bool skip = __syncthreads_or(any_q) == 0 && (flags & KF_ATTN_SKIP_EMPTY_Q) && bits_b;
 
   if (skip) {
     // Zero rows, written coalesced: one 32-row box of zeros in shared memory

@@ -791,6 +791,37 @@ def _reference_rows(q, k, v, keep, causal, rows):
     return p @ v.double()
 
 
+@pytest.mark.parametrize("Dh,S", [(16, 777), (64, 777), (128, 777), (256, 777), (64, 66000)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_flash_skip_empty_query_tiles(Dh, S, causal):
+    """KF_ATTN_SKIP_EMPTY_Q: tiles holding a valid query are bit-identical to
+    the unskipped kernel and a tile without one is zeroed. Valid rows are not
+    a prefix; one tile is empty in the middle of a sequence; S = 66000 keeps
+    the key bits in global memory (too long for the shared-memory staging)."""
+    from techjam2026_b200 import _lib
+    torch.manual_seed(Dh + S)
+    B, H = 3, 2
+    q, k, v = (torch.randn(B, H, S, Dh, device="cuda") for _ in range(3))
+    keep = (torch.rand(B, S, device="cuda") > 0.2).to(torch.uint8)
+    keep[0, 128:256] = 0          # an empty tile inside sequence 0
+    keep[1, 300:] = 0             # sequence 1 ends at 300: tiles 3.. are empty
+    keep[2] = 0                   # sequence 2 has no valid token at all
+    flags = _lib.KF_ATTN_CAUSAL if causal else 0
+    full = torch.empty(B, H, S, Dh, device="cuda")
+    _flash_raw(q, k, v, keep, full, flags, full.stride()[:3])
+    o = torch.full((B, H, S, Dh), 7.0, device="cuda")
+    _flash_raw(q, k, v, keep, o, flags | _lib.KF_ATTN_SKIP_EMPTY_Q, o.stride()[:3])
+    n_t = (S + 127) // 128
+    tile_live = torch.zeros(B, n_t, dtype=torch.bool, device="cuda")
+    for t in range(n_t):
+        tile_live[:, t] = keep[:, t * 128:(t + 1) * 128].any(dim=1)
+    row_live = tile_live.repeat_interleave(128, dim=1)[:, :S]
+    live = row_live[:, None, :, None].expand_as(o)
+    assert torch.equal(o[live], full[live])
+    assert torch.all(o[~live] == 0.0)
+    assert int((~row_live).sum()) > 0
+
+
 @pytest.mark.parametrize("Dh,S", [(64, 66000), (256, 15000)])
 def test_flash_key_bits_beyond_shared_memory_staging(Dh, S):
     """Rows whose key bits exceed the shared-memory staging area (2048 words
