@@ -218,6 +218,24 @@ int kf_flash_fwd_tf32(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm, 
                       int64_t o_sm, const uint32_t* keep_bits, int64_t B, int64_t H, int64_t S,
                       int dh, int dh_out, float sm_scale, int flags, void* stream);
 
+/* Batch rows of a kf_keep_bits workspace ranked by valid-key count, longest
+ * first (ties by row index): order[rank] = b, order holding B int32. One
+ * CTA; batches of more than 4096 rows get the identity order. No reference
+ * counterpart (the reference's Triton grid runs rows in batch order). */
+int kf_batch_order(const uint32_t* bits, int64_t B, int64_t S, int32_t* order, void* stream);
+
+/* kf_flash_fwd_tf32 with the grid's batch rows taken in the order of
+ * batch_order (a kf_batch_order result written by an earlier kernel in the
+ * stream): the longest rows' heavy causal tiles start first, so the launch
+ * ends on short rows instead of waiting for a late long one. Results are
+ * the same bit for bit as kf_flash_fwd_tf32's; only the schedule changes. */
+int kf_flash_fwd_tf32_ordered(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
+                              const float* k, int64_t k_sb, int64_t k_sh, int64_t k_sm,
+                              const float* v, int64_t v_sb, int64_t v_sh, int64_t v_sm, float* o,
+                              int64_t o_sb, int64_t o_sh, int64_t o_sm, const uint32_t* keep_bits,
+                              const int32_t* batch_order, int64_t B, int64_t H, int64_t S, int dh,
+                              int dh_out, float sm_scale, int flags, void* stream);
+
 /* ----------------------------------------------------------- no-allocation variant */
 
 /* Capacity of the library's static key-bit scratch: 1 MiB per device. */

@@ -50,6 +50,13 @@ SIGNATURES = {
                                    _c_ptr, _c_i64, _c_i64, _c_i64,
                                    _c_ptr, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_float,
                                    _c_int, _c_ptr]),
+    "kf_batch_order": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr]),
+    "kf_flash_fwd_tf32_ordered": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64,
+                                           _c_ptr, _c_i64, _c_i64, _c_i64,
+                                           _c_ptr, _c_i64, _c_i64, _c_i64,
+                                           _c_ptr, _c_i64, _c_i64, _c_i64,
+                                           _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_int,
+                                           _c_int, _c_float, _c_int, _c_ptr]),
     "kf_round_tf32": (_c_int, [_c_ptr, _c_ptr, _c_i64, _c_ptr]),
     "kf_flash_fwd_tf32_keep_noalloc": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64,
                                                 _c_ptr, _c_i64, _c_i64, _c_i64,

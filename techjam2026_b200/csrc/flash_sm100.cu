@@ -105,7 +105,8 @@ __global__ void __launch_bounds__(192, MINB)
                           const __grid_constant__ CUtensorMap tmV,
                           const __grid_constant__ CUtensorMap tmO, float* __restrict__ O,
                           int64_t o_sb, int64_t o_sh, int64_t o_sm,
-                          const uint32_t* __restrict__ keep_bits, int H, int S, int dh_out,
+                          const uint32_t* __restrict__ keep_bits,
+                          const int32_t* __restrict__ batch_order, int H, int S, int dh_out,
                           float scale_log2, int flags) {
   using Cfg = FlashCfg<DH, BN, KST, VST, MINB>;
   constexpr int BM = Cfg::BM;
@@ -133,9 +134,12 @@ __global__ void __launch_bounds__(192, MINB)
   // tiles of one (b, h) run together and share its K/V in L2 (a long
   // sequence's K/V is 32 MB per head -- streaming every head at once would
   // re-read K/V from HBM for every query tile). Within a head the heaviest
-  // causal tiles go first.
+  // causal tiles go first. With a batch order (kf_batch_order: rows by
+  // valid length, longest first) grid row y / H runs batch row
+  // batch_order[y / H], so the longest rows' heavy tiles start first and the
+  // launch ends on short ones; it is read after the wait on the previous
+  // kernel.
   const int bh = blockIdx.y;
-  const int b = bh / H;
   const int h = bh % H;
   const int nb = static_cast<int>(gridDim.y) / H;
   const int n_qt = gridDim.x;
@@ -144,7 +148,6 @@ __global__ void __launch_bounds__(192, MINB)
   const bool causal = (flags & KF_ATTN_CAUSAL) != 0;
   const bool split = (flags & KF_ATTN_OUT_BF16X2) != 0;
   const int words = (S + 31) >> 5;
-  const uint32_t* bits_b = keep_bits ? keep_bits + static_cast<int64_t>(b) * words : nullptr;
 
   // Set-up that reads nothing an earlier kernel writes (barriers, TMEM,
   // descriptor prefetch) runs before the wait on the previous kernel, so it
@@ -184,7 +187,13 @@ __global__ void __launch_bounds__(192, MINB)
   // TMEM, so a CTA of the next kernel that allocates TMEM before its own wait
   // can only ever wait for columns that a running CTA will free.
   pdl_launch_dependents();
-  pdl_wait();  // Q/K/V and the key bits come from earlier kernels
+  pdl_wait();  // Q/K/V, the key bits and the batch order come from earlier kernels
+  int b = bh / H;
+  if (batch_order) {
+    const int ob = __ldg(batch_order + b);
+    b = (ob >= 0 && ob < nb) ? ob : b;
+  }
+  const uint32_t* bits_b = keep_bits ? keep_bits + static_cast<int64_t>(b) * words : nullptr;
 
   const int n_kv_all = (S + BN - 1) / BN;
   int kv_end = n_kv_all;
@@ -699,8 +708,8 @@ __global__ void __launch_bounds__(192, MINB)
 template <int DH, int BN, int KST, int VST, int MINB>
 static int launch_flash(const float* q, const int64_t* qs, const float* k, const int64_t* ks,
                         const float* v, const int64_t* vs, float* o, const int64_t* os,
-                        const uint32_t* bits, int B, int H, int S, int dh_stored, int dh_out,
-                        float scale_log2, int flags, cudaStream_t st) {
+                        const uint32_t* bits, const int32_t* order, int B, int H, int S,
+                        int dh_stored, int dh_out, float scale_log2, int flags, cudaStream_t st) {
   using Cfg = FlashCfg<DH, BN, KST, VST, MINB>;
   CUtensorMap tq, tk, tv;
   const uint64_t dims[4] = {static_cast<uint64_t>(dh_stored), static_cast<uint64_t>(S),
@@ -767,7 +776,7 @@ static int launch_flash(const float* q, const int64_t* qs, const float* k, const
   const int n_qt = (S + Cfg::BM - 1) / Cfg::BM;
   dim3 grid(static_cast<unsigned>(n_qt), static_cast<unsigned>(B * H));
   return cuda_status(launch_chained(kern, grid, dim3(192), Cfg::SMEM_BYTES, st, tq, tk, tv, to, o,
-                                    os[0], os[1], os[2], bits, H, S, dh_out, scale_log2, flags),
+                                    os[0], os[1], os[2], bits, order, H, S, dh_out, scale_log2, flags),
                      "kf_flash_fwd_tf32 launch");
 }
 
@@ -775,12 +784,12 @@ static int launch_flash(const float* q, const int64_t* qs, const float* k, const
 
 using namespace kf;
 
-extern "C" int kf_flash_fwd_tf32(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
-                                 const float* k, int64_t k_sb, int64_t k_sh, int64_t k_sm,
-                                 const float* v, int64_t v_sb, int64_t v_sh, int64_t v_sm,
-                                 float* o, int64_t o_sb, int64_t o_sh, int64_t o_sm,
-                                 const uint32_t* keep_bits, int64_t B, int64_t H, int64_t S,
-                                 int dh, int dh_out, float sm_scale, int flags, void* stream) {
+static int flash_fwd_impl(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
+                          const float* k, int64_t k_sb, int64_t k_sh, int64_t k_sm,
+                          const float* v, int64_t v_sb, int64_t v_sh, int64_t v_sm, float* o,
+                          int64_t o_sb, int64_t o_sh, int64_t o_sm, const uint32_t* keep_bits,
+                          const int32_t* order, int64_t B, int64_t H, int64_t S, int dh,
+                          int dh_out, float sm_scale, int flags, void* stream) {
   if (!q || !k || !v || !o || B < 0 || H < 0 || S < 0) {
     set_last_error("kf_flash_fwd_tf32: invalid arguments");
     return KF_E_INVALID;
@@ -828,19 +837,46 @@ extern "C" int kf_flash_fwd_tf32(const float* q, int64_t q_sb, int64_t q_sh, int
   const int Bi = static_cast<int>(B), Hi = static_cast<int>(H), Si = static_cast<int>(S);
   switch (dh) {
     case 16:
-      return launch_flash<16, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+      return launch_flash<16, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi, Si, dh,
                                            dh_out, scale_log2, f, st);
     case 32:
-      return launch_flash<32, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+      return launch_flash<32, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi, Si, dh,
                                            dh_out, scale_log2, f, st);
     case 64:
-      return launch_flash<64, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+      return launch_flash<64, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi, Si, dh,
                                            dh_out, scale_log2, f, st);
     case 128:
-      return launch_flash<128, 64, 2, 2, 1>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+      return launch_flash<128, 64, 2, 2, 1>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi, Si, dh,
                                             dh_out, scale_log2, f, st);
     default:
-      return launch_flash<256, 32, 2, 1, 1>(q, qs, k, ks, v, vs, o, os, keep_bits, Bi, Hi, Si, dh,
+      return launch_flash<256, 32, 2, 1, 1>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi, Si, dh,
                                             dh_out, scale_log2, f, st);
   }
+}
+
+extern "C" int kf_flash_fwd_tf32(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
+                                 const float* k, int64_t k_sb, int64_t k_sh, int64_t k_sm,
+                                 const float* v, int64_t v_sb, int64_t v_sh, int64_t v_sm,
+                                 float* o, int64_t o_sb, int64_t o_sh, int64_t o_sm,
+                                 const uint32_t* keep_bits, int64_t B, int64_t H, int64_t S,
+                                 int dh, int dh_out, float sm_scale, int flags, void* stream) {
+  return flash_fwd_impl(q, q_sb, q_sh, q_sm, k, k_sb, k_sh, k_sm, v, v_sb, v_sh, v_sm, o, o_sb,
+                        o_sh, o_sm, keep_bits, nullptr, B, H, S, dh, dh_out, sm_scale, flags,
+                        stream);
+}
+
+extern "C" int kf_flash_fwd_tf32_ordered(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
+                                         const float* k, int64_t k_sb, int64_t k_sh, int64_t k_sm,
+                                         const float* v, int64_t v_sb, int64_t v_sh, int64_t v_sm,
+                                         float* o, int64_t o_sb, int64_t o_sh, int64_t o_sm,
+                                         const uint32_t* keep_bits, const int32_t* batch_order,
+                                         int64_t B, int64_t H, int64_t S, int dh, int dh_out,
+                                         float sm_scale, int flags, void* stream) {
+  if (!batch_order) {
+    set_last_error("kf_flash_fwd_tf32_ordered: batch_order is null");
+    return KF_E_INVALID;
+  }
+  return flash_fwd_impl(q, q_sb, q_sh, q_sm, k, k_sb, k_sh, k_sm, v, v_sb, v_sh, v_sm, o, o_sb,
+                        o_sh, o_sm, keep_bits, batch_order, B, H, S, dh, dh_out, sm_scale, flags,
+                        stream);
 }

@@ -171,6 +171,43 @@ __global__ void split_bf16x2_kernel(const float* __restrict__ src, int64_t rows,
   }
 }
 
+// Batch rows ranked by valid-key count, longest first (ties by index), from
+// the packed key bits: order[rank] = b. One CTA of 1024 threads; the counts
+// of up to KF_ORDER_MAX_B rows sit in shared memory, a larger batch gets the
+// identity order. A scheduling hint only: attention's results do not depend
+// on the order its CTAs run in.
+constexpr int KF_ORDER_MAX_B = 4096;
+
+__global__ void __launch_bounds__(1024) batch_order_kernel(const uint32_t* __restrict__ bits,
+                                                           int B, int words,
+                                                           int32_t* __restrict__ order) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ int len[KF_ORDER_MAX_B];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  if (B > KF_ORDER_MAX_B) {
+    for (int b = threadIdx.x; b < B; b += blockDim.x) order[b] = b;
+    return;
+  }
+  for (int b = warp; b < B; b += nwarps) {
+    int n = 0;
+    for (int w = lane; w < words; w += 32) n += __popc(bits[static_cast<int64_t>(b) * words + w]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+    if (lane == 0) len[b] = n;
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const int lb = len[b];
+    int rank = 0;
+    for (int c = 0; c < B; ++c) {
+      const int lc = len[c];
+      rank += (lc > lb) || (lc == lb && c < b);
+    }
+    order[rank] = b;
+  }
+}
+
 __global__ void round_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst,
                                   int64_t n) {
   pdl_launch_dependents();
@@ -233,6 +270,20 @@ extern "C" int kf_live_row_tiles(const uint8_t* keep, int64_t M, int32_t* tiles,
   return cuda_status(launch_chained(live_row_tiles_kernel, dim3(1), dim3(1024), 0,
                                     static_cast<cudaStream_t>(stream), keep, M, tiles, count),
                      "kf_live_row_tiles launch");
+}
+
+extern "C" int kf_batch_order(const uint32_t* bits, int64_t B, int64_t S, int32_t* order,
+                              void* stream) {
+  if (!bits || !order || B <= 0 || S <= 0 || B > INT32_MAX || S > INT32_MAX) {
+    set_last_error("kf_batch_order: invalid arguments (B=%lld S=%lld)", (long long)B,
+                   (long long)S);
+    return KF_E_INVALID;
+  }
+  const int words = static_cast<int>((S + 31) / 32);
+  return cuda_status(launch_chained(batch_order_kernel, dim3(1), dim3(1024), 0,
+                                    static_cast<cudaStream_t>(stream), bits,
+                                    static_cast<int>(B), words, order),
+                     "kf_batch_order launch");
 }
 
 extern "C" int kf_split_bf16x2(const float* src, int64_t rows, int64_t cols, int64_t ld_src,

@@ -88,6 +88,12 @@ class Plan:
     sk_ffn1: bool = False
     sk_ffn2: bool = False
 
+    # Attention walks the batch rows longest first (kf_batch_order, one small
+    # kernel per forward): a launch of several waves then ends on short
+    # rows instead of a late long row's heavy causal tiles. Schedule only;
+    # bit-identical output.
+    order_rows: bool = False
+
     # Narrow I/O dtypes (float16/bfloat16): run the organiser's own layer,
     # captured whole into one CUDA graph, instead of these kernels. At those
     # dtypes the gate only admits the reference's exact arithmetic
@@ -113,6 +119,8 @@ class Plan:
             bits.append("skip-padded-rows")
         if self.fuse_ln:
             bits.append("ln-in-gemm")
+        if self.order_rows:
+            bits.append("rows-longest-first")
         if self.exact_reference:
             return "exact-reference+cuda-graph"
         if self.cuda_graph:

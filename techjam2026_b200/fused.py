@@ -116,6 +116,7 @@ class _Workspace:
         self.bits = torch.zeros(B * words, **i32)
         self.live_tiles = torch.zeros((M + 127) // 128, **i32)
         self.live_count = torch.zeros(1, **i32)
+        self.order = torch.zeros(B, **i32)
         # Stream-K GEMMs share one zeroed workspace (partials + counters);
         # the kernels leave its counters zero, and they run one after another.
         sk_bytes = _Workspace.sk_bytes(cfg, M, plan)
@@ -141,7 +142,8 @@ class _Workspace:
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size()
                    for t in (self.res, self.h, self.h2, self.qkv, self.ctx, self.y, self.ffn,
-                             self.bits, self.live_tiles, self.live_count, self.sk)
+                             self.bits, self.live_tiles, self.live_count, self.order,
+                             self.sk)
                    if t is not None)
 
     @staticmethod
@@ -156,7 +158,7 @@ class _Workspace:
         per_row += 4 * d if (split["qkv"] or split["ffn1"]) else 0    # h2 planes
         per_row += 4 * 3 * H * dh_store + 4 * d + 4 * d + 4 * F       # qkv, ctx, y, ffn
         words = (S + 31) // 32
-        return (M * per_row + 4 * B * words + 4 * ((M + 127) // 128) + 4
+        return (M * per_row + 4 * B * words + 4 * B + 4 * ((M + 127) // 128) + 4
                 + _Workspace.sk_bytes(cfg, M, plan))
 
 
@@ -318,6 +320,9 @@ class FusedTransformer(LayerStack):
             run("keep_bits", L.kf_keep_bits, keep, S, B, S, bits, st)
         if skip_rows:
             run("keep_bits", L.kf_live_row_tiles, keep, M, lt, lc, st)
+        order = ws.order.data_ptr() if (keep is not None and plan.order_rows and B > 1) else None
+        if order is not None:
+            run("keep_bits", L.kf_batch_order, bits, B, S, order, st)
         l0 = w.layers[0]
         run("ln", L.kf_ln_add_mask, x.data_ptr(), d, None, 0, keep, l0["ln1w"].data_ptr(),
             l0["ln1b"].data_ptr(), res, d, h_qkv, d, M, d, l0["eps1"], f_ln1, st)
@@ -331,9 +336,15 @@ class FusedTransformer(LayerStack):
         for i, lw in enumerate(w.layers):
             gemm("qkv", "qkv", h_qkv, d, lw["wqkv"], lw["bqkv"], qkv, ldq, 3 * d, d,
                  _lib.KF_EPI_BIAS, _lib.KF_GEMM_ROUND_TF32 if R else 0, plan.bn_qkv, hd, hs)
-            run("attention", L.kf_flash_fwd_tf32, qkv, S * ldq, dhs, ldq,
-                qkv + 4 * H * dhs, S * ldq, dhs, ldq, qkv + 8 * H * dhs, S * ldq, dhs, ldq,
-                ctx, S * d, dh, d, bits, B, H, S, dhs, dh, dh ** -0.5, attn_flags, st)
+            if order is not None:
+                run("attention", L.kf_flash_fwd_tf32_ordered, qkv, S * ldq, dhs, ldq,
+                    qkv + 4 * H * dhs, S * ldq, dhs, ldq, qkv + 8 * H * dhs, S * ldq, dhs,
+                    ldq, ctx, S * d, dh, d, bits, order, B, H, S, dhs, dh, dh ** -0.5,
+                    attn_flags, st)
+            else:
+                run("attention", L.kf_flash_fwd_tf32, qkv, S * ldq, dhs, ldq,
+                    qkv + 4 * H * dhs, S * ldq, dhs, ldq, qkv + 8 * H * dhs, S * ldq, dhs,
+                    ldq, ctx, S * d, dh, d, bits, B, H, S, dhs, dh, dh ** -0.5, attn_flags, st)
             # out_proj, then the residual add + mask + LN2 (fused into the
             # GEMM's epilogue when the plan allows it).
             if fuse["out"]:

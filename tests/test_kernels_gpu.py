@@ -822,6 +822,70 @@ def test_flash_skip_empty_query_tiles(Dh, S, causal):
     assert int((~row_live).sum()) > 0
 
 
+@pytest.mark.parametrize("B,S", [(1, 100), (7, 333), (64, 2048), (300, 64), (4097, 32)])
+def test_batch_order_ranks_rows_longest_first(B, S):
+    """kf_batch_order: a permutation of the rows by valid-key count, longest
+    first, ties by row index; identity above 4096 rows."""
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    g = torch.Generator().manual_seed(B + S)
+    lengths = torch.randint(0, S + 1, (B,), generator=g)
+    lengths[: B // 3] = lengths[0]                      # ties
+    keep = (torch.rand(B, S, generator=g) < 0.7).to(torch.uint8)
+    keep &= (torch.arange(S)[None, :] < lengths[:, None]).to(torch.uint8)
+    keep = keep.cuda()
+    bits = torch.empty(int(L.kf_keep_bits_words(B, S)), dtype=torch.int32, device="cuda")
+    st = _lib.stream_ptr()
+    _lib.check(L.kf_keep_bits(keep.data_ptr(), S, B, S, bits.data_ptr(), st), "kf_keep_bits")
+    order = torch.full((B,), -1, dtype=torch.int32, device="cuda")
+    _lib.check(L.kf_batch_order(bits.data_ptr(), B, S, order.data_ptr(), st), "kf_batch_order")
+    got = order.cpu().tolist()
+    if B > 4096:
+        assert got == list(range(B))
+        return
+    n = keep.sum(dim=1).cpu().tolist()
+    assert got == sorted(range(B), key=lambda b: (-n[b], b))
+
+
+@pytest.mark.parametrize("Dh", [16, 64, 128, 256])
+def test_flash_ordered_rows_are_bit_identical(Dh):
+    """kf_flash_fwd_tf32_ordered only changes which CTA runs when: same bits
+    as kf_flash_fwd_tf32 on ragged, non-prefix masks (split output)."""
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    torch.manual_seed(Dh)
+    B, H, S = 6, 2, 700
+    d = H * Dh
+    qkv = torch.randn(B, S, 3, H, Dh, device="cuda")
+    q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+    lengths = torch.tensor([700, 5, 333, 0, 699, 128])
+    keep = (torch.arange(S)[None, :] < lengths[:, None]).to(torch.uint8)
+    keep &= (torch.rand(B, S) < 0.9).to(torch.uint8)
+    keep = keep.cuda()
+    st = _lib.stream_ptr()
+    bits = torch.empty(int(L.kf_keep_bits_words(B, S)), dtype=torch.int32, device="cuda")
+    _lib.check(L.kf_keep_bits(keep.data_ptr(), S, B, S, bits.data_ptr(), st), "kf_keep_bits")
+    order = torch.empty(B, dtype=torch.int32, device="cuda")
+    _lib.check(L.kf_batch_order(bits.data_ptr(), B, S, order.data_ptr(), st), "kf_batch_order")
+    flags = _lib.KF_ATTN_CAUSAL | _lib.KF_ATTN_SKIP_EMPTY_Q | _lib.KF_ATTN_OUT_BF16X2
+    qs = q.stride()
+    outs = []
+    for ordered in (False, True):
+        o = torch.full((2, B, S, d), 7, dtype=torch.int16, device="cuda")
+        args = [q.data_ptr(), *qs[:3], k.data_ptr(), *qs[:3], v.data_ptr(), *qs[:3],
+                o.data_ptr(), S * d, Dh, d, bits.data_ptr()]
+        if ordered:
+            rc = L.kf_flash_fwd_tf32_ordered(*args, order.data_ptr(), B, H, S, Dh, Dh,
+                                             Dh ** -0.5, flags, st)
+        else:
+            rc = L.kf_flash_fwd_tf32(*args, B, H, S, Dh, Dh, Dh ** -0.5, flags, st)
+        _lib.check(rc, "attention")
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    assert order.cpu().tolist()[-1] == 3          # the row without a valid key runs last
+
+
 @pytest.mark.parametrize("Dh,S", [(64, 66000), (256, 15000)])
 def test_flash_key_bits_beyond_shared_memory_staging(Dh, S):
     """Rows whose key bits exceed the shared-memory staging area (2048 words

@@ -264,3 +264,28 @@ def test_stream_k_gemms_share_one_workspace_and_pass_the_gate():
 def _lib_status():
     from techjam2026_b200 import _lib
     return _lib.lib().kf_device_status(0)
+
+
+@pytest.mark.parametrize("wname", ["c4", "c3b"])
+def test_rows_longest_first_is_bit_identical(wname):
+    """plan.order_rows (kf_batch_order + kf_flash_fwd_tf32_ordered) changes
+    only the attention schedule: the forward is bit-identical with and
+    without it, eager and graph, on ragged batches."""
+    import dataclasses
+    w = WORKLOADS[wname]
+    cfg = dataclasses.replace(w.cfg, batch_size=6, num_layers=1)
+    sd = make_state_dict(cfg, 5)
+    x, mask = generate_case(cfg, 5, w.padding_ratio, w.input_scale)
+    xd, md = x.cuda(), mask.cuda()
+    outs = []
+    for order_rows in (False, True):
+        from techjam2026_b200.dispatch import DispatchTable, probe
+        spec = probe()
+        plan, _ = DispatchTable.load_for(spec).lookup(spec.arch, torch.float32, cfg)
+        m = _model(cfg, sd, dataclasses.replace(plan, order_rows=order_rows))
+        outs.append((m(xd, md).clone(), m.eager_forward(xd, md).clone()))
+        m.release_buffers()
+    torch.cuda.synchronize()
+    assert _lib_status() == 0
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    assert padded_rows_exactly_zero(outs[1][0], mask)
