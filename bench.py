@@ -488,8 +488,21 @@ def main():
         if world > 1:
             dist.all_reduce(p_ms, op=dist.ReduceOp.MAX)
         e_step = float(p_ms.item()) / args.steps
+        # The L2 flush before each forward sits inside this timed region (it
+        # is queued on the compute stream between the steps): its own time,
+        # so the loop's overhead over the forward can be read off.
+        f_ts = []
+        for _ in range(5):
+            f0 = torch.cuda.Event(enable_timing=True)
+            f1 = torch.cuda.Event(enable_timing=True)
+            f0.record()
+            flush.zero_()
+            f1.record()
+            torch.cuda.synchronize()
+            f_ts.append(f0.elapsed_time(f1))
         e2e = {"value": round(flops_all / (e_step / 1e3) / 1e12, 3), "unit": "TFLOP/s",
                "ms_per_step": round(e_step, 4),
+               "l2_flush_ms_per_step_inside": round(statistics.median(f_ts), 4),
                "h2d_bytes_per_step": int(xh.numel() * 4 + mh.numel()),
                "d2h_bytes_per_step": int(oh.numel() * 4),
                "loop": "StreamedForward: copies on two streams overlap the forward",
