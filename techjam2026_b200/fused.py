@@ -460,15 +460,32 @@ class GraphRunner:
     callers legitimately hold results)."""
 
     def __init__(self, model: FusedTransformer, x: torch.Tensor,
-                 mask: Optional[torch.Tensor]):
+                 mask: Optional[torch.Tensor], out: Optional[torch.Tensor] = None,
+                 ws: Optional["_Workspace"] = None):
+        """With `out` given, x, mask and out themselves are the graph's
+        buffers (no copies: the caller writes inputs into x and mask and reads
+        results from out; mask must then be a contiguous bool tensor, read
+        as bytes in place), and `ws` may be a workspace shared with other
+        runners that never run at the same time."""
         self.model = model
         B, S, d = x.shape
-        self.static_x = x.detach().clone().contiguous()
-        self.static_keep = None if mask is None else model._keep_u8(mask).clone()
-        self.static_out = torch.empty_like(self.static_x)
+        if out is None:
+            self.static_x = x.detach().clone().contiguous()
+            self.static_keep = None if mask is None else model._keep_u8(mask).clone()
+            self.static_out = torch.empty_like(self.static_x)
+        else:
+            if not (x.is_contiguous() and out.is_contiguous() and out.shape == x.shape
+                    and out.dtype == x.dtype and out.device == x.device):
+                raise ValueError("bound buffers must be contiguous tensors of one shape")
+            if mask is not None and (mask.dtype != torch.bool or not mask.is_contiguous()):
+                raise ValueError("a bound mask must be a contiguous bool tensor")
+            self.static_x = x
+            self.static_keep = None if mask is None else model._keep_u8(mask)
+            self.static_out = out
         self.weights = model.prepare(x.device)
-        # A workspace of its own: eager calls of other shapes never alias it.
-        self.ws = _Workspace(model.config, B, S, x.device, model.plan)
+        # A workspace of its own unless shared: eager calls of other shapes
+        # never alias it.
+        self.ws = ws if ws is not None else _Workspace(model.config, B, S, x.device, model.plan)
         side = torch.cuda.Stream(device=x.device)
         side.wait_stream(torch.cuda.current_stream(x.device))
         with torch.cuda.stream(side):

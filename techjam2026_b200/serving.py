@@ -9,8 +9,11 @@ another. PCIe is full duplex and the GPU has several copy engines, so in
 steady state a batch costs the longest of the three, not their sum. Device
 buffers are double-buffered; every batch still crosses PCIe both ways.
 
-The forward itself is the model's CUDA graph (`FusedTransformer.graph_runner`),
-so results are bit-identical to calling the model on each batch.
+The forward itself is the model's CUDA graph, so results are bit-identical
+to calling the model on each batch. For a `FusedTransformer` with a bool
+mask (or none) there is one graph per buffer slot, captured on that slot's
+upload and download buffers, so a step makes no device-side copy; other
+models use their `graph_runner` and copy into and out of its buffers.
 """
 from __future__ import annotations
 
@@ -18,7 +21,7 @@ from typing import List, Optional, Sequence
 
 import torch
 
-from .fused import FusedTransformer
+from .fused import FusedTransformer, GraphRunner, _Workspace
 
 
 class StreamedForward:
@@ -33,14 +36,23 @@ class StreamedForward:
         if not x_example.is_cuda:
             raise ValueError("x_example must be a CUDA tensor of the batch shape")
         self.device = x_example.device
-        self.runner = model.graph_runner(x_example, mask_example)
         self.with_mask = mask_example is not None
-        self.xd = [torch.empty_like(x_example) for _ in range(2)]
-        self.md = ([torch.empty_like(mask_example) for _ in range(2)]
+        self.xd = [torch.empty_like(x_example).contiguous() for _ in range(2)]
+        self.md = ([torch.empty_like(mask_example).contiguous() for _ in range(2)]
                    if self.with_mask else [None, None])
-        self.od = [torch.empty_like(x_example) for _ in range(2)]
+        self.od = [torch.empty_like(x_example).contiguous() for _ in range(2)]
         self.up = torch.cuda.Stream(device=self.device)
         self.down = torch.cuda.Stream(device=self.device)
+        self.bound = None
+        self.runner = None
+        if isinstance(model, FusedTransformer) and (
+                mask_example is None or mask_example.dtype == torch.bool):
+            B, S, _ = x_example.shape
+            ws = _Workspace(model.config, B, S, self.device, model.plan)
+            self.bound = [GraphRunner(model, self.xd[b], self.md[b], self.od[b], ws)
+                          for b in range(2)]
+        else:
+            self.runner = model.graph_runner(x_example, mask_example)
 
     def run(self, xs: Sequence[torch.Tensor], masks: Optional[Sequence[torch.Tensor]],
             outs: Sequence[torch.Tensor], before_step=None) -> None:
@@ -82,12 +94,18 @@ class StreamedForward:
             if before_step is not None:
                 before_step(k)
             comp.wait_event(uploaded[k])
-            self.runner.load_inputs(self.xd[b], self.md[b])
-            loaded[k].record(comp)
-            self.runner.replay()
-            if k >= 2:
-                comp.wait_event(downloaded[k - 2])  # result k-2 has left buffer b
-            self.od[b].copy_(self.runner.static_out)
+            if self.bound is not None:
+                if k >= 2:
+                    comp.wait_event(downloaded[k - 2])  # result k-2 has left buffer b
+                self.bound[b].replay()                  # reads xd[b], md[b]; writes od[b]
+                loaded[k].record(comp)
+            else:
+                self.runner.load_inputs(self.xd[b], self.md[b])
+                loaded[k].record(comp)
+                self.runner.replay()
+                if k >= 2:
+                    comp.wait_event(downloaded[k - 2])  # result k-2 has left buffer b
+                self.od[b].copy_(self.runner.static_out)
             computed[k].record(comp)
             with torch.cuda.stream(self.down):
                 self.down.wait_event(computed[k])

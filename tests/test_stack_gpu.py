@@ -172,10 +172,13 @@ def test_native_library_is_the_one_loaded():
     assert _lib.lib().kf_device_status(0) == 0
 
 
-def test_streamed_forward_matches_per_batch_calls():
+@pytest.mark.parametrize("mask_dtype", [torch.bool, torch.float32])
+def test_streamed_forward_matches_per_batch_calls(mask_dtype):
     """The serving loop (uploads and downloads on their own streams, double
     buffers) returns, batch for batch, exactly what calling the model on each
-    batch returns, including when consecutive batches differ."""
+    batch returns, including when consecutive batches differ. A bool mask
+    runs one graph per buffer slot bound to the upload and download buffers;
+    a float mask takes the copying path."""
     from techjam2026_b200.serving import StreamedForward
     case = load_case("mini_s333")
     cfg = case["cfg"]
@@ -184,8 +187,9 @@ def test_streamed_forward_matches_per_batch_calls():
     for seed in range(5):
         x, mask = generate_case(cfg, 100 + seed, 0.5)
         xs.append(x.pin_memory())
-        masks.append(mask.pin_memory())
+        masks.append(mask.to(mask_dtype).pin_memory())
     pipe = StreamedForward(m, xs[0].cuda(), masks[0].cuda())
+    assert (pipe.bound is not None) == (mask_dtype == torch.bool)
     outs = pipe(xs, masks)
     again = pipe(xs[::-1], masks[::-1])
     for k in range(5):
