@@ -59,6 +59,13 @@ def test_invalid_arguments_are_rejected_without_a_device(lib):
     assert lib.kf_flash_fwd_tf32(None, 1, 1, 1, None, 1, 1, 1, None, 1, 1, 1, None, 1, 1, 1,
                                  None, 1, 1, 1, 64, 64, 0.125, 0, None) == _lib.KF_E_INVALID
     assert lib.kf_round_tf32(None, None, 4, None) == _lib.KF_E_INVALID
+    assert lib.kf_batch_order(None, 4, 64, None, None) == _lib.KF_E_INVALID
+    fake = ctypes.c_void_p(0x1000)   # never dereferenced: rejected before any launch
+    assert lib.kf_batch_order(fake, 0, 64, fake, None) == _lib.KF_E_INVALID
+    assert lib.kf_flash_fwd_tf32_ordered(fake, 64, 64, 64, fake, 64, 64, 64, fake, 64, 64, 64,
+                                         fake, 64, 64, 64, fake, None, 1, 1, 8, 64, 64, 0.125,
+                                         0, None) == _lib.KF_E_INVALID
+    assert b"batch_order is null" in lib.kf_last_error()
 
 
 def test_unsupported_shapes_are_reported(lib):
