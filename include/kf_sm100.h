@@ -228,7 +228,9 @@ int kf_batch_order(const uint32_t* bits, int64_t B, int64_t S, int32_t* order, v
  * batch_order (a kf_batch_order result written by an earlier kernel in the
  * stream): the longest rows' heavy causal tiles start first, so the launch
  * ends on short rows instead of waiting for a late long one. Results are
- * the same bit for bit as kf_flash_fwd_tf32's; only the schedule changes. */
+ * the same bit for bit as kf_flash_fwd_tf32's; only the schedule changes.
+ * Stands in for the same reference call as kf_flash_fwd_tf32
+ * (kernelforge/ops/flash.py:363-422). */
 int kf_flash_fwd_tf32_ordered(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
                               const float* k, int64_t k_sb, int64_t k_sh, int64_t k_sm,
                               const float* v, int64_t v_sb, int64_t v_sh, int64_t v_sm, float* o,
