@@ -776,7 +776,8 @@ static int launch_flash(const float* q, const int64_t* qs, const float* k, const
   const int n_qt = (S + Cfg::BM - 1) / Cfg::BM;
   dim3 grid(static_cast<unsigned>(n_qt), static_cast<unsigned>(B * H));
   return cuda_status(launch_chained(kern, grid, dim3(192), Cfg::SMEM_BYTES, st, tq, tk, tv, to, o,
-                                    os[0], os[1], os[2], bits, order, H, S, dh_out, scale_log2, flags),
+                                    os[0], os[1], os[2], bits, order, H, S, dh_out, scale_log2,
+                                    flags),
                      "kf_flash_fwd_tf32 launch");
 }
 
@@ -837,20 +838,20 @@ static int flash_fwd_impl(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_
   const int Bi = static_cast<int>(B), Hi = static_cast<int>(H), Si = static_cast<int>(S);
   switch (dh) {
     case 16:
-      return launch_flash<16, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi, Si, dh,
-                                           dh_out, scale_log2, f, st);
+      return launch_flash<16, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi,
+                                           Si, dh, dh_out, scale_log2, f, st);
     case 32:
-      return launch_flash<32, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi, Si, dh,
-                                           dh_out, scale_log2, f, st);
+      return launch_flash<32, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi,
+                                           Si, dh, dh_out, scale_log2, f, st);
     case 64:
-      return launch_flash<64, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi, Si, dh,
-                                           dh_out, scale_log2, f, st);
+      return launch_flash<64, 64, 2, 2, 2>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi,
+                                           Si, dh, dh_out, scale_log2, f, st);
     case 128:
-      return launch_flash<128, 64, 2, 2, 1>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi, Si, dh,
-                                            dh_out, scale_log2, f, st);
+      return launch_flash<128, 64, 2, 2, 1>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi,
+                                            Si, dh, dh_out, scale_log2, f, st);
     default:
-      return launch_flash<256, 32, 2, 1, 1>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi, Si, dh,
-                                            dh_out, scale_log2, f, st);
+      return launch_flash<256, 32, 2, 1, 1>(q, qs, k, ks, v, vs, o, os, keep_bits, order, Bi, Hi,
+                                            Si, dh, dh_out, scale_log2, f, st);
   }
 }
 
