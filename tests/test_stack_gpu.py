@@ -293,3 +293,24 @@ def test_rows_longest_first_is_bit_identical(wname):
     assert _lib_status() == 0
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
     assert padded_rows_exactly_zero(outs[1][0], mask)
+
+
+@pytest.mark.parametrize("with_mask", [False, True])
+def test_single_token_sequences(with_mask):
+    """S = 1 (the reference's single-token case: attention returns V of the
+    one key exactly): the stack passes the gate against the oracle, graph
+    and eager agree bit for bit."""
+    import dataclasses
+    cfg = dataclasses.replace(WORKLOADS["c1"].cfg, batch_size=5, seq_len=1, num_layers=2)
+    sd = make_state_dict(cfg, 11)
+    x, mask = generate_case(cfg, 11, 0.5)
+    mask = mask if with_mask else None
+    m = _model(cfg, sd)
+    xd = x.cuda()
+    md = mask.cuda() if mask is not None else None
+    out = m(xd, md)
+    eager = m.eager_forward(xd, md)
+    torch.cuda.synchronize()
+    assert _lib_status() == 0
+    assert torch.equal(out, eager)
+    _assert_gate(_oracle(cfg, sd, x, mask), out, f"S=1 mask={with_mask}")
