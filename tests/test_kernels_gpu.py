@@ -1010,3 +1010,47 @@ def test_gemm_layernorm_fusion_matches_two_kernels(M, N, K, mode):
         ha, hb = h_a, h_b
         bound = 2e-5 + 0 * ha
     assert bool(((ha - hb).abs() <= bound).all()), (ha - hb).abs().max().item()
+
+
+# --------------------------------------------------------------- ops surface options
+
+def test_add_mask_layernorm_options():
+    """want_residual=False returns (None, h) with the same h; keep given as
+    float, bool or uint8 gives the same bits; a strided x is accepted;
+    non-fp32 outputs are refused (the reference's fp16 options are out of
+    this fp32 path)."""
+    torch.manual_seed(21)
+    M, d = 300, 256
+    wide = torch.randn(M, 2 * d, device="cuda")
+    x = wide[:, :d]                                   # row stride 2d
+    y = torch.randn(M, d, device="cuda")
+    w, b = torch.randn(d, device="cuda"), torch.randn(d, device="cuda")
+    keep_f = (torch.rand(M, device="cuda") > 0.25).float()
+    s, h = add_mask_layernorm(x, y, keep_f, w, b, mask_out=True)
+    none, h2 = add_mask_layernorm(x, y, keep_f, w, b, mask_out=True, want_residual=False)
+    assert none is None and torch.equal(h, h2)
+    for keep in (keep_f.bool(), keep_f.to(torch.uint8)):
+        s3, h3 = add_mask_layernorm(x, y, keep, w, b, mask_out=True)
+        assert torch.equal(s3, s) and torch.equal(h3, h)
+    assert torch.equal(s, (x + y) * keep_f[:, None])
+    with pytest.raises(TypeError):
+        add_mask_layernorm(x, y, keep_f, w, b, out_dtype=torch.float16)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_flash_attention_options(causal):
+    """sm_scale other than Dh^-1/2, keep=None, a caller-provided `out` view,
+    and the reference's tuning hints (smem_kb, block) accepted and ignored;
+    round_scores_to (fp16/bf16 I/O only) refused."""
+    torch.manual_seed(22)
+    B, H, S, Dh = 2, 3, 200, 64
+    q, k, v = (torch.randn(B, H, S, Dh, device="cuda") for _ in range(3))
+    scale = 0.3
+    ref = _reference_rows(q * (scale / Dh ** -0.5), k, v, None, causal, list(range(S)))
+    buf = torch.full((B, S, H, Dh), 5.0, device="cuda")
+    o = flash_attention(q, k, v, causal=causal, sm_scale=scale, smem_kb=99.0,
+                        block=(128, 64, 2, 2), out=buf.permute(0, 2, 1, 3))
+    assert o.data_ptr() == buf.data_ptr()
+    assert (buf.permute(0, 2, 1, 3).double() - ref).abs().max().item() < 5e-3
+    with pytest.raises(NotImplementedError):
+        flash_attention(q, k, v, causal=causal, round_scores_to=torch.float16)
