@@ -37,6 +37,9 @@ CASES = {
     "mini_s333": (2, 333, 64, 4, 128, 2, True, 0.5, 7),
     "mini_dh8_noncausal": (3, 40, 32, 4, 64, 2, False, 0.6, 5),
     "mini_nopad": (2, 96, 64, 2, 128, 2, True, 0.0, 11),
+    # a long ragged row: S = 4097 (one query row past 32 tiles of 128),
+    # head_dim 8, as the chunked oracle restatement is pinned at this length
+    "mini_s4097": (1, 4097, 16, 2, 32, 1, True, 0.5, 17),
     # bfloat16 I/O: the reference module cast to bf16, inputs drawn in bf16
     # (the harness's --dtype bfloat16), output in bf16.
     "mini_bf16": (2, 96, 64, 2, 128, 2, True, 0.5, 13),

@@ -9,7 +9,7 @@ import torch
 from techjam2026_b200.configs import TransformerConfig
 
 GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-CASE_NAMES = ("c1", "mini_s333", "mini_dh8_noncausal", "mini_nopad")
+CASE_NAMES = ("c1", "mini_s333", "mini_dh8_noncausal", "mini_nopad", "mini_s4097")
 
 
 def load_case(name: str) -> dict:
