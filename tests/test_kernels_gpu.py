@@ -233,6 +233,7 @@ def reference_attention(q, k, v, keep, causal, scale=None):
 @pytest.mark.parametrize("shape", [
     (2, 8, 128, 64), (1, 4, 1, 64), (2, 8, 333, 64), (1, 8, 2048, 64),
     (1, 4, 100, 128), (2, 4, 64, 32), (2, 4, 200, 16), (1, 2, 300, 256), (2, 16, 257, 8),
+    (1, 4, 1023, 64), (2, 2, 777, 32),
 ])
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("pad", [0.0, 0.4])
