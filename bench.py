@@ -1,23 +1,33 @@
 #!/usr/bin/env python3
 """Benchmark of the layer-stack forward (BASELINE.json metric) on 1..8 B200s.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4]
                     [--impl ours|reference]
 
-A step is one forward of the stack over one batch of the workload (default
-c2: 6 layers, B=8, S=512, d=512, H=8, F=2048, causal + key padding). Under
-torchrun each rank runs its own batch (seed = rank) on its own GPU with no
-collective in the data path (weak scaling); the time is the max over ranks.
+A step is one forward of the stack over one fixed global batch of the
+workload. The default is c4, the largest configuration BASELINE.json runs
+on one GPU (4 layers, B=64, S=2048, d=768, H=12, F=3072, causal, valid
+lengths U[1, 2048]). Under torchrun the global batch (seed 0) is sharded
+over the ranks -- equal row counts, cost-balanced assignment
+(sharding.BatchShard), 64/32/16/8 rows at N = 1/2/4/8 -- and each rank runs
+its rows on its own GPU with no collective in the forward (strong scaling);
+the time is the max over ranks. A batch that does not split evenly (c1's
+two rows over four GPUs) runs as replicas instead ("scaling": "weak").
 
 Rank 0 prints one JSON line:
-  value        useful TFLOP/s of all ranks (valid tokens, valid causal pairs)
-               with inputs resident in HBM: CUDA-graph replays timed with
-               CUDA events, L2 flushed (256 MiB write) between steps;
+  value        useful TFLOP/s of the whole batch (valid tokens, valid causal
+               pairs) with inputs resident in HBM: CUDA-graph replays timed
+               with CUDA events, L2 flushed (256 MiB write) between steps;
   e2e          the same metric through the public API (submission's
-               UserOptimizedTransformer): pinned host x/mask -> device ->
-               forward -> pinned host output, all inside the timed region;
+               UserOptimizedTransformer in the serving loop): every step
+               copies its rows from pinned host memory and its result back,
+               inside the timed region;
+  gather       (N > 1) the NCCL all-gather that assembles the whole [B,S,d]
+               result on every rank, timed on its own (it is not part of a
+               step: the forward needs no inter-GPU traffic);
   roofline     the dominant kernel (largest share of forward time, measured
-               live with CUDA events around each launch of an eager forward);
+               live with CUDA events around each launch of an eager forward),
+               plus attention's own fraction;
   cpu_baseline the CPU oracle (reference layer restated in PyTorch) on a
                bounded sample, rank 0 at N=1;
   clocks       nvidia-smi samples taken during the timed region.
@@ -44,8 +54,9 @@ sys.path.insert(0, ROOT)
 import torch  # noqa: E402
 
 from techjam2026_b200.configs import WORKLOADS, generate_case, make_state_dict  # noqa: E402
-from techjam2026_b200.roofline import (lengths_of, measured_peaks, profiled_traffic, useful_flops,  # noqa: E402
-                                       dense_causal_flops)
+from techjam2026_b200.roofline import (dense_causal_flops, lengths_of,  # noqa: E402
+                                       ln_bytes_per_forward, measured_peaks, profiled_traffic,
+                                       useful_flops)
 
 METRIC = "layer-stack fwd latency ms & TFLOP/s (% tcgen05 peak) at 1/2/4/8 B200 vs CPU ref"
 
@@ -55,14 +66,16 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--config", default="c2", choices=sorted(WORKLOADS))
+    p.add_argument("--config", default="c4", choices=sorted(WORKLOADS))
     p.add_argument("--impl", default="ours", choices=("ours", "reference"))
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-gather", action="store_true",
+                   help="skip the timed NCCL all-gather of the outputs (N > 1)")
     p.add_argument("--batch-size", type=int, default=None,
-                   help="rows per rank (default: the workload's batch); for bounded profiling")
+                   help="global batch (default: the workload's); for bounded profiling")
     p.add_argument("--protocol", default="contract", choices=("contract", "organiser"),
                    help="organiser: time the public module the way the organiser's harness "
                         "does (fixed device input, per-call events, 3 rounds x 100, median)")
@@ -333,7 +346,8 @@ def kernel_work(kind: str, cfg, B: int, S: int, lengths) -> tuple:
 
     GEMMs count the valid tokens T only (2*T*N*K): padded rows are not
     algorithmic work, so skipping them cannot raise the fraction. Attention
-    counts valid causal pairs; the norm counts 16*d bytes per row."""
+    counts valid causal pairs; the norm counts the bytes of valid rows
+    (roofline.ln_bytes_per_forward, averaged over its 2L+1 launches)."""
     d, F, H = cfg.d_model, cfg.ffn_dim, cfg.num_heads
     M = B * S
     T = float(sum(lengths))
@@ -349,10 +363,44 @@ def kernel_work(kind: str, cfg, B: int, S: int, lengths) -> tuple:
         pairs = sum(n * (n + 1) // 2 for n in lengths) if cfg.causal else sum(n * n for n in lengths)
         return 4.0 * d * pairs, "flop", "tensor"
     if kind == "ln":
-        return 16.0 * d * M, "byte", "hbm"
+        # average over the forward's 2L+1 norm launches, valid rows only
+        return ln_bytes_per_forward(cfg, lengths) / (2 * cfg.num_layers + 1), "byte", "hbm"
     if kind == "keep_bits":
         return float(M + 4 * B * ((S + 31) // 32)), "byte", "hbm"
     return 0.0, "flop", "tensor"
+
+
+def _timed_gather(shard, out_local, dev, world, repeats: int = 5) -> dict:
+    """The optional NCCL all-gather of every rank's output rows into one
+    [B, S, d] tensor in batch order (sharding.BatchShard.gather), timed on
+    its own with CUDA events (median of `repeats`, max over ranks), and
+    checked: this rank's rows of the gathered tensor equal its own output
+    bit for bit on every rank."""
+    import torch.distributed as dist
+    for _ in range(2):
+        shard.gather(out_local)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(repeats):
+        dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        full = shard.gather(out_local)
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    ok = torch.tensor([1 if torch.equal(shard.take(full), out_local) else 0],
+                      dtype=torch.int32, device=dev)
+    t = torch.tensor([statistics.median(ts)], dtype=torch.float64, device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    nbytes = full.numel() * full.element_size()
+    ms = float(t.item())
+    return {"ms": round(ms, 4), "bytes": int(nbytes),
+            "algbw_gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+            "collective": "all_gather_into_tensor (NCCL) + un-permute to batch order",
+            "rows_match": bool(ok.item())}
 
 
 def main():
@@ -365,10 +413,13 @@ def main():
     if args.protocol == "organiser":
         return run_organiser_protocol(args, rank, world)
 
+    import dataclasses
+
     import torch.distributed as dist
     from techjam2026_b200 import _lib
     from techjam2026_b200.dispatch import DispatchTable, probe
     from techjam2026_b200.fused import FusedTransformer
+    from techjam2026_b200.sharding import BatchShard
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -378,18 +429,30 @@ def main():
 
     w = WORKLOADS[args.config]
     if args.batch_size:
-        import dataclasses
         w = dataclasses.replace(w, cfg=dataclasses.replace(w.cfg, batch_size=args.batch_size))
-    cfg = w.cfg
+    cfg_g = w.cfg
+    B_g, S = cfg_g.batch_size, cfg_g.seq_len
+    # One global batch (the workload's first seed), drawn identically on every
+    # rank; each rank keeps its share of the rows.
+    x_all, mask_all = generate_case(cfg_g, w.seeds[0], w.padding_ratio, w.input_scale)
+    lengths_all = lengths_of(mask_all, B_g, S)
+    strong = B_g % world == 0
+    if strong:
+        shard = BatchShard(lengths_all, world, rank, cfg_g.d_model, cfg_g.ffn_dim, cfg_g.causal)
+        x_cpu, mask_cpu = shard.take(x_all), shard.take(mask_all)
+        lengths = shard.local_lengths()
+    else:
+        # Replicas: a batch that does not split over the ranks runs whole on each.
+        shard = None
+        x_cpu, mask_cpu, lengths = x_all, mask_all, lengths_all
+    del x_all
+    cfg = dataclasses.replace(cfg_g, batch_size=x_cpu.shape[0])
     spec = probe(local)
     plan, source = DispatchTable.load_for(spec).lookup(spec.arch, torch.float32, cfg)
     model = FusedTransformer(cfg, plan)
     model.load_state_dict(make_state_dict(cfg, 0), strict=True)
     model.eval()
 
-    seed = w.seeds[rank % len(w.seeds)] if world == 1 else rank
-    x_cpu, mask_cpu = generate_case(cfg, seed, w.padding_ratio, w.input_scale)
-    lengths = lengths_of(mask_cpu, cfg.batch_size, cfg.seq_len)
     flops_rank = useful_flops(cfg, lengths)
     x = x_cpu.to(dev)
     mask = mask_cpu.to(dev)
@@ -422,14 +485,22 @@ def main():
     ms_total = sum(step_ms)
     t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
     f = torch.tensor([flops_rank], dtype=torch.float64, device=dev)
+    per_rank = [ms_total]
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        every = torch.empty(world, dtype=torch.float64, device=dev)
+        dist.all_gather_into_tensor(every, t)
+        per_rank = [float(v) for v in every.tolist()]
         dist.all_reduce(f, op=dist.ReduceOp.SUM)
-    ms_total_max = float(t.item())
+    ms_total_max = max(per_rank)
     flops_all = float(f.item())
     ms_per_step = ms_total_max / args.steps
     value = flops_all / (ms_per_step / 1e3) / 1e12
-    status = _lib.lib().kf_device_status(0)
+    status = _lib.lib().kf_device_status(local)
+
+    # ---- the optional all-gather of the outputs (N > 1), timed on its own
+    gather = None
+    if world > 1 and strong and not args.no_gather:
+        gather = _timed_gather(shard, runner.static_out, dev, world)
 
     # ---- e2e through the public API (pinned host buffers, copies timed)
     e2e = None
@@ -500,11 +571,15 @@ def main():
             f1.record()
             torch.cuda.synchronize()
             f_ts.append(f0.elapsed_time(f1))
+        h2d = int(xh.numel() * 4 + mh.numel())
+        d2h = int(oh.numel() * 4)
         e2e = {"value": round(flops_all / (e_step / 1e3) / 1e12, 3), "unit": "TFLOP/s",
                "ms_per_step": round(e_step, 4),
                "l2_flush_ms_per_step_inside": round(statistics.median(f_ts), 4),
-               "h2d_bytes_per_step": int(xh.numel() * 4 + mh.numel()),
-               "d2h_bytes_per_step": int(oh.numel() * 4),
+               "h2d_bytes_per_step": h2d * world,
+               "d2h_bytes_per_step": d2h * world,
+               "h2d_bytes_per_rank": h2d, "d2h_bytes_per_rank": d2h,
+               "h2d_d2h_gbs_per_rank": round((h2d + d2h) / (e_step / 1e3) / 1e9, 2),
                "loop": "StreamedForward: copies on two streams overlap the forward",
                "serial_ms_per_step": round(serial_step, 4),
                "serial_value": round(flops_all / (serial_step / 1e3) / 1e12, 3)}
@@ -515,29 +590,34 @@ def main():
     shares = {k: ms * n for k, (ms, n) in bd.items()}
     total = sum(shares.values())
     dom = max(shares, key=shares.get)
-    amount, unit, bound = kernel_work(dom, cfg, cfg.batch_size, cfg.seq_len, lengths)
     peaks = measured_peaks()
-    dom_ms = bd[dom][0]
     # A step of 100 ms or more keeps a 1 kW B200 at its power cap for most of
     # the step, so its tensor kernels are held to the sustained GEMM rate
     # (the seconds-long cuBLAS loop); shorter steps to the burst rate.
     long_step = ms_per_step >= 100.0
-    if bound == "tensor":
-        achieved = amount / (dom_ms / 1e3) / 1e12
-        peak = peaks["tf32_tflops_sustained" if long_step else "tf32_tflops"]
-        r_unit = "TFLOP/s"
-    else:
-        achieved = amount / (dom_ms / 1e3) / 1e9
-        peak = peaks["hbm_gbs"]
-        r_unit = "GB/s"
+
+    def kernel_roof(kind):
+        amount, unit, bound = kernel_work(kind, cfg, cfg.batch_size, cfg.seq_len, lengths)
+        k_ms = bd[kind][0]
+        if bound == "tensor":
+            achieved = amount / (k_ms / 1e3) / 1e12
+            peak = peaks["tf32_tflops_sustained" if long_step else "tf32_tflops"]
+            return bound, achieved, peak, "TFLOP/s", k_ms
+        return bound, amount / (k_ms / 1e3) / 1e9, peaks["hbm_gbs"], "GB/s", k_ms
+
+    bound, achieved, peak, r_unit, dom_ms = kernel_roof(dom)
     # DRAM bytes of one launch of the dominant kernel, from the committed ncu
-    # capture of this workload (null when no capture covers it).
-    prof = profiled_traffic(w.name, dom)
+    # capture of this workload under the same plan (null otherwise).
+    prof = profiled_traffic(w.name, cfg.batch_size, dom, plan.describe())
     roofline = {"kernel": dom, "bound": bound, "achieved": round(achieved, 2),
                 "peak": round(peak, 1), "unit": r_unit, "frac": round(achieved / peak, 4),
-                "traffic": prof["bytes"] if prof else None,
+                "traffic": prof["bytes"] if prof and prof["plan_match"] else None,
                 "traffic_source": (f"{prof['source']} (ncu dram__bytes_read.sum + "
-                                   "dram__bytes_write.sum, one launch)") if prof else None,
+                                   "dram__bytes_write.sum, one launch)"
+                                   + ("" if prof["plan_match"] else
+                                      ": captured under another plan, not used"))
+                if prof else "no committed capture of this workload and kernel",
+                "algorithmic": kernel_work(dom, cfg, cfg.batch_size, cfg.seq_len, lengths)[0],
                 "peak_source": (f"{peaks['source']} "
                                 f"{'sustained' if long_step else 'burst'} "
                                 f"(TF32 = measured dense BF16 / 2; step {ms_per_step:.1f} ms)")
@@ -546,31 +626,54 @@ def main():
                 if bound == "tensor" else None,
                 "launch_ms": round(dom_ms, 5),
                 "share": {k: round(v / total, 4) for k, v in sorted(shares.items())}}
+    # Per-kernel fractions: attention against the burst TF32 rate, the GEMMs
+    # against the TF32-equivalent rate, the norm against HBM.
+    kernels = {}
+    for kind in sorted(bd):
+        if kind == "keep_bits":
+            continue
+        kb_, ka, kp, ku, kms = kernel_roof(kind)
+        kernels[kind] = {"launch_ms": round(kms, 5), "achieved": round(ka, 2), "unit": ku,
+                         "frac": round(ka / kp, 4),
+                         "frac_of_burst": round(ka / peaks["tf32_tflops"], 4)
+                         if kb_ == "tensor" else None,
+                         "launches_per_step": bd[kind][1]}
+    roofline["kernels"] = kernels
+    if "attention" in kernels:
+        roofline["attention"] = dict(kernels["attention"], peak=round(peaks["tf32_tflops"], 1),
+                                     peak_source=f"{peaks['source']} burst (TF32 = dense BF16 / 2)")
 
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             v, desc, threads, ms = cpu_sample(w, args.cpu_seconds)
             cpu = {"value": round(v, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                   "sample": desc, "ms_per_sequence": round(ms, 2)}
+                   "sample": desc, "ms_per_sequence": round(ms, 2), "cpu_model": cpu_model()}
         clk = clocks.summary()
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong" if strong else "weak",
+            "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded generate_random_case draws, Xavier weights)",
-            "config": {"workload": w.name, "signature": sig(cfg),
-                       "global_batch": cfg.batch_size * world, "seq_len": cfg.seq_len,
-                       "parallelism": f"batch-sharded x{world}, no collective",
+            "config": {"workload": w.name, "signature": sig(cfg_g),
+                       "global_batch": B_g if strong else B_g * world, "seq_len": S,
+                       "rows_per_rank": cfg.batch_size,
+                       "parallelism": (f"batch sharded over {world} rank(s): equal row counts, "
+                                       "cost-balanced assignment, no collective in the forward"
+                                       if strong else f"{world} replicas of the whole batch"),
+                       "modeled_imbalance": round(shard.imbalance, 4) if shard else None,
+                       "per_rank_ms_per_step": [round(v / args.steps, 4) for v in per_rank],
                        "plan": plan.describe(), "plan_source": source,
                        "l2": "flushed between steps (256 MiB write)",
-                       "valid_tokens_per_rank": int(sum(lengths)),
-                       "dense_causal_tflop_per_rank": round(dense_causal_flops(cfg) / 1e12, 4),
-                       "useful_tflop_per_rank": round(flops_rank / 1e12, 4)},
+                       "valid_tokens": int(sum(lengths_all)),
+                       "valid_tokens_rank0": int(sum(lengths)),
+                       "dense_causal_tflop": round(dense_causal_flops(cfg_g) / 1e12, 4),
+                       "useful_tflop": round(flops_all / 1e12, 4)},
             "tc_frac_of_tf32_peak": round(value / world / peaks["tf32_tflops"], 4),
             "gpu_launches": int(runner.launches * args.steps),
-            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
-            "device_status": status,
+            "e2e": e2e, "gather": gather, "roofline": roofline, "cpu_baseline": cpu,
+            "clocks": clk, "device_status": status,
         }
         print(json.dumps(line), flush=True)
     runner = None
@@ -579,6 +682,17 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo", encoding="utf-8") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 if __name__ == "__main__":

@@ -44,8 +44,10 @@ int kf_version(void);
 const char* kf_last_error(void);
 
 /* Reads the device-side status word of the current device (synchronises the
- * device). 0 = no kernel has timed out on a barrier since the last reset;
- * otherwise the code of the first failure. `reset` != 0 clears it. */
+ * device). 0 = no kernel has failed since the last reset; otherwise the code
+ * of the first failure: 1-4 a bounded wait gave up (1 TMA producer, 2 MMA
+ * issuer, 3 GEMM epilogue, 4 attention softmax), 5 an ordered attention
+ * call got a batch_order entry outside [0, B). `reset` != 0 clears it. */
 int kf_device_status(int reset);
 
 /* ----------------------------------------------------------- LayerNorm */
@@ -229,6 +231,9 @@ int kf_batch_order(const uint32_t* bits, int64_t B, int64_t S, int32_t* order, v
  * stream): the longest rows' heavy causal tiles start first, so the launch
  * ends on short rows instead of waiting for a late long one. Results are
  * the same bit for bit as kf_flash_fwd_tf32's; only the schedule changes.
+ * batch_order must be a permutation of [0, B) (kf_batch_order's output for
+ * the same B and key bits); an entry outside [0, B) is not used as an index
+ * -- that grid row runs its own batch row -- and sets device status 5.
  * Stands in for the same reference call as kf_flash_fwd_tf32
  * (kernelforge/ops/flash.py:363-422). */
 int kf_flash_fwd_tf32_ordered(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
@@ -251,9 +256,12 @@ int kf_flash_fwd_tf32_ordered(const float* q, int64_t q_sb, int64_t q_sh, int64_
  * kf_keep_bits workspace and packs the key bits into a static device array of
  * the library (KF_NOALLOC_KEEP_WORDS_MAX words, held on every device that
  * loads the library until exit); it calls no allocator. B * ceil(S/32) above
- * the maximum returns KF_E_UNSUPPORTED before any launch. The first call on a
- * device resolves the array's address with cudaGetSymbolAddress: make it
- * before any stream capture. All calls share the array: the packer rewrites
+ * the maximum returns KF_E_UNSUPPORTED, and every argument kf_flash_fwd_tf32
+ * would reject is rejected, before any launch. The first call on a device
+ * resolves the array's address with cudaGetSymbolAddress: make it before any
+ * stream capture. That address is cached per device ordinal until the process
+ * exits, so it is stale after a cudaDeviceReset of that device; do not call
+ * this entry point on a device again after resetting it. All calls share the array: the packer rewrites
  * every word the kernel reads, so nothing needs clearing, but calls that
  * overlap on the GPU race -- order them on one stream or with events.
  * Other arguments, semantics and results as kf_flash_fwd_tf32.

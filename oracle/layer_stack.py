@@ -29,7 +29,9 @@ Differences from the reference's literal op sequence, all exact:
     12.9 GB per layer, c5's 1.1 PB). Softmax rows are independent and no op
     mixes batch elements, so this changes no value (the reference's
     scripts/shape14.py:124-145 streams the same way; it omits the padding
-    masks, which are restored here);
+    masks, which are restored here); with the causal mask a query chunk
+    multiplies only the keys up to its last query, the rest being -inf
+    (weight exactly 0) for every query of the chunk;
   * `dtype=torch.float64` runs the same math in double precision, used as a
     tighter reference when measuring error envelopes.
 """
@@ -78,16 +80,19 @@ def attention(h: torch.Tensor, params: Params, prefix: str, num_heads: int,
         key_ok = None if valid_token_mask is None else valid_token_mask[b]
         for i0 in range(0, S, chunk):
             i1 = min(S, i0 + chunk)
-            scores = torch.matmul(q[b, :, i0:i1], kb.transpose(-2, -1)) * scale
+            # With the causal mask, keys past the chunk's last query are -inf
+            # for every query of the chunk (weight exactly 0): leave them out.
+            kend = i1 if causal else S
+            scores = torch.matmul(q[b, :, i0:i1], kb[:, :kend].transpose(-2, -1)) * scale
             if causal:
                 qi = torch.arange(i0, i1, device=h.device)[:, None]
-                kj = torch.arange(S, device=h.device)[None, :]
+                kj = torch.arange(kend, device=h.device)[None, :]
                 scores = scores.masked_fill(kj > qi, float("-inf"))
             if key_ok is not None:
-                scores = scores.masked_fill(~key_ok[None, None, :], float("-inf"))
+                scores = scores.masked_fill(~key_ok[None, None, :kend], float("-inf"))
             # softmax in fp32 whatever the I/O dtype (torch_transformer_benchmark.py:110-111)
             probs = torch.softmax(scores.float(), dim=-1).to(dtype)
-            ctx[b, :, i0:i1] = torch.matmul(probs, vb)
+            ctx[b, :, i0:i1] = torch.matmul(probs, vb[:, :kend])
     ctx = ctx.transpose(1, 2).reshape(B, S, d)
     out = _linear(ctx, params, prefix + ".out_proj", dtype)
     if valid_token_mask is not None:

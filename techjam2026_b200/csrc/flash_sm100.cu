@@ -190,8 +190,15 @@ __global__ void __launch_bounds__(192, MINB)
   pdl_wait();  // Q/K/V, the key bits and the batch order come from earlier kernels
   int b = bh / H;
   if (batch_order) {
+    // An entry outside [0, B) (an order array not made by kf_batch_order
+    // for this B) is never used as an index: the row keeps its grid
+    // position and the device status records the error.
     const int ob = __ldg(batch_order + b);
-    b = (ob >= 0 && ob < nb) ? ob : b;
+    if (ob >= 0 && ob < nb) {
+      b = ob;
+    } else if (threadIdx.x == 0) {
+      record_device_status(KF_DEV_BAD_BATCH_ORDER);
+    }
   }
   const uint32_t* bits_b = keep_bits ? keep_bits + static_cast<int64_t>(b) * words : nullptr;
 
@@ -763,16 +770,13 @@ static int launch_flash(const float* q, const int64_t* qs, const float* k, const
   }
 
   auto kern = flash_fwd_tf32_kernel<DH, BN, KST, VST, MINB>;
-  static int attr_set[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!attr_set[dev]) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_status(e, "kf_flash_fwd_tf32: set smem attribute");
-    attr_set[dev] = 1;
-  }
+  static DeviceOnce once;
+  const int rc_attr = once.run("kf_flash_fwd_tf32", nullptr, [&](int) {
+    return cuda_status(
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES),
+        "kf_flash_fwd_tf32: set smem attribute");
+  });
+  if (rc_attr) return rc_attr;
   const int n_qt = (S + Cfg::BM - 1) / Cfg::BM;
   dim3 grid(static_cast<unsigned>(n_qt), static_cast<unsigned>(B * H));
   return cuda_status(launch_chained(kern, grid, dim3(192), Cfg::SMEM_BYTES, st, tq, tk, tv, to, o,
@@ -785,17 +789,21 @@ static int launch_flash(const float* q, const int64_t* qs, const float* k, const
 
 using namespace kf;
 
-static int flash_fwd_impl(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
-                          const float* k, int64_t k_sb, int64_t k_sh, int64_t k_sm,
-                          const float* v, int64_t v_sb, int64_t v_sh, int64_t v_sm, float* o,
-                          int64_t o_sb, int64_t o_sh, int64_t o_sm, const uint32_t* keep_bits,
-                          const int32_t* order, int64_t B, int64_t H, int64_t S, int dh,
-                          int dh_out, float sm_scale, int flags, void* stream) {
+// Host-side checks of an attention call; launches nothing and touches no
+// device state, so a caller can run them before any launch of its own.
+// Returns KF_OK and the kernel flags in *kernel_flags, or an error code.
+static int flash_fwd_validate(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
+                              const float* k, int64_t k_sb, int64_t k_sh, int64_t k_sm,
+                              const float* v, int64_t v_sb, int64_t v_sh, int64_t v_sm,
+                              const float* o, int64_t o_sb, int64_t o_sh, int64_t o_sm,
+                              int64_t B, int64_t H, int64_t S, int dh, int dh_out, int flags,
+                              int* kernel_flags) {
   if (!q || !k || !v || !o || B < 0 || H < 0 || S < 0) {
     set_last_error("kf_flash_fwd_tf32: invalid arguments");
     return KF_E_INVALID;
   }
-  if (B == 0 || H == 0 || S == 0) return KF_OK;
+  *kernel_flags = 0;
+  if (B == 0 || H == 0 || S == 0) return KF_OK;  // nothing to compute, nothing to check
   if (dh != 16 && dh != 32 && dh != 64 && dh != 128 && dh != 256) {
     set_last_error("kf_flash_fwd_tf32: stored head_dim %d not in {16,32,64,128,256}", dh);
     return KF_E_UNSUPPORTED;
@@ -831,6 +839,21 @@ static int flash_fwd_impl(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_
   if ((o_sm % 4 == 0) && !(reinterpret_cast<uintptr_t>(o) & 15u) && o_sb % 4 == 0 &&
       o_sh % 4 == 0)
     f |= (1 << 8);
+  *kernel_flags = f;
+  return KF_OK;
+}
+
+static int flash_fwd_impl(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
+                          const float* k, int64_t k_sb, int64_t k_sh, int64_t k_sm,
+                          const float* v, int64_t v_sb, int64_t v_sh, int64_t v_sm, float* o,
+                          int64_t o_sb, int64_t o_sh, int64_t o_sm, const uint32_t* keep_bits,
+                          const int32_t* order, int64_t B, int64_t H, int64_t S, int dh,
+                          int dh_out, float sm_scale, int flags, void* stream) {
+  int f = 0;
+  const int rc = flash_fwd_validate(q, q_sb, q_sh, q_sm, k, k_sb, k_sh, k_sm, v, v_sb, v_sh, v_sm,
+                                    o, o_sb, o_sh, o_sm, B, H, S, dh, dh_out, flags, &f);
+  if (rc) return rc;
+  if (B == 0 || H == 0 || S == 0) return KF_OK;
   const float scale_log2 = sm_scale * 1.4426950408889634f;
   const int64_t qs[3] = {q_sb, q_sh, q_sm}, ks[3] = {k_sb, k_sh, k_sm},
                 vs[3] = {v_sb, v_sh, v_sm}, os[3] = {o_sb, o_sh, o_sm};

@@ -1137,16 +1137,13 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
                        const int32_t* live_tiles, const int32_t* live_count, cudaStream_t st) {
   using Cfg = GemmCfg<BN, SPLIT>;
   auto kern = gemm_tf32_kernel<BN, EPI, SPLIT>;
-  static int attr_set[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!attr_set[dev]) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_status(e, "kf_gemm_tf32: set smem attribute");
-    attr_set[dev] = 1;
-  }
+  static DeviceOnce once;
+  const int rc_attr = once.run("kf_gemm_tf32", nullptr, [&](int) {
+    return cuda_status(
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES),
+        "kf_gemm_tf32: set smem attribute");
+  });
+  if (rc_attr) return rc_attr;
   // With a live-tile list the count is only known on the device: launch one
   // CTA per SM and let CTAs without work exit.
   const int tiles = ((M + Cfg::BM - 1) / Cfg::BM) * ((N + BN - 1) / BN);
@@ -1166,16 +1163,13 @@ static int launch_gemm_sk(const CUtensorMap& ta, const CUtensorMap& tb, const CU
                           const SkArgs& sk, cudaStream_t st) {
   using Cfg = GemmCfg<BN, SPLIT_BF16X3_PRE>;
   auto kern = gemm_tf32_kernel<BN, EPI, SPLIT_BF16X3_PRE, false, false, true>;
-  static int attr_set[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!attr_set[dev]) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_status(e, "kf_gemm_bf16x3_sk: set smem attribute");
-    attr_set[dev] = 1;
-  }
+  static DeviceOnce once;
+  const int rc_attr = once.run("kf_gemm_bf16x3_sk", nullptr, [&](int) {
+    return cuda_status(
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES),
+        "kf_gemm_bf16x3_sk: set smem attribute");
+  });
+  if (rc_attr) return rc_attr;
   return cuda_status(launch_chained(kern, dim3(static_cast<unsigned>(sm_count())),
                                     dim3(Cfg::THREADS), Cfg::SMEM_BYTES, st, ta, tb, tc, C, ldc,
                                     bias, M, N, K, flags, hd, hs, live_tiles, live_count, LnArgs{},
@@ -1192,18 +1186,13 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
                             const int32_t* live_count, cudaStream_t st) {
   using Cfg = GemmCfg<BN, SPLIT_BF16X3_PRE, true>;
   auto kern = gemm_tf32_kernel<BN, EPI, SPLIT_BF16X3_PRE, false, true>;
-  static int attr_set[64] = {0};
-  static int max_pairs[64] = {0};
+  static DeviceOnce once;
+  static int max_pairs[KF_MAX_DEVICES] = {0};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!attr_set[dev]) {
+  const int rc_attr = once.run("kf_gemm_bf16x3 (pair)", &dev, [&](int d) {
     const cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return cuda_status(e, "kf_gemm_bf16x3 (pair): set smem attribute");
-    attr_set[dev] = 1;
-  }
-  if (!max_pairs[dev]) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 8);
     cfg.blockDim = dim3(Cfg::THREADS);
@@ -1220,8 +1209,10 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
       cudaGetLastError();
       n = sm_count() / 2;
     }
-    max_pairs[dev] = n > 0 ? n : 1;
-  }
+    max_pairs[d] = n > 0 ? n : 1;
+    return static_cast<int>(KF_OK);
+  });
+  if (rc_attr) return rc_attr;
   // Units of 256 x BN over all row tiles (the live count is only known on
   // the device; pairs without work exit).
   const int units = (((M + Cfg::BM - 1) / Cfg::BM + 1) / 2) * ((N + BN - 1) / BN);
@@ -1240,38 +1231,38 @@ static int launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tb, const fl
                           const int32_t* live_count, cudaStream_t st) {
   using Cfg = GemmCfg<128, 3>;
   auto kern = gemm_tf32_kernel<128, KF_EPI_BIAS, 3, true>;
-  static int attr_set[64] = {0};
-  static int max_clusters[64][9] = {{0}};
+  static DeviceOnce once;
+  static int max_clusters[KF_MAX_DEVICES][9] = {{0}};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!attr_set[dev]) {
+  const int rc_attr = once.run("kf_gemm_bf16x3_add_ln", &dev, [&](int d) {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return cuda_status(e, "kf_gemm_bf16x3_add_ln: set attributes");
-    attr_set[dev] = 1;
-  }
-  const int csize = N / 128;
-  if (!max_clusters[dev][csize]) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(csize * 8));
-    cfg.blockDim = dim3(Cfg::THREADS);
-    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(csize);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-      cudaGetLastError();
-      n = sm_count() / csize;
+    // Resident clusters for every cluster size the entry accepts (N/128 = 1..8).
+    for (int cs = 1; cs <= 8; ++cs) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(cs * 8));
+      cfg.blockDim = dim3(Cfg::THREADS);
+      cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = static_cast<unsigned>(cs);
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = sm_count() / cs;
+      }
+      max_clusters[d][cs] = n > 0 ? n : 1;
     }
-    max_clusters[dev][csize] = n > 0 ? n : 1;
-  }
+    return static_cast<int>(KF_OK);
+  });
+  if (rc_attr) return rc_attr;
+  const int csize = N / 128;
   const int row_tiles = (M + Cfg::BM - 1) / Cfg::BM;
   const int clusters = row_tiles < max_clusters[dev][csize] ? row_tiles : max_clusters[dev][csize];
   CUtensorMap tc;

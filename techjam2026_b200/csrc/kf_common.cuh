@@ -13,6 +13,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
 #include <utility>
 
 #include "../../include/kf_sm100.h"
@@ -36,6 +38,7 @@ enum : int {
   KF_DEV_WAIT_TIMEOUT_MMA = 2,
   KF_DEV_WAIT_TIMEOUT_EPI = 3,
   KF_DEV_WAIT_TIMEOUT_SOFTMAX = 4,
+  KF_DEV_BAD_BATCH_ORDER = 5,  // a batch_order entry outside [0, B)
 };
 
 __device__ __forceinline__ void record_device_status(int code) {
@@ -605,6 +608,39 @@ int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank
 
 // Number of SMs of the current device (cached per device).
 int sm_count();
+
+// Per-device one-time set-up of a launch site (kernel attributes, occupancy
+// queries). One DeviceOnce per site, in static storage: `run` calls
+// set_up(device) once per device ordinal, the first time that device is
+// current, under a lock, so concurrent host threads neither race on the
+// site's cache nor run the set-up twice; later calls read an atomic flag
+// only. Device ordinals beyond KF_MAX_DEVICES are refused
+// (KF_E_UNSUPPORTED) rather than sharing another device's entry.
+constexpr int KF_MAX_DEVICES = 64;
+
+struct DeviceOnce {
+  std::atomic<int> done[KF_MAX_DEVICES];
+  std::mutex mu;
+
+  template <class F>
+  int run(const char* what, int* device, F&& set_up) {
+    int dev = 0;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e, what);
+    if (dev < 0 || dev >= KF_MAX_DEVICES) {
+      set_last_error("%s: device ordinal %d is beyond the %d this library supports", what, dev,
+                     KF_MAX_DEVICES);
+      return KF_E_UNSUPPORTED;
+    }
+    if (device) *device = dev;
+    if (done[dev].load(std::memory_order_acquire)) return KF_OK;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done[dev].load(std::memory_order_relaxed)) return KF_OK;
+    const int rc = set_up(dev);
+    if (rc == KF_OK) done[dev].store(1, std::memory_order_release);
+    return rc;
+  }
+};
 
 // Launch with programmatic stream serialization, so the kernel may start
 // while its predecessor in the stream finishes (it calls pdl_wait() before

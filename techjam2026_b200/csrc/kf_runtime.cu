@@ -66,16 +66,16 @@ int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank
 }
 
 int sm_count() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[KF_MAX_DEVICES];
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (!cached[dev]) {
-    int n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= KF_MAX_DEVICES) return 148;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (!n) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
       n = 148;
-    cached[dev] = n;
+    cached[dev].store(n, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return n;
 }
 
 // ---------------------------------------------------------------- kernels

@@ -16,10 +16,14 @@
 // Limits and sharing:
 //   * the array holds KF_NOALLOC_KEEP_WORDS_MAX words (1 MiB) on every device
 //     that loads the library, until the process exits; B * ceil(S/32) above
-//     that is rejected with KF_E_UNSUPPORTED before anything is launched;
+//     that is rejected with KF_E_UNSUPPORTED, and so is every argument the
+//     attention entry point refuses, before anything is launched;
 //   * the first call on a device resolves the array's device address with
 //     cudaGetSymbolAddress (the host-side name is only a stand-in, never a
-//     device pointer); make that first call before any stream capture;
+//     device pointer); make that first call before any stream capture. The
+//     address is cached per device ordinal for the life of the process: after
+//     a cudaDeviceReset it is stale, so do not reset a device this library
+//     has used and then call it again;
 //   * every call shares the array and it keeps the last call's contents. The
 //     packer writes every word the attention kernel then reads (bits past S
 //     as 0), so nothing has to start at zero; but calls whose kernels overlap
@@ -71,6 +75,18 @@ extern "C" int kf_flash_fwd_tf32_keep_noalloc(
     return KF_E_INVALID;
   }
   if (B == 0 || H == 0 || S == 0) return KF_OK;
+  // Every check of the attention call runs before the key-bit packer is
+  // queued, so a rejected call launches nothing and leaves the scratch as
+  // it was.
+  int kernel_flags = 0;
+  int rc = flash_fwd_validate(q, q_sb, q_sh, q_sm, k, k_sb, k_sh, k_sm, v, v_sb, v_sh, v_sm, o,
+                              o_sb, o_sh, o_sm, B, H, S, dh, dh_out, flags, &kernel_flags);
+  if (rc) return rc;
+  if (ld_keep < S) {
+    set_last_error("kf_flash_fwd_tf32_keep_noalloc: ld_keep %lld < S %lld", (long long)ld_keep,
+                   (long long)S);
+    return KF_E_INVALID;
+  }
   const size_t words = kf_keep_bits_words(B, S);
   if (words > static_cast<size_t>(KF_NOALLOC_KEEP_WORDS_MAX)) {
     set_last_error(
@@ -80,7 +96,7 @@ extern "C" int kf_flash_fwd_tf32_keep_noalloc(
     return KF_E_UNSUPPORTED;
   }
   uint32_t* bits = nullptr;
-  int rc = noalloc_scratch(&bits);
+  rc = noalloc_scratch(&bits);
   if (rc) return rc;
   rc = kf_keep_bits(keep, ld_keep, B, S, bits, stream);
   if (rc) return rc;

@@ -13,8 +13,9 @@ the reference's roofline.stack_flops convention (kernelforge/roofline.py:
 96-116, attention halved for causal).
 
 LayerNorm traffic: 16*d bytes per row per add+mask+LN call (read x and y,
-write s and h, fp32), 2L+1 calls per forward (an upper bound: the entry call
-reads no y, the final call writes no s).
+write s and h, fp32), 2L+1 calls per forward (`norm_bytes`, every row: an
+upper bound); `ln_bytes_per_forward` counts what the calls must move when
+padded rows are skipped (the roofline's algorithmic bytes).
 """
 from __future__ import annotations
 
@@ -65,6 +66,20 @@ def norm_bytes(cfg) -> float:
     return 16.0 * cfg.d_model * M * (2 * cfg.num_layers + 1)
 
 
+def ln_bytes_per_forward(cfg, lengths: Iterable[int]) -> float:
+    """Algorithmic DRAM bytes of the 2L+1 add+mask+LayerNorm calls of one
+    forward, the norms touching valid rows only (padded rows are skipped,
+    except that the final norm writes them as zeros):
+      entry norm        read x, write s and h     12*d bytes per valid row
+      2L-1 middle norms read x, y, write s, h     16*d
+      final norm        read x, y, write h        8*d, plus 4*d per padded row
+    """
+    T = float(sum(lengths))
+    M = float(cfg.batch_size * cfg.seq_len)
+    d, L = cfg.d_model, cfg.num_layers
+    return 12.0 * d * T + (2 * L - 1) * 16.0 * d * T + 8.0 * d * T + 4.0 * d * (M - T)
+
+
 def ln_call_bytes(M: int, d: int, has_y: bool = True, writes_s: bool = True) -> float:
     return 4.0 * d * M * (1 + int(has_y) + int(writes_s) + 1)
 
@@ -91,14 +106,23 @@ def measured_peaks(path: Optional[str] = None) -> dict:
     return out
 
 
-def profiled_traffic(workload: str, kind: str, folder: Optional[str] = None) -> Optional[dict]:
-    """DRAM bytes per launch of `kind` on `workload`, from an ncu capture.
+def plan_tag(plan_description: str) -> str:
+    """Short stable tag of a plan (its `Plan.describe()` text)."""
+    import hashlib
+    return hashlib.sha1(plan_description.encode("utf-8")).hexdigest()[:12]
 
-    Reads the `traffic <workload> <kind> <bytes>` lines of the committed
-    capture summaries (profiles/traffic_*.md: dram__bytes_read.sum +
-    dram__bytes_write.sum per launch, one ncu pass over one forward).
-    Returns {"bytes": N, "source": file name} or None when no capture covers
-    the pair."""
+
+def profiled_traffic(workload: str, batch: int, kind: str, plan_description: str,
+                     folder: Optional[str] = None) -> Optional[dict]:
+    """DRAM bytes per launch of `kind` on `workload` at `batch` rows, from an
+    ncu capture.
+
+    Reads the `traffic <workload> <batch> <kind> <bytes> <plan tag>` lines of
+    the committed capture summaries (profiles/traffic_*.md:
+    dram__bytes_read.sum + dram__bytes_write.sum per launch, one ncu pass
+    over one forward). Returns {"bytes", "source", "plan_match"} -- a capture
+    taken under another plan is reported as such and must not be used -- or
+    None when no capture covers the workload, batch and kernel."""
     here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     folder = folder or os.path.join(here, "profiles")
     try:
@@ -106,11 +130,17 @@ def profiled_traffic(workload: str, kind: str, folder: Optional[str] = None) -> 
                        if n.startswith("traffic_") and n.endswith(".md"))
     except OSError:
         return None
+    want = plan_tag(plan_description)
+    found = None
     for name in names:
         with open(os.path.join(folder, name), encoding="utf-8") as f:
             for line in f:
                 parts = line.split()
-                if (len(parts) == 4 and parts[0] == "traffic" and parts[1] == workload
-                        and parts[2] == kind):
-                    return {"bytes": int(parts[3]), "source": f"profiles/{name}"}
-    return None
+                if (len(parts) == 6 and parts[0] == "traffic" and parts[1] == workload
+                        and parts[2] == str(batch) and parts[3] == kind):
+                    hit = {"bytes": int(parts[4]), "source": f"profiles/{name}",
+                           "plan_match": parts[5] == want}
+                    if hit["plan_match"]:
+                        return hit
+                    found = found or hit
+    return found

@@ -4,8 +4,10 @@ No op of the stack mixes batch elements (kernelforge/optimized.py:343-348),
 so the forward needs no inter-GPU traffic: each rank runs the rows it owns
 with its own CUDA graph. Two policies:
 
-  * weak scaling: every rank runs a full batch of its own (the bench's mode);
-  * a fixed global batch split across ranks: equal row counts per rank (one
+  * replicas: every rank runs a full batch of its own (used only when the
+    batch does not split evenly, e.g. c1's two rows over four GPUs);
+  * a fixed global batch split across ranks (`BatchShard`, the bench's
+    mode: strong scaling): equal row counts per rank (one
     static shape, one graph) with a cost-balanced assignment -- greedy
     largest-first over the per-row cost 2*L*(4d^2+2dF) + 4d*L(L+1)/2 -- so the
     slowest rank is not the one that drew all the long sequences (lengths vary
@@ -72,3 +74,44 @@ def gather_rows(local: torch.Tensor, rows: List[List[int]], group=None) -> torch
     dist.all_gather_into_tensor(full, local.contiguous(), group=group)
     _, inv = permutation(rows)
     return full[inv.to(full.device)]
+
+
+class BatchShard:
+    """This rank's share of one fixed global batch.
+
+    Built from the global batch's valid lengths (every rank computes the same
+    assignment from the same lengths, so no message is needed to agree on
+    it): `rows` holds every rank's batch indices, `mine` this rank's, in
+    ascending order. `take(t)` selects this rank's rows of any [B, ...]
+    tensor (inputs on the host or the device), `gather(out)` runs the one
+    collective and returns the whole [B, ...] result in batch order on every
+    rank. With world == 1 the shard is the whole batch and `gather` is the
+    identity."""
+
+    def __init__(self, lengths: Sequence[int], world: int, rank: int, d: int, ffn: int,
+                 causal: bool = True):
+        if not 0 <= rank < world:
+            raise ValueError(f"rank {rank} outside a world of {world}")
+        self.world, self.rank = world, rank
+        self.lengths = [int(v) for v in lengths]
+        self.rows = assign_rows(self.lengths, world, d, ffn, causal)
+        self.mine = self.rows[rank]
+        self.imbalance = imbalance(self.lengths, self.rows, d, ffn, causal)
+        self._index = torch.tensor(self.mine, dtype=torch.long)
+
+    @property
+    def local_batch(self) -> int:
+        return len(self.mine)
+
+    def local_lengths(self) -> List[int]:
+        return [self.lengths[b] for b in self.mine]
+
+    def take(self, t: torch.Tensor) -> torch.Tensor:
+        if t.shape[0] != len(self.lengths):
+            raise ValueError(f"expected a batch of {len(self.lengths)} rows, got {t.shape[0]}")
+        return t.index_select(0, self._index.to(t.device)).contiguous()
+
+    def gather(self, local: torch.Tensor, group=None) -> torch.Tensor:
+        if self.world == 1:
+            return local
+        return gather_rows(local, self.rows, group)

@@ -35,6 +35,15 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs an sm_100 (B200) GPU")
 
 
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    from parity_log import RECORDS
+    if not RECORDS:
+        return
+    terminalreporter.write_sep("-", "parity against the oracle (envelope = max |err| / allowed)")
+    for what, res in RECORDS:
+        terminalreporter.write_line(f"{what}: {res}")
+
+
 def pytest_collection_modifyitems(config, items):
     if HAS_GPU:
         return

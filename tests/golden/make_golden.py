@@ -52,7 +52,10 @@ def x_checksum(x: torch.Tensor) -> str:
 
 
 def main() -> None:
-    ref_dir = os.environ.get("KF_REFERENCE_DIR", "/root/reference")
+    ref_dir = os.environ.get("KF_REFERENCE_DIR")
+    if not ref_dir:
+        raise SystemExit("set KF_REFERENCE_DIR to a checkout of the reference "
+                         "(the directory holding torch_transformer_benchmark.py)")
     sys.path.insert(0, ref_dir)
     import torch_transformer_benchmark as ref
 

@@ -99,3 +99,25 @@ def test_fused_gemm_layernorm_entry_rejects_before_any_launch():
     assert lib.kf_gemm_bf16x3_add_ln(*args(100)) == _lib.KF_E_UNSUPPORTED
     assert b"128" in lib.kf_last_error()
     assert lib.kf_gemm_bf16x3_add_ln(*args(2048)) == _lib.KF_E_UNSUPPORTED
+
+
+def test_noalloc_entry_rejects_bad_attention_arguments_before_any_launch():
+    """kf_flash_fwd_tf32_keep_noalloc runs every check of the attention call
+    before it queues the key-bit packer: an unsupported head_dim, an odd
+    stride or a short keep row stride is refused with no CUDA call at all
+    (this runs without a GPU, so any launch or device query would fail with
+    a CUDA error code instead)."""
+    lib = _lib.lib()
+    fake = ctypes.c_void_p(0x1000)   # never dereferenced
+
+    def call(dh=64, q_sm=64, ld_keep=8, S=8):
+        return lib.kf_flash_fwd_tf32_keep_noalloc(
+            fake, 4096, 512, q_sm, fake, 4096, 512, 64, fake, 4096, 512, 64,
+            fake, 4096, 512, 64, fake, ld_keep, 1, 1, S, dh, dh, 0.125, 0, None)
+
+    assert call(dh=48) == _lib.KF_E_UNSUPPORTED
+    assert b"head_dim" in lib.kf_last_error()
+    assert call(q_sm=6) == _lib.KF_E_UNSUPPORTED
+    assert b"strides" in lib.kf_last_error()
+    assert call(ld_keep=4) == _lib.KF_E_INVALID
+    assert b"ld_keep" in lib.kf_last_error()

@@ -118,3 +118,20 @@ def test_oracle_matches_reference_at_bfloat16_io():
     # Same CPU ops in the same order; a bf16 ulp at |x| ~ 4 is 2^-5.
     assert diff <= 2 ** -5, diff
     assert torch.count_nonzero(out[~case["mask"]]) == 0
+
+
+@pytest.mark.parametrize("name", ["mini_s333", "mini_s4097"])
+def test_oracle_on_a_valid_prefix_equals_the_padded_row(name):
+    """The full-size parity tests run the oracle on each row's valid prefix
+    only (c4, c5): with a prefix mask that reproduces the padded row's valid
+    outputs, since no valid output depends on a padded token. Pinned here
+    against the reference's own outputs of whole padded rows."""
+    case = load_case(name)
+    cfg, x, mask = case["cfg"], case["x"], case["mask"]
+    for b in range(x.shape[0]):
+        n = int(mask[b].sum())
+        assert bool(mask[b, :n].all()) and not bool(mask[b, n:].any())
+        part = oracle.forward(case["state_dict"], cfg.num_layers, cfg.num_heads,
+                              x[b:b + 1, :n], mask[b:b + 1, :n], causal=cfg.causal,
+                              query_chunk=256)
+        torch.testing.assert_close(part[0], case["out"][b, :n], rtol=2e-5, atol=2e-5)

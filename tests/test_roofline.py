@@ -2,8 +2,8 @@
 import torch
 
 from techjam2026_b200.configs import WORKLOADS
-from techjam2026_b200.roofline import (dense_causal_flops, lengths_of, profiled_traffic,
-                                       useful_flops)
+from techjam2026_b200.roofline import (dense_causal_flops, lengths_of, plan_tag,
+                                       profiled_traffic, useful_flops)
 
 
 def test_useful_flops_counts_valid_causal_pairs():
@@ -22,16 +22,26 @@ def test_lengths_of_mask():
     assert lengths_of(None, 3, 4) == [4, 4, 4]
 
 
-def test_profiled_traffic_reads_committed_capture():
-    t = profiled_traffic("c2", "ffn1")
-    assert t is not None and t["source"].startswith("profiles/traffic_")
-    # the capture's DRAM read of one FFN1 launch: W1 planes (4.19 MB) plus live A rows
-    assert 2048 * 512 * 4 < t["bytes"] < 2048 * 512 * 4 + 4096 * 512 * 4
-    assert profiled_traffic("c2", "no_such_kernel") is None
+def test_profiled_traffic_parses_lines_and_checks_the_plan(tmp_path):
+    tag = plan_tag("plan A")
+    (tmp_path / "traffic_x.md").write_text(
+        f"text\n```\ntraffic w 8 k 123 {tag}\ntraffic w 8 k2 7 {tag}\n"
+        f"traffic w 64 k 555 {tag}\ntraffic w 8 k3 9 {plan_tag('plan B')}\n```\n")
+    (tmp_path / "other.md").write_text(f"traffic w 8 k 999 {tag}\n")
+    hit = profiled_traffic("w", 8, "k", "plan A", str(tmp_path))
+    assert hit["bytes"] == 123 and hit["plan_match"]
+    assert profiled_traffic("w", 64, "k", "plan A", str(tmp_path))["bytes"] == 555
+    assert profiled_traffic("w", 8, "k4", "plan A", str(tmp_path)) is None
+    stale = profiled_traffic("w", 8, "k3", "plan A", str(tmp_path))
+    assert stale["bytes"] == 9 and not stale["plan_match"]
+    assert profiled_traffic("w", 16, "k", "plan A", str(tmp_path)) is None
 
 
-def test_profiled_traffic_parses_lines(tmp_path):
-    (tmp_path / "traffic_x.md").write_text("text\n```\ntraffic w k 123\ntraffic w k2 7\n```\n")
-    (tmp_path / "other.md").write_text("traffic w k 999\n")
-    assert profiled_traffic("w", "k", str(tmp_path))["bytes"] == 123
-    assert profiled_traffic("w", "k3", str(tmp_path)) is None
+def test_norm_bytes_count_valid_rows():
+    from techjam2026_b200.roofline import ln_bytes_per_forward
+    cfg = WORKLOADS["c2"].cfg
+    d, L, M = cfg.d_model, cfg.num_layers, cfg.batch_size * cfg.seq_len
+    full = ln_bytes_per_forward(cfg, [cfg.seq_len] * cfg.batch_size)
+    assert full == (12 + (2 * L - 1) * 16 + 8) * d * M
+    half = ln_bytes_per_forward(cfg, [cfg.seq_len // 2] * cfg.batch_size)
+    assert half == (12 + (2 * L - 1) * 16 + 8) * d * M / 2 + 4 * d * M / 2

@@ -54,18 +54,19 @@ def _worker(rank, world, port, q):
     import torch.distributed as dist
     import oracle
     from golden_cases import load_case
-    from techjam2026_b200.sharding import assign_rows, gather_rows
+    from techjam2026_b200.sharding import BatchShard
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         case = load_case("mini_s333")
         cfg, x, mask = case["cfg"], case["x"], case["mask"]
         lengths = mask.sum(1).tolist()
-        rows = assign_rows(lengths, world, cfg.d_model, cfg.ffn_dim)
-        mine = rows[rank]
+        shard = BatchShard(lengths, world, rank, cfg.d_model, cfg.ffn_dim, cfg.causal)
+        assert shard.local_batch == len(lengths) // world
         out_local = oracle.forward(case["state_dict"], cfg.num_layers, cfg.num_heads,
-                                   x[mine], mask[mine], causal=cfg.causal)
-        full = gather_rows(out_local, rows)
+                                   shard.take(x), shard.take(mask), causal=cfg.causal)
+        full = shard.gather(out_local)
+        assert torch.equal(shard.take(full), out_local)
         if rank == 0:
             # By value (a numpy array is pickled whole): a tensor would travel
             # as a shared-memory handle that dies with this process.
@@ -92,3 +93,24 @@ def test_two_rank_gloo_gather_matches_single_process():
     want = oracle.forward(case["state_dict"], cfg.num_layers, cfg.num_heads, case["x"],
                           case["mask"], causal=cfg.causal)
     assert torch.equal(got, want)
+
+
+def test_batch_shard_single_rank_is_the_whole_batch():
+    from techjam2026_b200.sharding import BatchShard
+    w = WORKLOADS["c4"]
+    _, mask = generate_case(w.cfg, 0, w.padding_ratio)
+    lengths = mask.sum(1).tolist()
+    shard = BatchShard(lengths, 1, 0, w.cfg.d_model, w.cfg.ffn_dim)
+    assert shard.mine == list(range(64)) and shard.imbalance == 1.0
+    t = torch.arange(64 * 3).view(64, 3)
+    assert torch.equal(shard.take(t), t) and shard.gather(t) is t
+    for world in (2, 4, 8):
+        shards = [BatchShard(lengths, world, r, w.cfg.d_model, w.cfg.ffn_dim)
+                  for r in range(world)]
+        assert all(s.rows == shards[0].rows for s in shards), "every rank derives one plan"
+        assert sorted(b for s in shards for b in s.mine) == list(range(64))
+        assert sum(sum(s.local_lengths()) for s in shards) == sum(lengths)
+    with pytest.raises(ValueError):
+        BatchShard(lengths, 2, 2, w.cfg.d_model, w.cfg.ffn_dim)
+    with pytest.raises(ValueError):
+        shard.take(torch.zeros(3, 2))
