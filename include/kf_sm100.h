@@ -243,6 +243,49 @@ int kf_flash_fwd_tf32_ordered(const float* q, int64_t q_sb, int64_t q_sh, int64_
                               const int32_t* batch_order, int64_t B, int64_t H, int64_t S, int dh,
                               int dh_out, float sm_scale, int flags, void* stream);
 
+/* ----------------------------------------------------------- persistent attention */
+
+#define KF_ATTN_EMPTY_Q_UNTOUCHED 16 /* kf_flash_fwd_tf32_sched: leave the rows of
+                                        query tiles without a valid query as they
+                                        are (no work at all for those tiles) */
+
+/* int32 words of a kf_attn_schedule work list for [B, S] rows of H heads:
+ * 8 header words plus two per (row, head, 128-query tile). */
+size_t kf_attn_schedule_words(int64_t B, int64_t H, int64_t S);
+
+/* Builds the work list of kf_flash_fwd_tf32_sched from a kf_keep_bits
+ * workspace (keep_bits may be null: every key valid) in `sched`
+ * (kf_attn_schedule_words int32 words, caller-owned, 8-byte aligned). One item per (row,
+ * head, 128-query tile): the rows by valid length, longest first, their heads
+ * in order, and within a head the query tiles that hold a valid query from
+ * the last to the first (the heaviest under the causal mask first); the tiles
+ * without a valid query come after all of those. Also zeroes the list's two
+ * counters. One CTA; B <= 16384 and B * H <= 65535. The list depends only on
+ * the key bits, so one list serves every layer of a forward. No reference
+ * counterpart (the reference's grid runs every query tile in grid order,
+ * kernelforge/ops/flash.py:397). */
+int kf_attn_schedule(const uint32_t* keep_bits, int64_t B, int64_t H, int64_t S,
+                     int32_t* sched, void* stream);
+
+/* kf_flash_fwd_tf32 as a persistent kernel over a kf_attn_schedule list for
+ * the same keep_bits, B, H and S: as many CTAs as fit on the GPU take items
+ * from the list with an atomic counter in its header until it is exhausted,
+ * keeping their barriers, TMEM and pipelines across items (the next item's Q
+ * loads while the current one drains). Per query row the arithmetic is the
+ * same as kf_flash_fwd_tf32's, so the output is bit-identical for the same
+ * flags; with KF_ATTN_EMPTY_Q_UNTOUCHED the rows of query tiles without a
+ * valid query are not written at all. The list's counters are reset by the
+ * kernel's last CTA, so the list can be reused by later calls on the same
+ * stream; calls that overlap on the GPU must not share a list.
+ * Replaces the same reference call as kf_flash_fwd_tf32
+ * (kernelforge/ops/flash.py:363-422). */
+int kf_flash_fwd_tf32_sched(const float* q, int64_t q_sb, int64_t q_sh, int64_t q_sm,
+                            const float* k, int64_t k_sb, int64_t k_sh, int64_t k_sm,
+                            const float* v, int64_t v_sb, int64_t v_sh, int64_t v_sm, float* o,
+                            int64_t o_sb, int64_t o_sh, int64_t o_sm, const uint32_t* keep_bits,
+                            int32_t* sched, int64_t B, int64_t H, int64_t S, int dh, int dh_out,
+                            float sm_scale, int flags, void* stream);
+
 /* ----------------------------------------------------------- no-allocation variant */
 
 /* Capacity of the library's static key-bit scratch: 1 MiB per device. */

@@ -58,6 +58,14 @@ SIGNATURES = {
                                            _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_int,
                                            _c_int, _c_float, _c_int, _c_ptr]),
     "kf_round_tf32": (_c_int, [_c_ptr, _c_ptr, _c_i64, _c_ptr]),
+    "kf_attn_schedule_words": (ctypes.c_size_t, [_c_i64, _c_i64, _c_i64]),
+    "kf_attn_schedule": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr]),
+    "kf_flash_fwd_tf32_sched": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64,
+                                         _c_ptr, _c_i64, _c_i64, _c_i64,
+                                         _c_ptr, _c_i64, _c_i64, _c_i64,
+                                         _c_ptr, _c_i64, _c_i64, _c_i64,
+                                         _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_int,
+                                         _c_int, _c_float, _c_int, _c_ptr]),
     "kf_flash_fwd_tf32_keep_noalloc": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64,
                                                 _c_ptr, _c_i64, _c_i64, _c_i64,
                                                 _c_ptr, _c_i64, _c_i64, _c_i64,
@@ -88,6 +96,7 @@ KF_ATTN_CAUSAL = 1
 KF_ATTN_SKIP_EMPTY_Q = 2
 KF_ATTN_ROUND_TF32 = 4
 KF_ATTN_OUT_BF16X2 = 8
+KF_ATTN_EMPTY_Q_UNTOUCHED = 16
 KF_GEMM_OUT_BF16X2 = 8
 KF_GEMM_K32 = 16
 KF_GEMM_PAIR = 32

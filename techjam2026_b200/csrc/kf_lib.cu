@@ -4,4 +4,5 @@
 #include "ln_sm100.cu"
 #include "gemm_sm100.cu"
 #include "flash_sm100.cu"
+#include "flash_persist_sm100.cu"
 #include "noalloc_sm100.cu"

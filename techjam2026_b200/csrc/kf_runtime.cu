@@ -208,6 +208,138 @@ __global__ void __launch_bounds__(1024) batch_order_kernel(const uint32_t* __res
   }
 }
 
+// Work list of the persistent attention forward (kf_attn_schedule).
+//
+// sched[0] / sched[1]: the attention kernel's fetch and finish counters
+// (zeroed here; the kernel's last CTA zeroes them again, so one list serves
+// every layer of a forward); sched[2] = live items, sched[3] = all items;
+// items from sched[KF_SCHED_HEADER] as {b * H + h, query tile} pairs.
+// Order: batch rows longest first (valid-key count, ties by index), within
+// a row its heads in order, within a head the query tiles that hold a valid
+// query from the last (heaviest under the causal mask) to the first; after
+// every live item, the query tiles without a valid query, in the same row
+// and head order. One CTA of 1024 threads, one warp per batch row; rows
+// beyond KF_ORDER_MAX_B keep the batch order (no ranking).
+constexpr int KF_SCHED_HEADER = 8;
+constexpr int KF_SCHED_MAX_B = 16384;
+
+// Does query tile t (128 queries = 4 key-bit words) hold a valid token?
+__device__ __forceinline__ bool q_tile_live(const uint32_t* rb, int words, int t) {
+  if (!rb) return true;
+  uint32_t any = 0;
+  const int w0 = t * 4;
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+    if (w0 + w < words) any |= rb[w0 + w];
+  return any != 0;
+}
+
+__global__ void __launch_bounds__(1024) attn_schedule_kernel(const uint32_t* __restrict__ bits,
+                                                             int B, int H, int S,
+                                                             int32_t* __restrict__ sched) {
+  pdl_launch_dependents();
+  pdl_wait();
+  // Dynamic shared memory: three int arrays of B entries.
+  extern __shared__ int sh[];
+  int* len = sh;           // valid keys per row, then live query tiles per row
+  int* order = sh + B;     // order[rank] = row
+  int* base = sh + 2 * B;  // first list index of each rank's live items
+  __shared__ int totals[2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int words = (S + 31) >> 5;
+  const int n_qt = (S + 127) >> 7;
+  const bool ranked = B <= KF_ORDER_MAX_B;
+  if (ranked) {
+    for (int b = warp; b < B; b += nwarps) {
+      int n = S;
+      if (bits) {
+        n = 0;
+        for (int w = lane; w < words; w += 32) n += __popc(bits[static_cast<int64_t>(b) * words + w]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+      }
+      if (lane == 0) len[b] = n;
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+      const int lb = len[b];
+      int rank = 0;
+      for (int c = 0; c < B; ++c) {
+        const int lc = len[c];
+        rank += (lc > lb) || (lc == lb && c < b);
+      }
+      order[rank] = b;
+    }
+  } else {
+    for (int b = threadIdx.x; b < B; b += blockDim.x) order[b] = b;
+  }
+  __syncthreads();
+  // Live query tiles per row (one warp per row, a ballot per 32 tiles).
+  for (int b = warp; b < B; b += nwarps) {
+    const uint32_t* rb = bits ? bits + static_cast<int64_t>(b) * words : nullptr;
+    int n = 0;
+    for (int t0 = 0; t0 < n_qt; t0 += 32)
+      n += __popc(__ballot_sync(0xffffffffu, t0 + lane < n_qt && q_tile_live(rb, words, t0 + lane)));
+    if (lane == 0) len[b] = n;  // every warp finished reading len[] before the barrier above
+  }
+  __syncthreads();
+  // List offsets in rank order: warp 0 scans H * live tiles over the ranks.
+  if (warp == 0) {
+    int run = 0;
+    for (int r0 = 0; r0 < B; r0 += 32) {
+      const int v = r0 + lane < B ? H * len[order[r0 + lane]] : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      if (r0 + lane < B) base[r0 + lane] = run + incl - v;
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      totals[0] = run;                   // live items
+      totals[1] = B * H * n_qt;          // all items
+    }
+  }
+  __syncthreads();
+  const int n_live = totals[0];
+  int2* items = reinterpret_cast<int2*>(sched + KF_SCHED_HEADER);
+  for (int r = warp; r < B; r += nwarps) {
+    const int b = order[r];
+    const uint32_t* rb = bits ? bits + static_cast<int64_t>(b) * words : nullptr;
+    const int nl = len[b], ne = n_qt - nl;
+    // Empty items of this rank start after every live item and the empty
+    // items of the ranks before it (which hold H * (n_qt - live) each).
+    const int live_base = base[r];
+    const int empty_base = n_live + (r * H * n_qt - live_base);
+    int seen_l = 0, seen_e = 0;
+    for (int t0 = 0; t0 < n_qt; t0 += 32) {
+      const int t = t0 + lane;
+      const bool in = t < n_qt;
+      const bool live = in && q_tile_live(rb, words, t);
+      const unsigned bl = __ballot_sync(0xffffffffu, live);
+      const unsigned be = __ballot_sync(0xffffffffu, in && !live);
+      const unsigned below = (1u << lane) - 1u;
+      if (live) {
+        const int pos = nl - 1 - (seen_l + __popc(bl & below));  // last tile first
+        for (int h = 0; h < H; ++h) items[live_base + h * nl + pos] = make_int2(b * H + h, t);
+      } else if (in) {
+        const int pos = seen_e + __popc(be & below);
+        for (int h = 0; h < H; ++h) items[empty_base + h * ne + pos] = make_int2(b * H + h, t);
+      }
+      seen_l += __popc(bl);
+      seen_e += __popc(be);
+    }
+  }
+  if (threadIdx.x == 0) {
+    sched[0] = 0;
+    sched[1] = 0;
+    sched[2] = n_live;
+    sched[3] = totals[1];
+  }
+}
+
 __global__ void round_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst,
                                   int64_t n) {
   pdl_launch_dependents();
@@ -284,6 +416,45 @@ extern "C" int kf_batch_order(const uint32_t* bits, int64_t B, int64_t S, int32_
                                     static_cast<cudaStream_t>(stream), bits,
                                     static_cast<int>(B), words, order),
                      "kf_batch_order launch");
+}
+
+extern "C" size_t kf_attn_schedule_words(int64_t B, int64_t H, int64_t S) {
+  if (B <= 0 || H <= 0 || S <= 0) return 0;
+  return static_cast<size_t>(KF_SCHED_HEADER) +
+         2 * static_cast<size_t>(B) * static_cast<size_t>(H) * static_cast<size_t>((S + 127) / 128);
+}
+
+extern "C" int kf_attn_schedule(const uint32_t* keep_bits, int64_t B, int64_t H, int64_t S,
+                                int32_t* sched, void* stream) {
+  if (!sched || B <= 0 || H <= 0 || S <= 0) {
+    set_last_error("kf_attn_schedule: invalid arguments (B=%lld H=%lld S=%lld)", (long long)B,
+                   (long long)H, (long long)S);
+    return KF_E_INVALID;
+  }
+  if (reinterpret_cast<uintptr_t>(sched) & 7u) {
+    set_last_error("kf_attn_schedule: sched must be 8-byte aligned");
+    return KF_E_INVALID;
+  }
+  if (B > KF_SCHED_MAX_B || B * H > 65535 || S > INT32_MAX - 127 ||
+      2 * B * H * ((S + 127) / 128) > static_cast<int64_t>(INT32_MAX)) {
+    set_last_error("kf_attn_schedule: needs B <= %d, B*H <= 65535 and a list of int32 size",
+                   KF_SCHED_MAX_B);
+    return KF_E_UNSUPPORTED;
+  }
+  const size_t smem = 3 * static_cast<size_t>(B) * sizeof(int);
+  static DeviceOnce once;
+  const int rc = once.run("kf_attn_schedule", nullptr, [&](int) {
+    return cuda_status(cudaFuncSetAttribute(attn_schedule_kernel,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            3 * KF_SCHED_MAX_B * static_cast<int>(sizeof(int))),
+                       "kf_attn_schedule: set smem attribute");
+  });
+  if (rc) return rc;
+  return cuda_status(launch_chained(attn_schedule_kernel, dim3(1), dim3(1024), smem,
+                                    static_cast<cudaStream_t>(stream), keep_bits,
+                                    static_cast<int>(B), static_cast<int>(H), static_cast<int>(S),
+                                    sched),
+                     "kf_attn_schedule launch");
 }
 
 extern "C" int kf_split_bf16x2(const float* src, int64_t rows, int64_t cols, int64_t ld_src,

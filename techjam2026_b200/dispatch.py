@@ -94,6 +94,15 @@ class Plan:
     # bit-identical output.
     order_rows: bool = False
 
+    # Persistent attention over a work list built once per forward
+    # (kf_attn_schedule + kf_flash_fwd_tf32_sched): one CTA per resident
+    # slot takes (row, head, query tile) items longest row first, heaviest
+    # causal tile first, keeping its barriers, TMEM and pipelines between
+    # items; query tiles without a valid query are not touched at all (their
+    # rows are padding, which every consumer masks). Bit-identical rows for
+    # every valid query.
+    attn_persistent: bool = True
+
     # Narrow I/O dtypes (float16/bfloat16): run the organiser's own layer,
     # captured whole into one CUDA graph, instead of these kernels. At those
     # dtypes the gate only admits the reference's exact arithmetic
@@ -119,7 +128,9 @@ class Plan:
             bits.append("skip-padded-rows")
         if self.fuse_ln:
             bits.append("ln-in-gemm")
-        if self.order_rows:
+        if self.attn_persistent:
+            bits.append("persistent-attn")
+        elif self.order_rows:
             bits.append("rows-longest-first")
         if self.exact_reference:
             return "exact-reference+cuda-graph"

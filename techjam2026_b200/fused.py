@@ -117,6 +117,10 @@ class _Workspace:
         self.live_tiles = torch.zeros((M + 127) // 128, **i32)
         self.live_count = torch.zeros(1, **i32)
         self.order = torch.zeros(B, **i32)
+        # Work list of the persistent attention (kf_attn_schedule), built once
+        # per forward; zeroed so its counters start at 0.
+        self.sched = (torch.zeros(int(_lib.lib().kf_attn_schedule_words(B, H, S)), **i32)
+                      if plan.attn_persistent else None)
         # Stream-K GEMMs share one zeroed workspace (partials + counters);
         # the kernels leave its counters zero, and they run one after another.
         sk_bytes = _Workspace.sk_bytes(cfg, M, plan)
@@ -143,7 +147,7 @@ class _Workspace:
         return sum(t.numel() * t.element_size()
                    for t in (self.res, self.h, self.h2, self.qkv, self.ctx, self.y, self.ffn,
                              self.bits, self.live_tiles, self.live_count, self.order,
-                             self.sk)
+                             self.sk, self.sched)
                    if t is not None)
 
     @staticmethod
@@ -158,8 +162,9 @@ class _Workspace:
         per_row += 4 * d if (split["qkv"] or split["ffn1"]) else 0    # h2 planes
         per_row += 4 * 3 * H * dh_store + 4 * d + 4 * d + 4 * F       # qkv, ctx, y, ffn
         words = (S + 31) // 32
+        sched = 4 * (8 + 2 * B * H * ((S + 127) // 128)) if plan.attn_persistent else 0
         return (M * per_row + 4 * B * words + 4 * B + 4 * ((M + 127) // 128) + 4
-                + _Workspace.sk_bytes(cfg, M, plan))
+                + _Workspace.sk_bytes(cfg, M, plan) + sched)
 
 
 class FusedTransformer(LayerStack):
@@ -320,9 +325,16 @@ class FusedTransformer(LayerStack):
             run("keep_bits", L.kf_keep_bits, keep, S, B, S, bits, st)
         if skip_rows:
             run("keep_bits", L.kf_live_row_tiles, keep, M, lt, lc, st)
-        order = ws.order.data_ptr() if (keep is not None and plan.order_rows and B > 1) else None
+        sched = ws.sched.data_ptr() if plan.attn_persistent else None
+        order = (ws.order.data_ptr() if (sched is None and keep is not None and plan.order_rows
+                                         and B > 1) else None)
         if order is not None:
             run("keep_bits", L.kf_batch_order, bits, B, S, order, st)
+        if sched is not None:
+            run("keep_bits", L.kf_attn_schedule, bits, B, H, S, sched, st)
+            if keep is not None and plan.skip_empty_queries:
+                # rows of query tiles without a valid query are padding: not written
+                attn_flags = (attn_flags & ~_lib.KF_ATTN_SKIP_EMPTY_Q) | _lib.KF_ATTN_EMPTY_Q_UNTOUCHED
         l0 = w.layers[0]
         run("ln", L.kf_ln_add_mask, x.data_ptr(), d, None, 0, keep, l0["ln1w"].data_ptr(),
             l0["ln1b"].data_ptr(), res, d, h_qkv, d, M, d, l0["eps1"], f_ln1, st)
@@ -336,7 +348,12 @@ class FusedTransformer(LayerStack):
         for i, lw in enumerate(w.layers):
             gemm("qkv", "qkv", h_qkv, d, lw["wqkv"], lw["bqkv"], qkv, ldq, 3 * d, d,
                  _lib.KF_EPI_BIAS, _lib.KF_GEMM_ROUND_TF32 if R else 0, plan.bn_qkv, hd, hs)
-            if order is not None:
+            if sched is not None:
+                run("attention", L.kf_flash_fwd_tf32_sched, qkv, S * ldq, dhs, ldq,
+                    qkv + 4 * H * dhs, S * ldq, dhs, ldq, qkv + 8 * H * dhs, S * ldq, dhs,
+                    ldq, ctx, S * d, dh, d, bits, sched, B, H, S, dhs, dh, dh ** -0.5,
+                    attn_flags, st)
+            elif order is not None:
                 run("attention", L.kf_flash_fwd_tf32_ordered, qkv, S * ldq, dhs, ldq,
                     qkv + 4 * H * dhs, S * ldq, dhs, ldq, qkv + 8 * H * dhs, S * ldq, dhs,
                     ldq, ctx, S * d, dh, d, bits, order, B, H, S, dhs, dh, dh ** -0.5,

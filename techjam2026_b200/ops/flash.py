@@ -5,9 +5,12 @@
 
 per (batch, head), softmax in fp32; Q/K/V are strided [B, H, S, Dh] views
 with unit stride on Dh (e.g. views into a fused [B, S, 3, H, Dh] QKV buffer).
-Runs `kf_keep_bits` + `kf_flash_fwd_tf32` (csrc/flash_sm100.cu): TF32
-tcgen05 contractions with FP32 TMEM accumulators. A query row whose keys are
-all masked yields 0 (not NaN), as in the reference kernel (flash.py:241-243).
+Runs `kf_keep_bits`, `kf_attn_schedule` and the persistent
+`kf_flash_fwd_tf32_sched` (csrc/flash_persist_sm100.cu), or with
+`persistent=False` the one-CTA-per-query-tile `kf_flash_fwd_tf32`
+(csrc/flash_sm100.cu); both give the same bits: TF32 tcgen05 contractions
+with FP32 TMEM accumulators. A query row whose keys are all masked yields 0
+(not NaN), as in the reference kernel (flash.py:241-243).
 
 `smem_kb` and `block` are accepted for signature compatibility; the sm_100
 kernel's tiling is fixed per head_dim. `round_scores_to` (fp16/bf16 score
@@ -61,6 +64,7 @@ def flash_attention(
     round_scores_to: Optional[torch.dtype] = None,
     skip_empty_queries: bool = False,
     round_tf32_out: bool = False,
+    persistent: bool = True,
 ) -> torch.Tensor:
     B, H, S, Dh = q.shape
     assert flash_supported(Dh), f"unsupported head_dim {Dh}"
@@ -90,12 +94,34 @@ def flash_attention(
     flags = ((_lib.KF_ATTN_CAUSAL if causal else 0)
              | (_lib.KF_ATTN_SKIP_EMPTY_Q if skip_empty_queries else 0)
              | (_lib.KF_ATTN_ROUND_TF32 if round_tf32_out else 0))
-    rc = _lib.lib().kf_flash_fwd_tf32(
-        q.data_ptr(), q.stride(0), q.stride(1), q.stride(2),
-        k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
-        v.data_ptr(), v.stride(0), v.stride(1), v.stride(2),
-        o.data_ptr(), o.stride(0), o.stride(1), o.stride(2),
-        bits.data_ptr() if bits is not None else None,
-        B, H, S, dh_store, Dh, float(sm_scale), flags, _lib.stream_ptr())
-    _lib.check(rc, "kf_flash_fwd_tf32")
+    L = _lib.lib()
+    st = _lib.stream_ptr()
+    args = (q.data_ptr(), q.stride(0), q.stride(1), q.stride(2),
+            k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+            v.data_ptr(), v.stride(0), v.stride(1), v.stride(2),
+            o.data_ptr(), o.stride(0), o.stride(1), o.stride(2),
+            bits.data_ptr() if bits is not None else None)
+    if persistent and B > 0 and H > 0 and S > 0:
+        sched = attn_schedule(bits, B, H, S)
+        rc = L.kf_flash_fwd_tf32_sched(*args, sched.data_ptr(), B, H, S, dh_store, Dh,
+                                       float(sm_scale), flags, st)
+        _lib.check(rc, "kf_flash_fwd_tf32_sched")
+    else:
+        rc = L.kf_flash_fwd_tf32(*args, B, H, S, dh_store, Dh, float(sm_scale), flags, st)
+        _lib.check(rc, "kf_flash_fwd_tf32")
     return o
+
+
+def attn_schedule(bits: Optional[torch.Tensor], B: int, H: int, S: int,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Work list of the persistent attention for key bits of [B, S] rows
+    (None: every key valid) and H heads (kf_attn_schedule)."""
+    L = _lib.lib()
+    words = int(L.kf_attn_schedule_words(B, H, S))
+    device = bits.device if bits is not None else torch.device("cuda", torch.cuda.current_device())
+    if out is None:
+        out = torch.empty(words, dtype=torch.int32, device=device)
+    rc = L.kf_attn_schedule(bits.data_ptr() if bits is not None else None, B, H, S,
+                            out.data_ptr(), _lib.stream_ptr())
+    _lib.check(rc, "kf_attn_schedule")
+    return out

@@ -121,3 +121,22 @@ def test_noalloc_entry_rejects_bad_attention_arguments_before_any_launch():
     assert b"strides" in lib.kf_last_error()
     assert call(ld_keep=4) == _lib.KF_E_INVALID
     assert b"ld_keep" in lib.kf_last_error()
+
+
+def test_persistent_attention_entries_reject_before_any_launch():
+    lib = _lib.lib()
+    fake = ctypes.c_void_p(0x1000)   # never dereferenced
+    assert lib.kf_attn_schedule_words(2, 3, 129) == 8 + 2 * 2 * 3 * 2
+    assert lib.kf_attn_schedule_words(0, 3, 129) == 0
+    assert lib.kf_attn_schedule(None, 2, 3, 100, None, None) == _lib.KF_E_INVALID
+    assert lib.kf_attn_schedule(None, 20000, 1, 100, fake, None) == _lib.KF_E_UNSUPPORTED
+    assert lib.kf_attn_schedule(None, 2, 1, 100, ctypes.c_void_p(0x1004), None) == \
+        _lib.KF_E_INVALID
+    assert lib.kf_attn_schedule(None, 1000, 100, 100, fake, None) == _lib.KF_E_UNSUPPORTED
+    args = (fake, 4096, 512, 64, fake, 4096, 512, 64, fake, 4096, 512, 64, fake, 4096, 512, 64,
+            None)
+    assert lib.kf_flash_fwd_tf32_sched(*args, None, 1, 1, 8, 64, 64, 0.125, 0, None) == \
+        _lib.KF_E_INVALID
+    assert b"sched is null" in lib.kf_last_error()
+    assert lib.kf_flash_fwd_tf32_sched(*args, fake, 1, 1, 8, 48, 48, 0.125, 0, None) == \
+        _lib.KF_E_UNSUPPORTED

@@ -1055,3 +1055,199 @@ def test_flash_attention_options(causal):
     assert (buf.permute(0, 2, 1, 3).double() - ref).abs().max().item() < 5e-3
     with pytest.raises(NotImplementedError):
         flash_attention(q, k, v, causal=causal, round_scores_to=torch.float16)
+
+
+# ------------------------------------------------------------ persistent attention
+
+def _bits_of(keep):
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    B, S = keep.shape
+    bits = torch.empty(int(L.kf_keep_bits_words(B, S)), dtype=torch.int32, device="cuda")
+    _lib.check(L.kf_keep_bits(keep.data_ptr(), keep.stride(0), B, S, bits.data_ptr(),
+                              _lib.stream_ptr()), "kf_keep_bits")
+    return bits
+
+
+def _expected_schedule(keep, B, H, S):
+    """The work list kf_attn_schedule documents, built on the host: rows by
+    valid-key count (longest first, ties by index), per row its heads, per
+    head the query tiles holding a valid token from the last to the first;
+    then the tiles without one, in the same row and head order."""
+    n_qt = (S + 127) // 128
+    if keep is None:
+        counts = [S] * B
+        live = [[True] * n_qt for _ in range(B)]
+    else:
+        kc = keep.cpu().bool()
+        counts = kc.sum(1).tolist()
+        live = [[bool(kc[b, t * 128:(t + 1) * 128].any()) for t in range(n_qt)] for b in range(B)]
+    order = sorted(range(B), key=lambda b: (-counts[b], b)) if B <= 4096 else list(range(B))
+    items = []
+    for b in order:
+        for h in range(H):
+            items += [(b * H + h, t) for t in reversed(range(n_qt)) if live[b][t]]
+    n_live = len(items)
+    for b in order:
+        for h in range(H):
+            items += [(b * H + h, t) for t in range(n_qt) if not live[b][t]]
+    return n_live, items
+
+
+@pytest.mark.parametrize("B,H,S,masked", [(1, 1, 100, True), (7, 3, 333, True), (64, 12, 2048, True),
+                                          (5, 2, 66000, True), (300, 2, 200, True),
+                                          (3, 4, 1000, False)])
+def test_attn_schedule_matches_its_definition(B, H, S, masked):
+    from techjam2026_b200.ops.flash import attn_schedule
+    g = torch.Generator().manual_seed(B * 7 + S)
+    keep = None
+    if masked:
+        lengths = torch.randint(0, S + 1, (B,), generator=g)
+        lengths[: B // 3] = lengths[0]                          # ties
+        keep = (torch.rand(B, S, generator=g) < 0.8).to(torch.uint8)
+        keep &= (torch.arange(S)[None, :] < lengths[:, None]).to(torch.uint8)
+        if S > 300:
+            keep[0, 128:256] = 0                                # an empty tile mid-row
+        keep = keep.cuda()
+    bits = _bits_of(keep) if keep is not None else None
+    sched = attn_schedule(bits, B, H, S)
+    torch.cuda.synchronize()
+    n_live, items = _expected_schedule(keep, B, H, S)
+    s = sched.cpu()
+    assert s[0].item() == 0 and s[1].item() == 0
+    assert s[2].item() == n_live and s[3].item() == len(items) == B * H * ((S + 127) // 128)
+    got = s[8:8 + 2 * len(items)].view(-1, 2).tolist()
+    assert [tuple(x) for x in got] == items
+
+
+def _attn_call(q, k, v, o, bits, flags, sched=None, o_strides=None, dh_out=None):
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    B, H, S, Dh = q.shape
+    qs = q.stride()
+    args = [q.data_ptr(), *qs[:3], k.data_ptr(), *k.stride()[:3], v.data_ptr(), *v.stride()[:3],
+            o.data_ptr(), *(o_strides or o.stride()[:3]),
+            bits.data_ptr() if bits is not None else None]
+    if sched is None:
+        rc = L.kf_flash_fwd_tf32(*args, B, H, S, Dh, dh_out or Dh, Dh ** -0.5, flags,
+                                 _lib.stream_ptr())
+    else:
+        rc = L.kf_flash_fwd_tf32_sched(*args, sched.data_ptr(), B, H, S, Dh, dh_out or Dh,
+                                       Dh ** -0.5, flags, _lib.stream_ptr())
+    _lib.check(rc, "attention")
+
+
+@pytest.mark.parametrize("Dh", [16, 32, 64, 128, 256])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("mode", ["zeros", "compute", "untouched"])
+def test_flash_sched_is_bit_identical_to_one_cta_per_tile(Dh, causal, mode):
+    """kf_flash_fwd_tf32_sched gives the bits of kf_flash_fwd_tf32 for every
+    row it writes, on ragged non-prefix masks with empty query tiles (inside
+    a row, at its end, a row without any valid token), twice in a row on one
+    work list (its counters reset themselves). Empty query tiles: zeros
+    (KF_ATTN_SKIP_EMPTY_Q), computed like any tile, or left untouched
+    (KF_ATTN_EMPTY_Q_UNTOUCHED)."""
+    from techjam2026_b200 import _lib
+    from techjam2026_b200.ops.flash import attn_schedule
+    torch.manual_seed(Dh * 3 + causal)
+    B, H, S = (5, 3, 777) if Dh < 256 else (3, 2, 500)
+    q, k, v = (torch.randn(B, H, S, Dh, device="cuda") for _ in range(3))
+    keep = (torch.rand(B, S, device="cuda") > 0.2).to(torch.uint8)
+    keep[0, 128:256] = 0
+    keep[1, 300:] = 0
+    keep[2] = 0
+    bits = _bits_of(keep)
+    base = _lib.KF_ATTN_CAUSAL if causal else 0
+    ref_flags = base | (_lib.KF_ATTN_SKIP_EMPTY_Q if mode != "compute" else 0)
+    ref = torch.full((B, H, S, Dh), 7.0, device="cuda")
+    _attn_call(q, k, v, ref, bits, ref_flags)
+    flags = base | {"zeros": _lib.KF_ATTN_SKIP_EMPTY_Q, "compute": 0,
+                    "untouched": _lib.KF_ATTN_EMPTY_Q_UNTOUCHED}[mode]
+    sched = attn_schedule(bits, B, H, S)
+    outs = []
+    for _ in range(2):
+        o = torch.full((B, H, S, Dh), 7.0, device="cuda")
+        _attn_call(q, k, v, o, bits, flags, sched)
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    o = outs[0]
+    if mode == "untouched":
+        n_t = (S + 127) // 128
+        kb = keep.bool()
+        tile_live = torch.stack([kb[:, t * 128:(t + 1) * 128].any(1) for t in range(n_t)], 1)
+        row_live = tile_live.repeat_interleave(128, dim=1)[:, :S][:, None, :, None].expand_as(o)
+        assert torch.equal(o[row_live], ref[row_live])
+        assert torch.all(o[~row_live] == 7.0)
+    else:
+        assert torch.equal(o, ref)
+    assert sched[:2].cpu().tolist() == [0, 0]
+    assert _lib.lib().kf_device_status(0) == 0
+
+
+@pytest.mark.parametrize("Dh,H", [(64, 12), (16, 8), (32, 8), (128, 4), (256, 2)])
+@pytest.mark.parametrize("split", [False, True])
+def test_flash_sched_many_items_per_cta(split, Dh, H):
+    """More items than resident CTAs (c4's rows: 16 rows x 16 query tiles
+    per head, lengths from 1 to 2048, so items of 1 to 32 key tiles follow
+    one another in every CTA) on strided views of a fused QKV buffer with
+    [B, S, H, Dh] output rows, fp32 or bf16 hi/lo planes: the persistent
+    kernel matches the one-CTA-per-tile kernel bit for bit, call after call
+    on one list, and the float64 reference."""
+    from techjam2026_b200 import _lib
+    from techjam2026_b200.ops.flash import attn_schedule
+    torch.manual_seed(41 + split + Dh)
+    B, S = 16, 2048
+    d = H * Dh
+    qkv = torch.randn(B, S, 3, H, Dh, device="cuda")
+    q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+    lengths = torch.randint(1, S + 1, (B,))
+    keep = (torch.arange(S)[None, :] < lengths[:, None]).to(torch.uint8).cuda()
+    bits = _bits_of(keep)
+    flags = _lib.KF_ATTN_CAUSAL | _lib.KF_ATTN_SKIP_EMPTY_Q
+    if split:
+        flags |= _lib.KF_ATTN_OUT_BF16X2
+        mk = lambda: torch.full((2, B, S, d), 7, dtype=torch.int16, device="cuda")  # noqa: E731
+    else:
+        mk = lambda: torch.full((B, S, d), 7.0, device="cuda")  # noqa: E731
+    strides = (S * d, Dh, d)
+    ref = mk()
+    _attn_call(q, k, v, ref, bits, flags, o_strides=strides)
+    sched = attn_schedule(bits, B, H, S)
+    for _ in range(3):
+        o = mk()
+        _attn_call(q, k, v, o, bits, flags, sched, o_strides=strides)
+        torch.cuda.synchronize()
+        assert torch.equal(o, ref)
+    got = from_planes(o) if split else o
+    got = got.reshape(B, S, H, Dh).permute(0, 2, 1, 3)
+    rows = [0, 127, 128, 1000, 2047]
+    want = _reference_rows(q, k, v, keep, True, rows)
+    # rows of query tiles without a valid query are zeros (KF_ATTN_SKIP_EMPTY_Q)
+    lens = lengths.cuda()
+    live = (torch.tensor(rows, device="cuda")[None, :] // 128 * 128 < lens[:, None])
+    live = live[:, None, :, None].expand_as(want)
+    assert (got[:, :, rows].double() - want)[live].abs().max().item() < 5e-3
+    assert torch.all(got[:, :, rows][~live] == 0)
+    assert _lib.lib().kf_device_status(0) == 0
+
+
+def test_flash_sched_without_mask_and_long_rows():
+    """No key mask (every tile live) and a row long enough that the key bits
+    do not fit the one-CTA kernel's shared-memory staging (S = 66000)."""
+    from techjam2026_b200 import _lib
+    from techjam2026_b200.ops.flash import attn_schedule
+    torch.manual_seed(43)
+    for (B, H, S, masked) in [(2, 4, 1000, False), (1, 2, 66000, True)]:
+        q, k, v = (torch.randn(B, H, S, 64, device="cuda") for _ in range(3))
+        keep = bits = None
+        if masked:
+            keep = (torch.rand(B, S, device="cuda") > 0.3).to(torch.uint8)
+            keep[:, 5000:9000] = 0
+            bits = _bits_of(keep)
+        ref = torch.empty(B, H, S, 64, device="cuda")
+        _attn_call(q, k, v, ref, bits, _lib.KF_ATTN_CAUSAL)
+        o = torch.empty_like(ref)
+        _attn_call(q, k, v, o, bits, _lib.KF_ATTN_CAUSAL, attn_schedule(bits, B, H, S))
+        torch.cuda.synchronize()
+        assert torch.equal(o, ref)

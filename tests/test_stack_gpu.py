@@ -354,3 +354,31 @@ def test_single_token_sequences(with_mask):
     assert _lib_status() == 0
     assert torch.equal(out, eager)
     _assert_gate(_oracle(cfg, sd, x, mask), out, f"S=1 mask={with_mask}")
+
+
+@pytest.mark.parametrize("wname", ["c4", "c3b", "c2", "c3a"])
+def test_persistent_attention_forward_is_bit_identical(wname):
+    """plan.attn_persistent (kf_attn_schedule + kf_flash_fwd_tf32_sched)
+    changes only how attention is scheduled and that query tiles without a
+    valid query are left unwritten (their rows are padding, masked by every
+    consumer): the forward is bit-identical to the one-CTA-per-tile kernel,
+    through the captured graph and eagerly, on ragged batches."""
+    import dataclasses
+    from techjam2026_b200.dispatch import DispatchTable, probe
+    w = WORKLOADS[wname]
+    cfg = dataclasses.replace(w.cfg, batch_size=6, num_layers=2)
+    sd = make_state_dict(cfg, 7)
+    x, mask = generate_case(cfg, 7, w.padding_ratio, w.input_scale)
+    xd, md = x.cuda(), mask.cuda()
+    spec = probe()
+    plan, _ = DispatchTable.load_for(spec).lookup(spec.arch, torch.float32, cfg)
+    outs = []
+    for persistent in (False, True):
+        m = _model(cfg, sd, dataclasses.replace(plan, attn_persistent=persistent))
+        outs.append((m(xd, md).clone(), m.eager_forward(xd, md).clone(), m(xd, md).clone()))
+        m.release_buffers()
+    torch.cuda.synchronize()
+    assert _lib_status() == 0
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a, b)
+    assert padded_rows_exactly_zero(outs[1][0], mask)
