@@ -45,3 +45,17 @@ def test_norm_bytes_count_valid_rows():
     assert full == (12 + (2 * L - 1) * 16 + 8) * d * M
     half = ln_bytes_per_forward(cfg, [cfg.seq_len // 2] * cfg.batch_size)
     assert half == (12 + (2 * L - 1) * 16 + 8) * d * M / 2 + 4 * d * M / 2
+
+
+def test_committed_c4_capture_matches_the_tables_plan():
+    """profiles/traffic_c4.md was captured under the plan the dispatch table
+    gives c4 today, for every kernel kind of the forward; a plan change
+    without a new capture fails here (bench.py would report no traffic)."""
+    from techjam2026_b200.dispatch import DispatchTable
+    cfg = WORKLOADS["c4"].cfg
+    plan, source = DispatchTable.load("sm_100").lookup("sm_100", torch.float32, cfg)
+    assert source == "exact"
+    for kind in ("qkv", "attention", "out_proj", "ln", "ffn1", "ffn2"):
+        hit = profiled_traffic("c4", cfg.batch_size, kind, plan.describe())
+        assert hit is not None and hit["plan_match"], kind
+        assert hit["source"] == "profiles/traffic_c4.md"
