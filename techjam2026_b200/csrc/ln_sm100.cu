@@ -27,8 +27,14 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Rows of 768 and 1024 floats (NV 6, 8) keep four 256-thread blocks per SM
+// (64 registers a thread, no spills): the norm is a memory-latency-bound
+// stream, and more rows in flight per SM is what brings it to the copy
+// bandwidth (c4: 165.9 -> 135.2 us per norm, 0.95 of the measured copy
+// rate). Other widths keep the compiler's choice (at 64 registers NV 4
+// would spill).
 template <int NV>
-__global__ void __launch_bounds__(256) ln_add_mask_vec_kernel(
+__global__ void __launch_bounds__(256, (NV == 6 || NV == 8) ? 4 : 1) ln_add_mask_vec_kernel(
     const float* x, int64_t ldx, const float* y, int64_t ldy, const uint8_t* __restrict__ keep,
     const float* __restrict__ w, const float* __restrict__ b, float* s_out, int64_t lds,
     float* __restrict__ h_out, int64_t ldh, int64_t M,
@@ -39,13 +45,15 @@ __global__ void __launch_bounds__(256) ln_add_mask_vec_kernel(
   if (row >= M) return;
   const int nv4 = d >> 2;
   // The kernel is latency-bound (one short row per warp), so every load it
-  // needs -- the row's keep byte, x, y and, for rows of up to 1024 floats,
+  // needs -- the row's keep byte, x, y and, for rows of up to 512 floats,
   // gamma and beta -- is issued up front instead of one dependent round trip
   // after another; a padded row's loads are simply not used. With
   // KF_LN_STATIC_PARAMS (keep, gamma and beta were written before the
   // previous kernel in the stream started) those go out before the wait on
   // the previous kernel, and a skipped padded row leaves without waiting.
-  constexpr bool PREFETCH_WB = NV <= 8;
+  // Wider rows read gamma and beta (L1-resident) where they are used, which
+  // keeps their register count low enough for four blocks per SM.
+  constexpr bool PREFETCH_WB = NV <= 4;  // wider rows load gamma/beta where they are used
   constexpr int NW = PREFETCH_WB ? NV : 1;
   const bool early = (flags & KF_LN_STATIC_PARAMS) != 0;
   float4 gw[NW], gb[NW];
