@@ -571,8 +571,10 @@ def main():
             f1.record()
             torch.cuda.synchronize()
             f_ts.append(f0.elapsed_time(f1))
-        h2d = int(xh.numel() * 4 + mh.numel())
-        d2h = int(oh.numel() * 4)
+        # Bytes the loop moved per step: each row's valid prefix (prefix masks)
+        # plus the mask; whole tensors otherwise.
+        h2d = int(pipe.last_h2d_bytes)
+        d2h = int(pipe.last_d2h_bytes)
         e2e = {"value": round(flops_all / (e_step / 1e3) / 1e12, 3), "unit": "TFLOP/s",
                "ms_per_step": round(e_step, 4),
                "l2_flush_ms_per_step_inside": round(statistics.median(f_ts), 4),
@@ -580,7 +582,8 @@ def main():
                "d2h_bytes_per_step": d2h * world,
                "h2d_bytes_per_rank": h2d, "d2h_bytes_per_rank": d2h,
                "h2d_d2h_gbs_per_rank": round((h2d + d2h) / (e_step / 1e3) / 1e9, 2),
-               "loop": "StreamedForward: copies on two streams overlap the forward",
+               "loop": ("StreamedForward: copies on two streams overlap the forward; "
+                        + ("valid row prefixes only" if pipe.packed else "whole tensors")),
                "serial_ms_per_step": round(serial_step, 4),
                "serial_value": round(flops_all / (serial_step / 1e3) / 1e12, 3)}
 

@@ -9,6 +9,14 @@ another. PCIe is full duplex and the GPU has several copy engines, so in
 steady state a batch costs the longest of the three, not their sum. Device
 buffers are double-buffered; every batch still crosses PCIe both ways.
 
+Padding stays on the host. With a bool prefix mask (each row's valid
+tokens first, as the organiser's generator draws them) only each row's
+valid prefix crosses PCIe in either direction: the forward never reads a
+padded row of x (the first norm masks it by a select), and a padded row of
+the result is exactly zero, which the loop writes into the host result
+buffer itself (once per buffer, and again only where a row got shorter).
+For c4 that is about half the bytes of the whole [B, S, d] tensors.
+
 The forward itself is the model's CUDA graph, so results are bit-identical
 to calling the model on each batch. For a `FusedTransformer` with a bool
 mask (or none) there is one graph per buffer slot, captured on that slot's
@@ -32,7 +40,7 @@ class StreamedForward:
     otherwise the copies are synchronous and nothing overlaps."""
 
     def __init__(self, model: FusedTransformer, x_example: torch.Tensor,
-                 mask_example: Optional[torch.Tensor] = None):
+                 mask_example: Optional[torch.Tensor] = None, packed: bool = True):
         if not x_example.is_cuda:
             raise ValueError("x_example must be a CUDA tensor of the batch shape")
         self.device = x_example.device
@@ -53,6 +61,44 @@ class StreamedForward:
                           for b in range(2)]
         else:
             self.runner = model.graph_runner(x_example, mask_example)
+        # Copies of valid prefixes only (fused model with a bool mask).
+        self.packed = packed and self.bound is not None
+        # Host result buffers: rows this loop has written per batch row
+        # (None: unknown) and the event of the last download into each.
+        self._out_rows = {}
+        self._out_event = {}
+        self.last_h2d_bytes = 0
+        self.last_d2h_bytes = 0
+
+    @staticmethod
+    def prefix_lengths(mask: Optional[torch.Tensor]) -> Optional[List[int]]:
+        """Valid length of every row of a host bool [B, S] mask whose valid
+        tokens form a prefix of the row; None for any other mask."""
+        if (mask is None or mask.is_cuda or mask.dtype != torch.bool or mask.dim() != 2):
+            return None
+        lens = mask.sum(dim=1)
+        if not torch.equal(torch.arange(mask.shape[1])[None, :] < lens[:, None], mask):
+            return None
+        return [int(v) for v in lens.tolist()]
+
+    def _clear_padding(self, out: torch.Tensor, lens: List[int]) -> None:
+        """Make the padded rows of host result buffer `out` zero before a
+        download of valid prefixes only: all of them the first time the
+        buffer is seen, later only rows that were valid in its last use.
+        Rows an earlier download may still be writing are cleared only after
+        that download has finished."""
+        key = (out.data_ptr(), tuple(out.shape))
+        prev = self._out_rows.get(key)
+        S = out.shape[1]
+        todo = [(i, l, S if prev is None else prev[i]) for i, l in enumerate(lens)]
+        todo = [(i, a, e) for i, a, e in todo if e > a]
+        if todo:
+            ev = self._out_event.get(key)
+            if ev is not None:
+                ev.synchronize()
+            for i, a, e in todo:
+                out[i, a:e].zero_()
+        self._out_rows[key] = list(lens)
 
     def run(self, xs: Sequence[torch.Tensor], masks: Optional[Sequence[torch.Tensor]],
             outs: Sequence[torch.Tensor], before_step=None) -> None:
@@ -75,13 +121,35 @@ class StreamedForward:
         downloaded = [torch.cuda.Event() for _ in range(n)]
         self.up.wait_stream(comp)
         self.down.wait_stream(comp)
+        memo = {}  # one prefix check per distinct mask tensor of the call
+
+        def lengths_of(m):
+            if id(m) not in memo:
+                memo[id(m)] = self.prefix_lengths(m)
+            return memo[id(m)]
+        lens = [lengths_of(masks[k]) if (self.packed and masks is not None) else None
+                for k in range(n)]
+        row_bytes = xs[0].shape[-1] * xs[0].element_size()
+        h2d = d2h = 0
+        for k in range(n):
+            full = xs[k].numel() * xs[k].element_size()
+            h2d += full if lens[k] is None else sum(lens[k]) * row_bytes
+            d2h += full if lens[k] is None else sum(lens[k]) * row_bytes
+            if self.with_mask:
+                h2d += masks[k].numel() * masks[k].element_size()
+        self.last_h2d_bytes, self.last_d2h_bytes = h2d // n, d2h // n
 
         def upload(k: int) -> None:
             b = k % 2
             with torch.cuda.stream(self.up):
                 if k >= 2:
                     self.up.wait_event(loaded[k - 2])  # forward k-2 has read buffer b
-                self.xd[b].copy_(xs[k], non_blocking=True)
+                if lens[k] is None:
+                    self.xd[b].copy_(xs[k], non_blocking=True)
+                else:
+                    for i, l in enumerate(lens[k]):
+                        if l:
+                            self.xd[b][i, :l].copy_(xs[k][i, :l], non_blocking=True)
                 if self.with_mask:
                     self.md[b].copy_(masks[k], non_blocking=True)
                 uploaded[k].record(self.up)
@@ -109,8 +177,17 @@ class StreamedForward:
             computed[k].record(comp)
             with torch.cuda.stream(self.down):
                 self.down.wait_event(computed[k])
-                outs[k].copy_(self.od[b], non_blocking=True)
+                key = (outs[k].data_ptr(), tuple(outs[k].shape))
+                if lens[k] is None:
+                    outs[k].copy_(self.od[b], non_blocking=True)
+                    self._out_rows[key] = None
+                else:
+                    self._clear_padding(outs[k], lens[k])
+                    for i, l in enumerate(lens[k]):
+                        if l:
+                            outs[k][i, :l].copy_(self.od[b][i, :l], non_blocking=True)
                 downloaded[k].record(self.down)
+                self._out_event[key] = downloaded[k]
         comp.wait_event(downloaded[n - 1])
 
     def __call__(self, xs: List[torch.Tensor], masks: Optional[List[torch.Tensor]] = None

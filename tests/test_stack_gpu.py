@@ -212,6 +212,45 @@ def test_native_library_is_the_one_loaded():
     assert _lib.lib().kf_device_status(0) == 0
 
 
+def test_streamed_forward_packed_copies_handle_changing_lengths():
+    """Valid-prefix copies: the serving loop moves only each row's valid
+    prefix, yet every result equals the model's whole output bit for bit
+    (padded rows exactly zero), also when the same host result buffers are
+    reused while rows get longer and shorter, and for a mask that is not a
+    prefix (which takes whole-tensor copies)."""
+    from techjam2026_b200.serving import StreamedForward
+    case = load_case("mini_s333")
+    cfg = case["cfg"]
+    m = _model(cfg, case["state_dict"])
+    B, S = cfg.batch_size, cfg.seq_len
+    g = torch.Generator().manual_seed(5)
+    xs, masks = [], []
+    for k in range(6):
+        lens = torch.randint(0, S + 1, (B,), generator=g)
+        if k == 3:
+            lens[:] = S                                 # every row full length
+        mask = torch.arange(S)[None, :] < lens[:, None]
+        x = torch.randn(B, S, cfg.d_model, generator=g).masked_fill(~mask[..., None], 0)
+        if k == 4:
+            mask = mask.clone()
+            mask[0, 0] = False                          # not a prefix: whole copies
+        xs.append(x.pin_memory())
+        masks.append(mask.pin_memory())
+    pipe = StreamedForward(m, xs[0].cuda(), masks[0].cuda())
+    assert pipe.packed
+    assert StreamedForward.prefix_lengths(masks[4]) is None
+    outs = [torch.full_like(xs[0], 9.0).pin_memory() for _ in range(2)]
+    for rnd in range(2):
+        sched = list(range(6)) if rnd == 0 else list(range(5, -1, -1))
+        res = [outs[i % 2] for i in range(6)]
+        for i, k in enumerate(sched):
+            pipe.run([xs[k]], [masks[k]], [res[i]])
+            torch.cuda.current_stream().synchronize()
+            want = m(xs[k].cuda(), masks[k].cuda()).cpu()
+            assert torch.equal(res[i], want), f"round {rnd} batch {k}"
+    assert pipe.last_h2d_bytes > 0
+
+
 @pytest.mark.parametrize("mask_dtype", [torch.bool, torch.float32])
 def test_streamed_forward_matches_per_batch_calls(mask_dtype):
     """The serving loop (uploads and downloads on their own streams, double
