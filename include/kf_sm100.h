@@ -50,6 +50,20 @@ const char* kf_last_error(void);
  * call got a batch_order entry outside [0, B). `reset` != 0 clears it. */
 int kf_device_status(int reset);
 
+/* The same status word copied into host_dst (pinned host memory, one int32)
+ * by a copy queued on `stream`, without synchronising: it holds the status
+ * once that stream reaches the copy. Lets a caller check the library's health
+ * after each call at no cost to the call (submission.py reads it one call
+ * later and falls back when it is nonzero). */
+int kf_device_status_async(int32_t* host_dst, void* stream);
+
+/* Time limit of every bounded wait of the current device's kernels, in SM
+ * cycles (synchronous; takes effect for later launches). cycles <= 0 restores
+ * the default (~2 s). Waits that drain in-flight copies while a CTA unwinds
+ * keep the default, so a short limit only makes a stuck wait give up sooner.
+ * For tests of the failure path: a real wait takes microseconds. */
+int kf_set_wait_limit(int64_t cycles);
+
 /* ----------------------------------------------------------- LayerNorm */
 
 #define KF_LN_MASK_OUT 1   /* zero h on rows whose keep byte is 0 (final norm) */

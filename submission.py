@@ -11,7 +11,11 @@ Same contract as the reference's submission.py:40-106:
     its exact arithmetic there, as the reference's own table records);
   * if choosing or running the CUDA path raises, it says so on stdout and
     returns the organiser's baseline answer from then on (sticky), because the
-    harness's accuracy gate is a hard failure. Nothing is silent.
+    harness's accuracy gate is a hard failure. Nothing is silent;
+  * the library's kernels never hang: a wait that gives up records a device
+    status word instead. After every fused forward a 4-byte copy of that word
+    is queued on a side stream (no synchronisation); the next call reads it
+    and, if a kernel reported a failure, falls back the same way.
 
 Use inside the organiser's harness either by replacing the class body with
 `from submission import UserOptimizedTransformer`, or by assigning
@@ -53,6 +57,9 @@ class UserOptimizedTransformer(BaselineTransformer):
         self._plan: Optional[Plan] = None
         self._source = "uninitialized"
         self._failed = False
+        self._status_host = None    # pinned int32: the device status word, read async
+        self._status_stream = None
+        self._status_event = None
 
     def _select(self, x: torch.Tensor) -> None:
         if self._impl is not None or self._failed:
@@ -85,13 +92,46 @@ class UserOptimizedTransformer(BaselineTransformer):
             print(f"[kf-b200] cannot use the sm_100 path ({type(e).__name__}: {e}); "
                   f"falling back to the reference implementation")
 
+    def _reported_failure(self) -> int:
+        """The library's device status word as of the previous fused forward
+        (0 while its read has not landed yet)."""
+        ev = self._status_event
+        if ev is None or not ev.query():
+            return 0
+        return int(self._status_host[0])
+
+    def _queue_status_read(self, device: torch.device) -> None:
+        from techjam2026_b200 import _lib
+        if self._status_host is None:
+            self._status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+            self._status_stream = torch.cuda.Stream(device=device)
+        self._status_stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(self._status_stream):
+            _lib.check(_lib.lib().kf_device_status_async(self._status_host.data_ptr(),
+                                                         _lib.stream_ptr()),
+                       "kf_device_status_async")
+            ev = torch.cuda.Event()
+            ev.record(self._status_stream)
+        self._status_event = ev
+
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None
                 ) -> torch.Tensor:
         self._select(x)
         if self._impl is None:
             return super().forward(x, valid_token_mask)
+        fused = isinstance(self._impl, FusedTransformer)
+        code = self._reported_failure() if fused else 0
+        if code:
+            self._failed, self._impl = True, None
+            print(f"[kf-b200] the CUDA kernels reported device status {code} (a bounded wait "
+                  f"gave up on this GPU)\n[kf-b200] falling back to the reference "
+                  f"implementation for the rest of this run; results stay correct, speed does not.")
+            return super().forward(x, valid_token_mask)
         try:
-            return self._impl(x, valid_token_mask)
+            out = self._impl(x, valid_token_mask)
+            if fused:
+                self._queue_status_read(x.device)
+            return out
         except Exception as e:
             self._failed, self._impl = True, None
             print(f"[kf-b200] the fused path raised {type(e).__name__}: {e}\n"

@@ -23,6 +23,8 @@ SIGNATURES = {
     "kf_version": (_c_int, []),
     "kf_last_error": (ctypes.c_char_p, []),
     "kf_device_status": (_c_int, [_c_int]),
+    "kf_device_status_async": (_c_int, [_c_ptr, _c_ptr]),
+    "kf_set_wait_limit": (_c_int, [_c_i64]),
     "kf_ln_add_mask": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_ptr,
                                 _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64, _c_float,
                                 _c_int, _c_ptr]),

@@ -31,7 +31,7 @@
 //
 // The fetch counter and a finish counter live in the list's header: the
 // CTA that finishes last zeroes both, so the list built once per forward
-// serves every layer. Every wait is bounded (KF_WAIT_CYCLES); on a timeout
+// serves every layer. Every wait is bounded (wait_limit()); on a timeout
 // the CTA raises its abort flag, drains in-flight copies and products,
 // frees TMEM and records the device status word.
 
@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(192, MINB)
         if (*abort_flag) {
           ok = false;
           break;
-        } else if (clock64() - t_idle > KF_WAIT_CYCLES) {
+        } else if (clock64() - t_idle > wait_limit()) {
           *abort_flag = 1;
           record_device_status(KF_DEV_WAIT_TIMEOUT_TMA);
           ok = false;

@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(192, MINB)
         if (*abort_flag) {
           ok = false;
           break;
-        } else if (clock64() - t_idle > KF_WAIT_CYCLES) {
+        } else if (clock64() - t_idle > wait_limit()) {
           *abort_flag = 1;
           record_device_status(KF_DEV_WAIT_TIMEOUT_TMA);
           ok = false;

@@ -943,7 +943,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
             int got = 1;
             const long long t0 = clock64();
             while (*fl < sk_np) {
-              if (*abort_flag || clock64() - t0 > KF_WAIT_CYCLES) {
+              if (*abort_flag || clock64() - t0 > wait_limit()) {
                 *abort_flag = 1;
                 record_device_status(KF_DEV_WAIT_TIMEOUT_EPI);
                 got = 0;

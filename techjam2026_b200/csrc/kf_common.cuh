@@ -4,7 +4,8 @@
 // (mbarrier, cp.async.bulk.tensor, tcgen05.*) plus the two descriptor formats
 // the 5th-generation tensor core reads (shared-memory matrix descriptor and
 // instruction descriptor). No waits are unbounded: every spin on an mbarrier
-// gives up after KF_WAIT_CYCLES, raises a CTA-wide abort flag and records a
+// gives up after the device's wait limit (KF_WAIT_CYCLES, ~2 s, unless
+// kf_set_wait_limit changed it), raises a CTA-wide abort flag and records a
 // device status word that the host can read back (kf_device_status()).
 #pragma once
 
@@ -40,6 +41,17 @@ enum : int {
   KF_DEV_WAIT_TIMEOUT_SOFTMAX = 4,
   KF_DEV_BAD_BATCH_ORDER = 5,  // a batch_order entry outside [0, B)
 };
+
+// Time limit of every bounded wait on work (mbarrier phases, the producer's
+// idle time, the stream-K part counters), in SM cycles: KF_WAIT_CYCLES
+// unless kf_set_wait_limit changed it for this device. The waits used while
+// unwinding after an abort (mbar_wait_drain) keep the fixed KF_WAIT_CYCLES,
+// so in-flight copies and products always land before a CTA leaves.
+__device__ long long g_wait_cycles = KF_WAIT_CYCLES;
+
+__device__ __forceinline__ long long wait_limit() {
+  return *static_cast<volatile long long*>(&g_wait_cycles);
+}
 
 __device__ __forceinline__ void record_device_status(int code) {
   atomicCAS(&g_device_status, 0, code);
@@ -144,7 +156,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     // flag and the time limit.
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > KF_WAIT_CYCLES) {
+    if (clock64() - t0 > wait_limit()) {
       *abort_flag = 1;
       record_device_status(who);
       return false;
@@ -214,7 +226,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   while (true) {
     if (mbar_try_wait_cluster(bar, parity, 20000u)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > KF_WAIT_CYCLES) {
+    if (clock64() - t0 > wait_limit()) {
       *abort_flag = 1;
       record_device_status(who);
       return false;

@@ -372,6 +372,22 @@ extern "C" int kf_device_status(int reset) {
   return v;
 }
 
+extern "C" int kf_device_status_async(int32_t* host_dst, void* stream) {
+  if (!host_dst) {
+    set_last_error("kf_device_status_async: host_dst is null");
+    return KF_E_INVALID;
+  }
+  return cuda_status(cudaMemcpyFromSymbolAsync(host_dst, g_device_status, sizeof(int), 0,
+                                               cudaMemcpyDeviceToHost,
+                                               static_cast<cudaStream_t>(stream)),
+                     "kf_device_status_async");
+}
+
+extern "C" int kf_set_wait_limit(int64_t cycles) {
+  const long long v = cycles > 0 ? static_cast<long long>(cycles) : KF_WAIT_CYCLES;
+  return cuda_status(cudaMemcpyToSymbol(g_wait_cycles, &v, sizeof(v)), "kf_set_wait_limit");
+}
+
 extern "C" size_t kf_keep_bits_words(int64_t B, int64_t S) {
   if (B <= 0 || S <= 0) return 0;
   return static_cast<size_t>(B) * static_cast<size_t>((S + 31) / 32);

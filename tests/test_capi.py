@@ -140,3 +140,9 @@ def test_persistent_attention_entries_reject_before_any_launch():
     assert b"sched is null" in lib.kf_last_error()
     assert lib.kf_flash_fwd_tf32_sched(*args, fake, 1, 1, 8, 48, 48, 0.125, 0, None) == \
         _lib.KF_E_UNSUPPORTED
+
+
+def test_status_entries_reject_a_null_destination():
+    lib = _lib.lib()
+    assert lib.kf_device_status_async(None, None) == _lib.KF_E_INVALID
+    assert b"null" in lib.kf_last_error()
