@@ -199,9 +199,11 @@ def run_reference(args, rank, world):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded generate_random_case draws, Xavier weights)",
-        "config": {"workload": w.name, "signature": sig(w.cfg)},
+        "config": {"workload": w.name, "signature": sig(w.cfg),
+                   "global_batch": w.cfg.batch_size, "seq_len": w.cfg.seq_len,
+                   "parallelism": "one CPU process (host cores); GPUs unused"},
         "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads,
-                         "kind": "port", "sample": descs[-1]},
+                         "kind": "port", "sample": descs[-1], "cpu_model": cpu_model()},
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
