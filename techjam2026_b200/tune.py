@@ -1,8 +1,10 @@
 """Populate the sm_100 dispatch table by measurement (gate, then time).
 
-    python -m techjam2026_b200.tune --config c4 [--write]
+    python -m techjam2026_b200.tune --config c4 [--shards 8] [--write]
 
-For one BASELINE configuration, on the current GPU:
+For one BASELINE configuration -- or, with --shards N, the share of its
+batch that one rank runs when the batch is split over N GPUs
+(sharding.BatchShard, rank 0) -- on the current GPU:
 
 1. Build the forward with the table's current plan for that shape and keep
    its output on a seeded input as the reference.
@@ -11,7 +13,9 @@ For one BASELINE configuration, on the current GPU:
    forward with only that choice changed. The gate: its output must be
    bit-identical to the reference (a tile only decides which CTA computes an
    output element, never the order of its accumulation), so a candidate
-   that changes any bit is rejected as a bug.
+   that changes any bit is rejected as a bug. The attention kernel (one CTA
+   per query tile, or the persistent kernel over a work list) is a candidate
+   of the same kind: the forward's output is bit-identical either way.
 3. Time every surviving candidate as a CUDA-graph replay (median of
    `--repeats`, L2 flushed before each), keep the fastest tile per GEMM, and
    confirm the combined plan against the reference and the current plan.
@@ -83,14 +87,20 @@ def _time(model: FusedTransformer, x, mask, repeats: int, flush: torch.Tensor) -
     return statistics.median(times)
 
 
-def tune(name: str, repeats: int = 10, seed: int = 0, log=print) -> Dict:
+def tune(name: str, repeats: int = 10, seed: int = 0, log=print, shards: int = 1) -> Dict:
     w = WORKLOADS[name]
     cfg = w.cfg
+    x_cpu, m_cpu = generate_case(cfg, seed, w.padding_ratio, w.input_scale)
+    if shards > 1:
+        from .sharding import BatchShard
+        shard = BatchShard(m_cpu.sum(1).tolist(), shards, 0, cfg.d_model, cfg.ffn_dim,
+                           cfg.causal)
+        x_cpu, m_cpu = shard.take(x_cpu), shard.take(m_cpu)
+        cfg = dataclasses.replace(cfg, batch_size=shard.local_batch)
     spec = probe()
     table = DispatchTable.load_for(spec)
     base, source = table.lookup(spec.arch, torch.float32, cfg)
     sd = make_state_dict(cfg, seed)
-    x_cpu, m_cpu = generate_case(cfg, seed, w.padding_ratio, w.input_scale)
     dev = torch.device("cuda", torch.cuda.current_device())
     x, mask = x_cpu.to(dev), m_cpu.to(dev)
     flush = torch.empty(64 * 1024 * 1024, device=dev)
@@ -127,12 +137,31 @@ def tune(name: str, repeats: int = 10, seed: int = 0, log=print) -> Dict:
             best[field], best[pfield] = bn_best, pair_best
         else:
             best[field], best[pfield] = getattr(base, field), getattr(base, pfield)
+    # The attention kernel, with the GEMM tiles chosen above.
+    timed = []
+    for persistent in (False, True):
+        cand = dataclasses.replace(base, **best, attn_persistent=persistent)
+        model, out = _forward(cfg, sd, cand, x, mask)
+        exact = torch.equal(out, ref)
+        t = _time(model, x, mask, repeats, flush) if exact else float("inf")
+        model.release_buffers()
+        del model, out
+        gc.collect()
+        torch.cuda.empty_cache()
+        results.append({"gemm": "attention", "persistent": persistent, "ms": t,
+                        "bit_exact": exact})
+        log(f"  attention {'persistent' if persistent else 'one CTA per query tile'}: "
+            f"{'%.3f ms' % t if exact else 'REJECTED (output differs)'}")
+        if exact:
+            timed.append((t, persistent))
+    best["attn_persistent"] = min(timed)[1] if timed else base.attn_persistent
     tuned = dataclasses.replace(base, **best)
     model, out = _forward(cfg, sd, tuned, x, mask)
     exact = torch.equal(out, ref)
     t_tuned = _time(model, x, mask, repeats, flush) if exact else float("inf")
     log(f"  combined {tuned.describe()}: {t_tuned:.3f} ms, bit-exact {exact}")
-    return {"config": name, "signature": signature(cfg), "base_ms": t_base,
+    label = name if shards == 1 else f"{name}, one rank's rows of {shards} (cost-balanced shard)"
+    return {"config": name, "label": label, "signature": signature(cfg), "base_ms": t_base,
             "tuned_ms": t_tuned, "bit_exact": exact, "plan": tuned, "base": base,
             "candidates": results}
 
@@ -150,7 +179,8 @@ def write_entry(result: Dict, arch: str = "sm_100") -> str:
             e.note = f"{keep}; {note}"
             break
     else:
-        table.entries.append(Entry(sig, "float32", "sm_100", tuned, note))
+        table.entries.append(Entry(sig, "float32", "sm_100", tuned,
+                                   f"{result.get('label', result.get('config', sig))}; {note}"))
     return table.save(arch)
 
 
@@ -158,14 +188,21 @@ def main(argv=None) -> int:
     p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     p.add_argument("--config", action="append", choices=sorted(WORKLOADS), required=True)
     p.add_argument("--repeats", type=int, default=10)
+    p.add_argument("--shards", type=int, action="append", default=None,
+                   help="tune the shard one rank runs when the batch is split over N GPUs")
     p.add_argument("--write", action="store_true", help="store faster plans in the table")
     args = p.parse_args(argv)
     for name in args.config:
-        r = tune(name, args.repeats)
-        if args.write and r["bit_exact"] and r["tuned_ms"] < r["base_ms"]:
-            print(f"  written to {write_entry(r)}")
-        print(json.dumps({k: (dataclasses.asdict(v) if isinstance(v, Plan) else v)
-                          for k, v in r.items() if k != "candidates"}))
+        for shards in (args.shards or [1]):
+            r = tune(name, args.repeats, shards=shards)
+            # Written when faster; a shard shape's measured plan is also written
+            # when it is the plan the table would give it anyway.
+            same = r["plan"] == r["base"]
+            if args.write and r["bit_exact"] and (r["tuned_ms"] < r["base_ms"]
+                                                  or (shards > 1 and same)):
+                print(f"  written to {write_entry(r)}")
+            print(json.dumps({k: (dataclasses.asdict(v) if isinstance(v, Plan) else v)
+                              for k, v in r.items() if k != "candidates"}))
     return 0
 
 
