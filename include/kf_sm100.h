@@ -126,9 +126,6 @@ int kf_gemm_tf32(const float* A, int64_t lda, const float* W, int64_t ldw, const
                  const int32_t* live_count, void* stream);
 
 #define KF_GEMM_OUT_BF16X2 8 /* kf_gemm_bf16x3: write C as bf16 hi/lo planes */
-#define KF_GEMM_K32 16       /* kf_gemm_bf16x3: stream k blocks of 32 instead of 64
-                                (twice as many half-size stages in flight; same
-                                MMA order, so C is bit-identical) */
 #define KF_GEMM_W_STATIC 64  /* kf_gemm_bf16x3: W was written before the kernel that
                                 precedes this call in the stream started (weights
                                 prepared once), so the first W tiles may be loaded
@@ -161,7 +158,7 @@ int kf_gemm_bf16x3(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t 
  * K loop. A tile split between CTAs is finished by the CTA holding its first
  * k blocks, which adds the other parts (fp32, in a fixed order: results are
  * deterministic, not bit-identical to kf_gemm_bf16x3). `bn` 64, 128 or 256
- * (0 = 128), no KF_GEMM_PAIR / KF_GEMM_K32. `workspace`: at least
+ * (0 = 128), no KF_GEMM_PAIR. `workspace`: at least
  * kf_gemm_sk_workspace_bytes(M, N, bn) bytes, 16-byte aligned, ZEROED before
  * its first use (the kernel leaves its counters zero again); partials go at
  * its start and the per-tile counters at its end, so GEMMs of several shapes
@@ -174,26 +171,6 @@ int kf_gemm_bf16x3_sk(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64
                       const int32_t* live_tiles, const int32_t* live_count, void* workspace,
                       int64_t workspace_bytes, void* stream);
 int64_t kf_gemm_sk_workspace_bytes(int64_t M, int64_t N, int bn);
-
-/* kf_gemm_bf16x3 (bias epilogue) followed by kf_ln_add_mask in one kernel:
- * y = A.W^T + bias stays on chip; s = keep ? res + y : 0 is written to s_out
- * (may equal res, or be null) and h = LayerNorm(s) * gamma + beta to h_out,
- * with kf_ln_add_mask's ln_flags (KF_LN_*: mask_out, TF32 rounding, skipping
- * padded rows, bf16 hi/lo planes [2][M][ldh]). s is bit-identical to the
- * two-kernel sequence; h differs only by the order of the row reductions.
- * N (= the LayerNorm width) must be a multiple of 128 and at most 1024: a
- * cluster of N/128 CTAs computes the N/128 column tiles of a row tile and
- * exchanges the row sums through distributed shared memory. Needs the
- * alignments of kf_gemm_bf16x3 and 16-byte aligned res, s_out, gamma, beta,
- * h_out. Replaces the out_proj / FFN2 F.linear plus the next
- * add_mask_layernorm (kernelforge/optimized.py:573-574, 441-446 with
- * :460-476; kernelforge/ops/layernorm.py:101-156). */
-int kf_gemm_bf16x3_add_ln(const uint16_t* A2, int64_t lda, const uint16_t* W2, int64_t ldw,
-                          const float* bias, const float* res, int64_t ldr, const uint8_t* keep,
-                          const float* gamma, const float* beta, float eps, float* s_out,
-                          int64_t lds, void* h_out, int64_t ldh, int64_t M, int64_t N, int64_t K,
-                          int ln_flags, const int32_t* live_tiles, const int32_t* live_count,
-                          void* stream);
 
 /* ----------------------------------------------------------- attention */
 

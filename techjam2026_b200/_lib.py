@@ -39,10 +39,6 @@ SIGNATURES = {
                                    _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int,
                                    _c_int, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_ptr]),
     "kf_gemm_sk_workspace_bytes": (_c_i64, [_c_i64, _c_i64, _c_int]),
-    "kf_gemm_bf16x3_add_ln": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
-                                       _c_ptr, _c_ptr, _c_ptr, _c_float, _c_ptr, _c_i64,
-                                       _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
-                                       _c_ptr, _c_ptr, _c_ptr]),
     "kf_split_bf16x2": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_i64, _c_ptr]),
     "kf_keep_bits_words": (ctypes.c_size_t, [_c_i64, _c_i64]),
     "kf_keep_bits": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_i64, _c_ptr, _c_ptr]),
@@ -100,7 +96,6 @@ KF_ATTN_ROUND_TF32 = 4
 KF_ATTN_OUT_BF16X2 = 8
 KF_ATTN_EMPTY_Q_UNTOUCHED = 16
 KF_GEMM_OUT_BF16X2 = 8
-KF_GEMM_K32 = 16
 KF_GEMM_PAIR = 32
 KF_GEMM_W_STATIC = 64
 KF_NOALLOC_KEEP_WORDS_MAX = 262144

@@ -43,15 +43,11 @@ namespace kf {
 enum : int { KF_GEMM_VEC_OK = 1 << 8, KF_GEMM_TMA_OUT = 1 << 9, KF_GEMM_OUT_SPLIT = 1 << 10 };
 // SPLIT_BF16X3_PRE: operands arrive already split into bf16 hi/lo planes
 // (kf_gemm_bf16x3); TMA loads the four planes, no converter warps.
-// SPLIT_BF16X3_PRE32: the same with 32-wide k blocks (64-byte rows, 64-byte
-// swizzle): stages of half the size, so twice as many are in flight in the
-// same shared memory. The MMAs run in the same order, so C is bit-identical.
 enum : int {
   SPLIT_NONE = 0,
   SPLIT_TF32X3 = 1,
   SPLIT_BF16X3 = 2,
-  SPLIT_BF16X3_PRE = 3,
-  SPLIT_BF16X3_PRE32 = 4
+  SPLIT_BF16X3_PRE = 3
 };
 
 // PAIR: cta_group::2 tiles of 256 x BN computed by a cluster of two CTAs;
@@ -61,10 +57,10 @@ template <int BN, int SPLIT, bool PAIR = false>
 struct GemmCfg {
   static constexpr int BM = 128;
   // One swizzle row per k block and plane: 128 bytes (32 fp32 or, pre-split,
-  // 64 bf16), or 64 bytes (32 bf16) for SPLIT_BF16X3_PRE32.
-  static constexpr int ROW_BYTES = SPLIT == SPLIT_BF16X3_PRE32 ? 64 : 128;
+  // 64 bf16).
+  static constexpr int ROW_BYTES = 128;
   static constexpr int BK = SPLIT == SPLIT_BF16X3_PRE ? 64 : 32;
-  static constexpr bool PRESPLIT = SPLIT == SPLIT_BF16X3_PRE || SPLIT == SPLIT_BF16X3_PRE32;
+  static constexpr bool PRESPLIT = SPLIT == SPLIT_BF16X3_PRE;
   static constexpr int A_BYTES = BM * ROW_BYTES;  // one plane
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B rows staged by this CTA
   static constexpr int B_BYTES = B_ROWS * ROW_BYTES;
@@ -261,24 +257,6 @@ __device__ __forceinline__ void gemm_store_chunk(const float (&v)[32], float* __
   }
 }
 
-// Arguments of the residual-add + mask + LayerNorm epilogue (LNF kernels):
-// the GEMM output y never reaches memory; s = keep ? res + y : 0 and
-// h = LayerNorm(s) (gamma, beta, eps) are written as kf_ln_add_mask writes
-// them (flags KF_LN_*).
-struct LnArgs {
-  const float* res;
-  int64_t ldr;
-  const uint8_t* keep;
-  const float* gamma;
-  const float* beta;
-  float* s_out;
-  int64_t lds;
-  void* h_out;
-  int64_t ldh;
-  float eps;
-  int flags;
-};
-
 // Stream-K workspace (SK kernels): fp32 partial accumulators of tiles split
 // between CTAs, [tiles][2 parts][128 rows][BN], and per (tile, epilogue half)
 // arrival counters, zero between launches.
@@ -287,17 +265,16 @@ struct SkArgs {
   int* flags;
 };
 
-template <int BN, int EPI, int SPLIT, bool LNF = false, bool PAIR = false, bool SK = false>
+template <int BN, int EPI, int SPLIT, bool PAIR = false, bool SK = false>
 __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, float* __restrict__ C, int64_t ldc, const float* __restrict__ bias, int M,
                      int N, int K, int flags, int head_dim, int head_stride,
                      const int32_t* __restrict__ live_tiles, const int32_t* __restrict__ live_count,
-                     const __grid_constant__ LnArgs ln, const __grid_constant__ SkArgs sk) {
+                     const __grid_constant__ SkArgs sk) {
   using Cfg = GemmCfg<BN, SPLIT, PAIR>;
   constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
-  static_assert(!(LNF && PAIR), "pair kernels have the plain epilogues");
-  static_assert(!SK || (SPLIT == SPLIT_BF16X3_PRE && !PAIR && !LNF), "stream-K shape");
+  static_assert(!SK || (SPLIT == SPLIT_BF16X3_PRE && !PAIR), "stream-K shape");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -307,14 +284,9 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   uint64_t* acc_full = conv + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  // LNF: cluster exchanges of row statistics, [sum | centred sum of squares]
-  // x [tile parity]; other kernels keep the old barrier layout.
-  uint64_t* xbar = drain + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(LNF ? xbar + 4 : drain + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* epi_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [2], per half
-  static_assert(!LNF || (3 * STAGES + 9) * 8 + 16 <= Cfg::BAR_BYTES, "LN barriers");
-  static_assert(!LNF || (BN == 128 && SPLIT == 3 && EPI == KF_EPI_BIAS), "LN epilogue shape");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -335,8 +307,6 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
       mbar_init(&acc_empty[a], PAIR ? 2 * Cfg::EPI_WARPS : Cfg::EPI_WARPS);
     }
     mbar_init(drain, 1);
-    if (LNF)
-      for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 128 * num_n);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -356,10 +326,10 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // LNF / PAIR: every CTA of the cluster has initialised its barriers (and
-  // holds its TMEM) before any CTA signals them remotely (warp-aligned:
+  // PAIR: both CTAs of the pair have initialised their barriers (and hold
+  // their TMEM) before either signals the other's remotely (warp-aligned:
   // reconverge first).
-  if (LNF || PAIR) {
+  if (PAIR) {
     __syncwarp();
     cluster_sync_all();
   }
@@ -374,7 +344,7 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   // previous kernel's tail. Their barriers expect those bytes now and the A
   // bytes and the arrival later (the phase cannot end in between).
   int pre_w = 0;
-  if constexpr (Cfg::PRESPLIT && !PAIR && !LNF && !SK) {
+  if constexpr (Cfg::PRESPLIT && !PAIR && !SK) {
     if ((flags & KF_GEMM_W_STATIC) && warp == 0 && lane == 0) {
       const int nw0 = (static_cast<int>(blockIdx.x) % num_n) * BN;
       pre_w = num_kb < STAGES ? num_kb : STAGES;
@@ -593,18 +563,6 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
               mma_bf16_ss(d_tmem, ah, bl, idesc_bf, 1u);
               mma_bf16_ss(d_tmem, ah, bh, idesc_bf, 1u);
             }
-          } else if (SPLIT == SPLIT_BF16X3_PRE32) {
-            // TMA-loaded bf16 planes, 64-byte rows (SW64): 2 k steps of 16.
-#pragma unroll
-            for (int k = 0; k < BK / 16; ++k) {
-              const uint64_t ah = make_smem_desc(a_addr + k * 32, 16, 512, KF_SWIZZLE_64B);
-              const uint64_t bh = make_smem_desc(b_addr + k * 32, 16, 512, KF_SWIZZLE_64B);
-              const uint64_t al = make_smem_desc(alo_addr + k * 32, 16, 512, KF_SWIZZLE_64B);
-              const uint64_t bl = make_smem_desc(blo_addr + k * 32, 16, 512, KF_SWIZZLE_64B);
-              mma_bf16_ss(d_tmem, al, bh, idesc_bf, (kb != kb_b || k != 0) ? 1u : 0u);
-              mma_bf16_ss(d_tmem, ah, bl, idesc_bf, 1u);
-              mma_bf16_ss(d_tmem, ah, bh, idesc_bf, 1u);
-            }
           } else if (SPLIT == SPLIT_BF16X3) {
             // bf16 tiles: A_hi | A_lo | B_hi | B_lo, 64-byte rows (SW64).
             const uint32_t ahi = alo_addr, alo = ahi + Cfg::A_BYTES / 2;
@@ -714,171 +672,6 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
           stage = 0;
           phase ^= 1u;
         }
-      }
-    }
-  } else if constexpr (LNF) {
-    // ------------------------------ epilogue: residual add + mask + LayerNorm
-    // The cluster's num_n CTAs hold the num_n 128-column tiles of the same
-    // 128 rows. Thread r of each half owns row r of its tile: pass 1 forms
-    // s = keep ? res + (acc + bias) : 0 (y rounded exactly as the GEMM would
-    // store it), writes s back over the accumulator and sums its 64 columns;
-    // the two halves and then the cluster's CTAs (through distributed shared
-    // memory) complete the row sum; pass 2 the centred sum of squares; pass 3
-    // writes s and h. Summation order is fixed, so results are deterministic.
-    const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int r = quarter * 32 + lane;
-    const bool leader = threadIdx.x == 64;
-    const int csize = num_n;
-    const uint32_t rank = static_cast<uint32_t>(blockIdx.x % csize);
-    float* xs = reinterpret_cast<float*>(smem + Cfg::EPI_OFF);  // [2 kinds][2 parities][8][128]
-    float* red = xs + 2 * 2 * 8 * 128;                          // [2 halves][128]
-    const float inv_n = 1.f / static_cast<float>(N);
-    const bool split_h = (ln.flags & KF_LN_OUT_BF16X2) != 0;
-    const bool rnd_h = (ln.flags & KF_LN_ROUND_TF32) != 0;
-    const bool skip_padded = (ln.flags & KF_LN_SKIP_PADDED) != 0;
-    const bool mask_out = (ln.flags & KF_LN_MASK_OUT) != 0;
-    // One bounded wait by the leader, shared through named barrier 1 (all 256
-    // epilogue threads), so every thread takes the same exits.
-    auto shared_wait = [&](uint64_t* bar, uint32_t parity, bool cluster_scope) -> bool {
-      if (leader)
-        epi_ok[0] = (cluster_scope ? mbar_wait_cluster(bar, parity, abort_flag, KF_DEV_WAIT_TIMEOUT_EPI)
-                                   : mbar_wait(bar, parity, abort_flag, KF_DEV_WAIT_TIMEOUT_EPI))
-                        ? 1 : 0;
-      named_bar_sync(1, 256);
-      const bool ok = epi_ok[0] != 0;
-      // completed phase: this re-test returns at once and acquires for this thread
-      if (ok && cluster_scope) mbar_try_wait_cluster(bar, parity, 0u);
-      return ok;
-    };
-    // Exchange one value per row with every CTA of the cluster; returns the
-    // sum over the cluster's CTAs in rank order.
-    auto exchange = [&](int kind, int tc, float part, bool& ok) -> float {
-      const int buf = tc & 1;
-      float* x = xs + (kind * 2 + buf) * 8 * 128;
-      uint64_t* bar = &xbar[kind * 2 + buf];
-      if (half == 0) {
-        const uint32_t slot = smem_u32(x + rank * 128 + r);
-        const uint32_t b = smem_u32(bar);
-        for (int q = 0; q < csize; ++q) {
-          st_cluster_f32(mapa_shared(slot, static_cast<uint32_t>(q)), part);
-          mbar_arrive_cluster(mapa_shared(b, static_cast<uint32_t>(q)));
-        }
-      }
-      ok = shared_wait(bar, static_cast<uint32_t>((tc >> 1) & 1), true);
-      float tot = 0.f;
-      if (ok)
-        for (int q = 0; q < csize; ++q) tot += x[q * 128 + r];
-      return tot;
-    };
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    int tc = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tc) {
-      const int m0 = row0(tile);
-      const int n0 = (tile % num_n) * BN;
-      if (!shared_wait(&acc_full[acc], acc_phase, false)) break;
-      tc_fence_after();
-      const int row = m0 + r;
-      const bool in_range = row < M;
-      const bool kept = in_range && (ln.keep ? (__ldg(ln.keep + row) != 0) : true);
-      const uint32_t tbase =
-          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      // pass 1
-      float part = 0.f;
-#pragma unroll 1
-      for (int c = 32 * half; c < BN; c += 64) {
-        float v[32];
-        tmem_ld32(tbase + static_cast<uint32_t>(c), v);
-        const float* xrow = ln.res + static_cast<int64_t>(row) * ln.ldr + n0 + c;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (bias) bb = __ldg(reinterpret_cast<const float4*>(bias + n0 + c) + j);
-          float4 xx = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (kept) xx = *reinterpret_cast<const float4*>(xrow + 4 * j);
-          const float y0 = v[4 * j] + bb.x, y1 = v[4 * j + 1] + bb.y;
-          const float y2 = v[4 * j + 2] + bb.z, y3 = v[4 * j + 3] + bb.w;
-          v[4 * j] = kept ? xx.x + y0 : 0.f;
-          v[4 * j + 1] = kept ? xx.y + y1 : 0.f;
-          v[4 * j + 2] = kept ? xx.z + y2 : 0.f;
-          v[4 * j + 3] = kept ? xx.w + y3 : 0.f;
-          part += (v[4 * j] + v[4 * j + 1]) + (v[4 * j + 2] + v[4 * j + 3]);
-        }
-        tmem_st32(tbase + static_cast<uint32_t>(c), v);
-      }
-      red[half * 128 + r] = part;
-      named_bar_sync(1, 256);
-      bool ok = true;
-      const float mean = exchange(0, tc, red[r] + red[128 + r], ok) * inv_n;
-      if (!ok) break;
-      // pass 2 (every thread has read red: the exchange's barrier is behind it)
-      float sq = 0.f;
-#pragma unroll 1
-      for (int c = 32 * half; c < BN; c += 64) {
-        float v[32];
-        tmem_ld32(tbase + static_cast<uint32_t>(c), v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float a = v[4 * j] - mean, b = v[4 * j + 1] - mean;
-          const float cc = v[4 * j + 2] - mean, dd = v[4 * j + 3] - mean;
-          sq += (a * a + b * b) + (cc * cc + dd * dd);
-        }
-      }
-      red[half * 128 + r] = sq;
-      named_bar_sync(1, 256);
-      const float var = exchange(1, tc, red[r] + red[128 + r], ok) * inv_n;
-      if (!ok) break;
-      const float rstd = 1.f / sqrtf(var + ln.eps);
-      // pass 3 (tcgen05.ld is warp-aligned: every lane loads, only the
-      // stores depend on the row)
-      {
-        const bool write_row = in_range && (kept || !skip_padded);
-        const bool zero_h = mask_out && !kept;
-        uint16_t* h_hi = reinterpret_cast<uint16_t*>(ln.h_out) + static_cast<int64_t>(row) * ln.ldh;
-        uint16_t* h_lo = h_hi + static_cast<int64_t>(M) * ln.ldh;
-        float* h_f = reinterpret_cast<float*>(ln.h_out) + static_cast<int64_t>(row) * ln.ldh;
-#pragma unroll 1
-        for (int c = 32 * half; c < BN; c += 64) {
-          float v[32];
-          tmem_ld32(tbase + static_cast<uint32_t>(c), v);
-          const int col0 = n0 + c;
-          if (!write_row) continue;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int col = col0 + 4 * j;
-            const float4 sv = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            if (ln.s_out)
-              *reinterpret_cast<float4*>(ln.s_out + static_cast<int64_t>(row) * ln.lds + col) = sv;
-            float4 hv = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (!zero_h) {
-              const float4 ww = __ldg(reinterpret_cast<const float4*>(ln.gamma + col));
-              const float4 bb = __ldg(reinterpret_cast<const float4*>(ln.beta + col));
-              hv.x = (sv.x - mean) * rstd * ww.x + bb.x;
-              hv.y = (sv.y - mean) * rstd * ww.y + bb.y;
-              hv.z = (sv.z - mean) * rstd * ww.z + bb.z;
-              hv.w = (sv.w - mean) * rstd * ww.w + bb.w;
-              if (rnd_h) {
-                hv.x = round_tf32(hv.x);
-                hv.y = round_tf32(hv.y);
-                hv.z = round_tf32(hv.z);
-                hv.w = round_tf32(hv.w);
-              }
-            }
-            if (split_h)
-              store_split4(h_hi + col, h_lo + col, hv);
-            else
-              *reinterpret_cast<float4*>(h_f + col) = hv;
-          }
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
-      named_bar_sync(1, 256);  // epi_ok and red are rewritten for the next tile
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1u;
       }
     }
   } else {
@@ -1115,9 +908,9 @@ __global__ void __launch_bounds__((SPLIT == 1 || SPLIT == 2) ? 576 : 320, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // LNF / PAIR: no CTA leaves while a peer may still write into its shared
-  // memory or arrive on its barriers; PAIR frees TMEM as a pair.
-  if (LNF || PAIR) {
+  // PAIR: no CTA leaves while its peer may still write into its shared
+  // memory or arrive on its barriers; the pair frees TMEM together.
+  if (PAIR) {
     __syncwarp();
     cluster_sync_all();
   }
@@ -1150,7 +943,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   const int grid = tiles < sm_count() ? tiles : sm_count();
   return cuda_status(launch_chained(kern, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM_BYTES, st, ta,
                                     tb, tc, C, ldc, bias, M, N, K, flags, hd, hs, live_tiles,
-                                    live_count, LnArgs{}, SkArgs{}),
+                                    live_count, SkArgs{}),
                      "kf_gemm_tf32 launch");
 }
 
@@ -1162,7 +955,7 @@ static int launch_gemm_sk(const CUtensorMap& ta, const CUtensorMap& tb, const CU
                           int hd, int hs, const int32_t* live_tiles, const int32_t* live_count,
                           const SkArgs& sk, cudaStream_t st) {
   using Cfg = GemmCfg<BN, SPLIT_BF16X3_PRE>;
-  auto kern = gemm_tf32_kernel<BN, EPI, SPLIT_BF16X3_PRE, false, false, true>;
+  auto kern = gemm_tf32_kernel<BN, EPI, SPLIT_BF16X3_PRE, false, true>;
   static DeviceOnce once;
   const int rc_attr = once.run("kf_gemm_bf16x3_sk", nullptr, [&](int) {
     return cuda_status(
@@ -1172,8 +965,7 @@ static int launch_gemm_sk(const CUtensorMap& ta, const CUtensorMap& tb, const CU
   if (rc_attr) return rc_attr;
   return cuda_status(launch_chained(kern, dim3(static_cast<unsigned>(sm_count())),
                                     dim3(Cfg::THREADS), Cfg::SMEM_BYTES, st, ta, tb, tc, C, ldc,
-                                    bias, M, N, K, flags, hd, hs, live_tiles, live_count, LnArgs{},
-                                    sk),
+                                    bias, M, N, K, flags, hd, hs, live_tiles, live_count, sk),
                      "kf_gemm_bf16x3_sk launch");
 }
 
@@ -1185,7 +977,7 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
                             int flags, int hd, int hs, const int32_t* live_tiles,
                             const int32_t* live_count, cudaStream_t st) {
   using Cfg = GemmCfg<BN, SPLIT_BF16X3_PRE, true>;
-  auto kern = gemm_tf32_kernel<BN, EPI, SPLIT_BF16X3_PRE, false, true>;
+  auto kern = gemm_tf32_kernel<BN, EPI, SPLIT_BF16X3_PRE, true>;
   static DeviceOnce once;
   static int max_pairs[KF_MAX_DEVICES] = {0};
   int dev = 0;
@@ -1220,63 +1012,10 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
   return cuda_status(
       launch_chained_cluster(kern, dim3(static_cast<unsigned>(2 * pairs)), dim3(Cfg::THREADS),
                              Cfg::SMEM_BYTES, st, 2u, ta, tb, tc, C, ldc, bias, M, N, K, flags, hd,
-                             hs, live_tiles, live_count, LnArgs{}, SkArgs{}),
+                             hs, live_tiles, live_count, SkArgs{}),
       "kf_gemm_bf16x3 (pair) launch");
 }
 
-// The LayerNorm-fused GEMM: clusters of N/128 CTAs, one row tile per cluster
-// at a time, as many clusters as can be resident at once.
-static int launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tb, const float* bias,
-                          int M, int N, int K, const LnArgs& ln, const int32_t* live_tiles,
-                          const int32_t* live_count, cudaStream_t st) {
-  using Cfg = GemmCfg<128, 3>;
-  auto kern = gemm_tf32_kernel<128, KF_EPI_BIAS, 3, true>;
-  static DeviceOnce once;
-  static int max_clusters[KF_MAX_DEVICES][9] = {{0}};
-  int dev = 0;
-  const int rc_attr = once.run("kf_gemm_bf16x3_add_ln", &dev, [&](int d) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return cuda_status(e, "kf_gemm_bf16x3_add_ln: set attributes");
-    // Resident clusters for every cluster size the entry accepts (N/128 = 1..8).
-    for (int cs = 1; cs <= 8; ++cs) {
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(static_cast<unsigned>(cs * 8));
-      cfg.blockDim = dim3(Cfg::THREADS);
-      cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = static_cast<unsigned>(cs);
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-        cudaGetLastError();
-        n = sm_count() / cs;
-      }
-      max_clusters[d][cs] = n > 0 ? n : 1;
-    }
-    return static_cast<int>(KF_OK);
-  });
-  if (rc_attr) return rc_attr;
-  const int csize = N / 128;
-  const int row_tiles = (M + Cfg::BM - 1) / Cfg::BM;
-  const int clusters = row_tiles < max_clusters[dev][csize] ? row_tiles : max_clusters[dev][csize];
-  CUtensorMap tc;
-  memset(&tc, 0, sizeof(tc));
-  return cuda_status(
-      launch_chained_cluster(kern, dim3(static_cast<unsigned>(clusters * csize)),
-                             dim3(Cfg::THREADS), Cfg::SMEM_BYTES, st,
-                             static_cast<unsigned>(csize), ta, tb, tc, static_cast<float*>(nullptr),
-                             static_cast<int64_t>(0), bias, M, N, K, 0, 0, 0, live_tiles,
-                             live_count, ln, SkArgs{}),
-      "kf_gemm_bf16x3_add_ln launch");
-}
-
-// Pick the N tile that minimises (waves x per-tile cost) on this GPU.
 static int choose_bn(int64_t M, int64_t N) {
   const int sms = sm_count();
   const int64_t mt = (M + 127) / 128;
@@ -1434,6 +1173,11 @@ static int gemm_bf16x3_impl(const uint16_t* A2, int64_t lda, const uint16_t* W2,
     set_last_error("kf_gemm_bf16x3: invalid arguments");
     return KF_E_INVALID;
   }
+  if (flags & ~(KF_GEMM_ROUND_TF32 | KF_GEMM_BF16X3 | KF_GEMM_OUT_BF16X2 | KF_GEMM_PAIR |
+                KF_GEMM_W_STATIC)) {
+    set_last_error("kf_gemm_bf16x3: unknown flags 0x%x", flags);
+    return KF_E_INVALID;
+  }
   if (M == 0 || N == 0) return KF_OK;
   const bool out_split = (flags & KF_GEMM_OUT_BF16X2) != 0;
   if (K == 0 || K % 8 || lda % 8 || ldw % 8 || lda < K || ldw < K || ldc < N ||
@@ -1471,21 +1215,20 @@ static int gemm_bf16x3_impl(const uint16_t* A2, int64_t lda, const uint16_t* W2,
     set_last_error("kf_gemm_bf16x3: bn 112 needs fp32 output and one-CTA tiles");
     return KF_E_INVALID;
   }
-  if (sk && (bn == 96 || bn == 112 || (flags & (KF_GEMM_PAIR | KF_GEMM_K32)))) {
-    set_last_error("kf_gemm_bf16x3_sk: bn must be 64, 128 or 256, without KF_GEMM_PAIR/K32");
+  if (sk && (bn == 96 || bn == 112 || (flags & KF_GEMM_PAIR))) {
+    set_last_error("kf_gemm_bf16x3_sk: bn must be 64, 128 or 256, without KF_GEMM_PAIR");
     return KF_E_INVALID;
   }
-  // k blocks of 64 bf16 (128-byte rows) or, with KF_GEMM_K32, of 32 (64-byte
-  // rows): the x coordinate of every load is a multiple of 32 elements.
-  const bool k32 = (flags & KF_GEMM_K32) != 0;
+  // k blocks of 64 bf16 (128-byte rows): the x coordinate of every load is a
+  // multiple of 64 elements.
   // KF_GEMM_PAIR: cta_group::2 tiles of 256 x bn; each CTA stages bn/2 B rows.
   const bool pair = (flags & KF_GEMM_PAIR) != 0;
-  if (pair && (k32 || (bn != 128 && bn != 256))) {
-    set_last_error("kf_gemm_bf16x3: KF_GEMM_PAIR needs bn 128 or 256 and no KF_GEMM_K32");
+  if (pair && bn != 128 && bn != 256) {
+    set_last_error("kf_gemm_bf16x3: KF_GEMM_PAIR needs bn 128 or 256");
     return KF_E_INVALID;
   }
-  const uint32_t kbox = k32 ? 32 : 64;
-  const CUtensorMapSwizzle ksw = k32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+  const uint32_t kbox = 64;
+  const CUtensorMapSwizzle ksw = CU_TENSOR_MAP_SWIZZLE_128B;
   CUtensorMap ta, tb, tcm;
   memset(&tcm, 0, sizeof(tcm));
   int rc;
@@ -1569,15 +1312,6 @@ static int gemm_bf16x3_impl(const uint16_t* A2, int64_t lda, const uint16_t* W2,
                                                          live_count, st);
   }
 #define KF_GEMM_PRE_CASE(BNV)                                                                  \
-  if (bn == BNV && k32) {                                                                      \
-    if (epilogue == KF_EPI_BIAS)                                                               \
-      return launch_gemm<BNV, KF_EPI_BIAS, 4>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,          \
-                                              head_dim, head_stride, live_tiles, live_count,   \
-                                              st);                                             \
-    return launch_gemm<BNV, KF_EPI_BIAS_GELU, 4>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,       \
-                                                 head_dim, head_stride, live_tiles,            \
-                                                 live_count, st);                              \
-  }                                                                                            \
   if (bn == BNV) {                                                                             \
     if (epilogue == KF_EPI_BIAS)                                                               \
       return launch_gemm<BNV, KF_EPI_BIAS, 3>(ta, tb, tcm, Cf, ldc, bias, m, n, k, f,          \
@@ -1635,74 +1369,3 @@ extern "C" int kf_gemm_bf16x3_sk(const uint16_t* A2, int64_t lda, const uint16_t
                           head_stride, live_tiles, live_count, &sk, stream);
 }
 
-extern "C" int kf_gemm_bf16x3_add_ln(const uint16_t* A2, int64_t lda, const uint16_t* W2,
-                                     int64_t ldw, const float* bias, const float* res, int64_t ldr,
-                                     const uint8_t* keep, const float* gamma, const float* beta,
-                                     float eps, float* s_out, int64_t lds, void* h_out,
-                                     int64_t ldh, int64_t M, int64_t N, int64_t K, int ln_flags,
-                                     const int32_t* live_tiles, const int32_t* live_count,
-                                     void* stream) {
-  if (!A2 || !W2 || !res || !gamma || !beta || !h_out || M < 0 || N < 0 || K < 0) {
-    set_last_error("kf_gemm_bf16x3_add_ln: invalid arguments");
-    return KF_E_INVALID;
-  }
-  if (M == 0 || N == 0) return KF_OK;
-  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  if (N % 128 || N / 128 > 8 || K == 0 || K % 8 || lda % 8 || ldw % 8 || lda < K || ldw < K ||
-      ldr % 4 || ldr < N || ldh < N || (s_out && (lds % 4 || lds < N || !a16(s_out))) ||
-      !a16(A2) || !a16(W2) || !a16(res) || !a16(gamma) || !a16(beta) || !a16(h_out) ||
-      (bias && !a16(bias)) || ((ln_flags & KF_LN_OUT_BF16X2) ? ldh % 8 : ldh % 4)) {
-    set_last_error(
-        "kf_gemm_bf16x3_add_ln: needs N %% 128 == 0 and N <= 1024, K, lda, ldw %% 8 == 0, "
-        "ldr, lds %% 4 == 0, ldh %% %d == 0 and 16-byte aligned pointers (N=%lld K=%lld)",
-        (ln_flags & KF_LN_OUT_BF16X2) ? 8 : 4, (long long)N, (long long)K);
-    return KF_E_UNSUPPORTED;
-  }
-  if (M > INT32_MAX / 2 || K > INT32_MAX) {
-    set_last_error("kf_gemm_bf16x3_add_ln: dimensions beyond 2^30");
-    return KF_E_UNSUPPORTED;
-  }
-  if ((ln_flags & KF_LN_OUT_BF16X2) && (ln_flags & KF_LN_ROUND_TF32)) {
-    set_last_error("kf_gemm_bf16x3_add_ln: KF_LN_OUT_BF16X2 and KF_LN_ROUND_TF32 are exclusive");
-    return KF_E_INVALID;
-  }
-  if ((live_tiles == nullptr) != (live_count == nullptr)) {
-    set_last_error("kf_gemm_bf16x3_add_ln: live_tiles and live_count go together");
-    return KF_E_INVALID;
-  }
-  CUtensorMap ta, tb;
-  int rc;
-  {
-    const uint64_t dims[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M), 2};
-    const uint64_t strides[2] = {static_cast<uint64_t>(lda) * 2,
-                                 static_cast<uint64_t>(M) * static_cast<uint64_t>(lda) * 2};
-    const uint32_t box[3] = {64, 128, 1};
-    rc = encode_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, A2, dims, strides, box,
-                           CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
-  }
-  {
-    const uint64_t dims[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N), 2};
-    const uint64_t strides[2] = {static_cast<uint64_t>(ldw) * 2,
-                                 static_cast<uint64_t>(N) * static_cast<uint64_t>(ldw) * 2};
-    const uint32_t box[3] = {64, 128, 1};
-    rc = encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, W2, dims, strides, box,
-                           CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
-  }
-  LnArgs ln;
-  ln.res = res;
-  ln.ldr = ldr;
-  ln.keep = keep;
-  ln.gamma = gamma;
-  ln.beta = beta;
-  ln.s_out = s_out;
-  ln.lds = lds;
-  ln.h_out = h_out;
-  ln.ldh = ldh;
-  ln.eps = eps;
-  ln.flags = ln_flags & (KF_LN_MASK_OUT | KF_LN_ROUND_TF32 | KF_LN_SKIP_PADDED | KF_LN_OUT_BF16X2);
-  return launch_gemm_ln(ta, tb, bias, static_cast<int>(M), static_cast<int>(N),
-                        static_cast<int>(K), ln, live_tiles, live_count,
-                        static_cast<cudaStream_t>(stream));
-}

@@ -53,24 +53,11 @@ class Plan:
     # GEMMs compute only 128-row tiles holding a real token and the non-final
     # norms leave padded rows untouched (every consumer masks those rows).
     skip_padded_rows: bool = True
-    # Residual add + mask + LayerNorm in the epilogue of out_proj and FFN2
-    # (bf16x3 GEMMs, d a multiple of 128 up to 1024): one kernel fewer per
-    # norm, and y never reaches memory. Off unless the table turns it on for
-    # a shape: with one row tile per cluster (c2) the fused epilogue is
-    # exposed and the forward is slower (0.850 vs 0.731 ms).
-    fuse_ln: bool = False
     # N tile of each GEMM (0 = pick by wave quantisation at launch).
     bn_qkv: int = 0
     bn_out: int = 0
     bn_ffn1: int = 0
     bn_ffn2: int = 0
-    # k block of each bf16x3 GEMM's shared-memory stages: 64 bf16 (128-byte
-    # rows) or 32 (64-byte rows, twice as many half-size stages in flight).
-    # Same MMA order either way, so the output is bit-identical.
-    kb_qkv: int = 64
-    kb_out: int = 64
-    kb_ffn1: int = 64
-    kb_ffn2: int = 64
     # bf16x3 GEMM on CTA pairs (tcgen05 cta_group::2, 256 x bn tiles, bn 128
     # or 256): each SM stages half of B, which relieves shared-memory
     # bandwidth on large GEMMs (c3b/c4: 9-18% faster per GEMM at bn 256);
@@ -126,8 +113,6 @@ class Plan:
             bits.append("skip-empty-q")
         if self.skip_padded_rows:
             bits.append("skip-padded-rows")
-        if self.fuse_ln:
-            bits.append("ln-in-gemm")
         if self.attn_persistent:
             bits.append("persistent-attn")
         elif self.order_rows:
@@ -139,9 +124,6 @@ class Plan:
         tiles = (self.bn_qkv, self.bn_out, self.bn_ffn1, self.bn_ffn2)
         if any(tiles):
             bits.append("bn=" + "/".join(str(t or "auto") for t in tiles))
-        kbs = (self.kb_qkv, self.kb_out, self.kb_ffn1, self.kb_ffn2)
-        if any(k != 64 for k in kbs):
-            bits.append("kb=" + "/".join(str(k) for k in kbs))
         pairs = (self.pair_qkv, self.pair_out, self.pair_ffn1, self.pair_ffn2)
         if any(pairs):
             bits.append("cta-pair=" + "/".join("y" if p else "n" for p in pairs))

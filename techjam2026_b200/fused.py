@@ -304,8 +304,6 @@ class FusedTransformer(LayerStack):
 
         def gemm(kind, g, A, lda, W, bias, C, ldc, N, K, epi, flags, bn, hd_=0, hs_=0):
             if split[g]:
-                if getattr(plan, f"kb_{g}") == 32:
-                    flags |= _lib.KF_GEMM_K32
                 if getattr(plan, f"sk_{g}"):
                     run(kind, L.kf_gemm_bf16x3_sk, A, lda, W.data_ptr(), K, bias.data_ptr(), C,
                         ldc, M, N, K, epi, flags, bn or 128, hd_, hs_, lt, lc,
@@ -339,10 +337,6 @@ class FusedTransformer(LayerStack):
         run("ln", L.kf_ln_add_mask, x.data_ptr(), d, None, 0, keep, l0["ln1w"].data_ptr(),
             l0["ln1b"].data_ptr(), res, d, h_qkv, d, M, d, l0["eps1"], f_ln1, st)
         nl = len(w.layers)
-        # LayerNorm fused into the epilogue of the GEMMs whose width is d:
-        # clusters of d/128 CTAs exchange row statistics (d <= 1024).
-        can_fuse = plan.fuse_ln and d % 128 == 0 and d <= 1024
-        fuse = {"out": can_fuse and split["out"], "ffn2": can_fuse and split["ffn2"]}
         f_ffn1_out = _lib.KF_GEMM_OUT_BF16X2 if split["ffn2"] else (
             _lib.KF_GEMM_ROUND_TF32 if (R and prec["ffn2"] == "tf32") else 0)
         for i, lw in enumerate(w.layers):
@@ -362,18 +356,11 @@ class FusedTransformer(LayerStack):
                 run("attention", L.kf_flash_fwd_tf32, qkv, S * ldq, dhs, ldq,
                     qkv + 4 * H * dhs, S * ldq, dhs, ldq, qkv + 8 * H * dhs, S * ldq, dhs,
                     ldq, ctx, S * d, dh, d, bits, B, H, S, dhs, dh, dh ** -0.5, attn_flags, st)
-            # out_proj, then the residual add + mask + LN2 (fused into the
-            # GEMM's epilogue when the plan allows it).
-            if fuse["out"]:
-                run("out_proj", L.kf_gemm_bf16x3_add_ln, ctx, d, lw["wo"].data_ptr(), d,
-                    lw["bo"].data_ptr(), res, d, keep, lw["ln2w"].data_ptr(),
-                    lw["ln2b"].data_ptr(), lw["eps2"], res, d, h_ffn1, d, M, d, d, f_ln2, lt,
-                    lc, st)
-            else:
-                gemm("out_proj", "out", ctx, d, lw["wo"], lw["bo"], y, d, d, d,
-                     _lib.KF_EPI_BIAS, 0, plan.bn_out)
-                run("ln", L.kf_ln_add_mask, res, d, y, d, keep, lw["ln2w"].data_ptr(),
-                    lw["ln2b"].data_ptr(), res, d, h_ffn1, d, M, d, lw["eps2"], f_ln2, st)
+            # out_proj, then the residual add + mask + LN2.
+            gemm("out_proj", "out", ctx, d, lw["wo"], lw["bo"], y, d, d, d,
+                 _lib.KF_EPI_BIAS, 0, plan.bn_out)
+            run("ln", L.kf_ln_add_mask, res, d, y, d, keep, lw["ln2w"].data_ptr(),
+                lw["ln2b"].data_ptr(), res, d, h_ffn1, d, M, d, lw["eps2"], f_ln2, st)
             gemm("ffn1", "ffn1", h_ffn1, d, lw["w1"], lw["b1"], ffn, F, F, d,
                  _lib.KF_EPI_BIAS_GELU, f_ffn1_out, plan.bn_ffn1)
             # FFN2, then the next layer's LN1 (or the final norm).
@@ -384,15 +371,10 @@ class FusedTransformer(LayerStack):
                 nx = w.layers[i + 1]
                 nw, nb, ne = nx["ln1w"].data_ptr(), nx["ln1b"].data_ptr(), nx["eps1"]
                 s_out, h_out, f_next = res, h_qkv, f_ln1
-            if fuse["ffn2"]:
-                run("ffn2", L.kf_gemm_bf16x3_add_ln, ffn, F, lw["w2"].data_ptr(), F,
-                    lw["b2"].data_ptr(), res, d, keep, nw, nb, ne, s_out, d, h_out, d, M, d, F,
-                    f_next, lt, lc, st)
-            else:
-                gemm("ffn2", "ffn2", ffn, F, lw["w2"], lw["b2"], y, d, d, F, _lib.KF_EPI_BIAS, 0,
-                     plan.bn_ffn2)
-                run("ln", L.kf_ln_add_mask, res, d, y, d, keep, nw, nb, s_out, d, h_out, d, M, d,
-                    ne, f_next, st)
+            gemm("ffn2", "ffn2", ffn, F, lw["w2"], lw["b2"], y, d, d, F, _lib.KF_EPI_BIAS, 0,
+                 plan.bn_ffn2)
+            run("ln", L.kf_ln_add_mask, res, d, y, d, keep, nw, nb, s_out, d, h_out, d, M, d,
+                ne, f_next, st)
         self.launches_per_forward = n
         return n
 

@@ -86,19 +86,19 @@ def test_empty_problems_are_no_ops(lib):
                               0, None) == 0
 
 
-def test_fused_gemm_layernorm_entry_rejects_before_any_launch():
-    """kf_gemm_bf16x3_add_ln validates its arguments on the host: null
-    operands, and widths that are not a multiple of 128 (or above 1024), are
-    refused with an error code before any CUDA call."""
+def test_bf16x3_gemm_rejects_unknown_flags_before_any_launch():
+    """kf_gemm_bf16x3 and its stream-K form refuse flag bits they do not know
+    (bit 16 is no longer a GEMM flag) with an error code and no CUDA call,
+    instead of silently ignoring them."""
     lib = _lib.lib()
-    args = lambda N: (16, 64, 16, 64, None, 16, N, None, 16, 16, 1e-5, None, 0, 16, N, 128, N,
-                      64, 0, None, None, None)
-    assert lib.kf_gemm_bf16x3_add_ln(None, 64, None, 64, None, None, 128, None, None, None, 1e-5,
-                                     None, 0, None, 128, 128, 128, 64, 0, None, None, None) == \
-        _lib.KF_E_INVALID
-    assert lib.kf_gemm_bf16x3_add_ln(*args(100)) == _lib.KF_E_UNSUPPORTED
-    assert b"128" in lib.kf_last_error()
-    assert lib.kf_gemm_bf16x3_add_ln(*args(2048)) == _lib.KF_E_UNSUPPORTED
+    fake = ctypes.c_void_p(0x1000)
+    for bits in (16, 128, 1 << 12):
+        assert lib.kf_gemm_bf16x3(fake, 64, fake, 64, None, fake, 64, 128, 64, 64, 0, bits, 0, 0,
+                                  0, None, None, None) == _lib.KF_E_INVALID
+        assert b"unknown flags" in lib.kf_last_error()
+        assert lib.kf_gemm_bf16x3_sk(fake, 64, fake, 64, None, fake, 64, 128, 64, 64, 0, bits,
+                                     64, 0, 0, None, None, fake, 1 << 20,
+                                     None) == _lib.KF_E_INVALID
 
 
 def test_noalloc_entry_rejects_bad_attention_arguments_before_any_launch():
