@@ -425,6 +425,10 @@ def main():
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    # Several ranks on one host: each stays on its GPU's NUMA node. (One rank
+    # keeps every core: the CPU baseline runs there.)
+    host_binding = bind_host_to_gpu(local) if world > 1 else {"bound": False,
+                                                              "why": "one rank"}
     if world > 1:
         dist.init_process_group("nccl", device_id=dev,
                                 timeout=datetime.timedelta(seconds=120))
@@ -677,7 +681,8 @@ def main():
                        "useful_tflop": round(flops_all / 1e12, 4)},
             "tc_frac_of_tf32_peak": round(value / world / peaks["tf32_tflops"], 4),
             "gpu_launches": int(runner.launches * args.steps),
-            "e2e": e2e, "gather": gather, "roofline": roofline, "cpu_baseline": cpu,
+            "e2e": e2e, "gather": gather, "host_binding": host_binding,
+            "roofline": roofline, "cpu_baseline": cpu,
             "clocks": clk, "device_status": status,
         }
         print(json.dumps(line), flush=True)
@@ -687,6 +692,40 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def bind_host_to_gpu(device_index: int) -> dict:
+    """Pin this process to the CPU cores NVML reports as nearest to the GPU
+    (its NUMA node), so the pinned host buffers of the e2e leg live on, and
+    are copied from, that node when several ranks share the host. Only NVML
+    queries are made and only this process's CPU affinity changes."""
+    try:
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            try:
+                h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-")
+                                                     else "GPU-" + uuid)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            n = os.cpu_count() or 1
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, (n + 63) // 64)
+            try:
+                node = int(pynvml.nvmlDeviceGetNumaNodeId(h))
+            except Exception:
+                node = None
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception as e:  # no NVML: leave the affinity alone
+        return {"bound": False, "why": f"NVML: {e}"[:100]}
+    near = {64 * i + b for i, w in enumerate(words) for b in range(64) if (int(w) >> b) & 1}
+    cores = near & set(os.sched_getaffinity(0))
+    if not cores:
+        return {"bound": False, "why": "no allowed core near the GPU"}
+    os.sched_setaffinity(0, cores)
+    return {"bound": True, "cores": len(cores), "numa_node": node}
 
 
 def cpu_model() -> str:
