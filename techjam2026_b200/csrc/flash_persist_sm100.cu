@@ -529,15 +529,8 @@ __global__ void __launch_bounds__(192, MINB)
 #pragma unroll
         for (int w = 0; w < BN / 32; ++w) all_keys = all_keys && (kw[w] == 0xffffffffu);
         const bool diag = causal && (k0 + BN - 1 > q0);
-        if (!(all_keys && !diag)) {
-#pragma unroll
-          for (int c = 0; c < BN; ++c) {
-            const int kidx = k0 + c;
-            const bool valid =
-                ((kw[c >> 5] >> (c & 31)) & 1u) && (kidx < S) && (!causal || kidx <= qi);
-            s[c] = valid ? s[c] : -INFINITY;
-          }
-        }
+        if (!(all_keys && !diag))
+          mask_scores<BN>(s, kw, (causal && qi + 1 < S ? qi + 1 : S) - k0);
         float mp[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) mp[u] = fmaxf(s[u], s[u + 8]);

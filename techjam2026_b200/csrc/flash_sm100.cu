@@ -95,6 +95,22 @@ __device__ __forceinline__ bool kv_tile_live(const uint32_t* kb, int words, int 
   return any != 0;
 }
 
+// Masks one query row of a key tile: s[c] becomes -inf unless key k0 + c is
+// valid (its bit in the tile's words kw) and k0 + c < k0 + limit, where the
+// limit is S (or, causal, min(S, query + 1)) minus k0. One 32-bit valid mask
+// per word, then one select per score: the cost of a masked tile stays
+// close to that of an unmasked one.
+template <int BN>
+__device__ __forceinline__ void mask_scores(float (&s)[BN], const uint32_t* kw, int limit) {
+#pragma unroll
+  for (int w = 0; w < BN / 32; ++w) {
+    const int lw = limit - 32 * w;
+    const uint32_t vb = kw[w] & (lw >= 32 ? 0xffffffffu : (lw <= 0 ? 0u : ((1u << lw) - 1u)));
+#pragma unroll
+    for (int c = 0; c < 32; ++c) s[32 * w + c] = ((vb >> c) & 1u) ? s[32 * w + c] : -INFINITY;
+  }
+}
+
 // Internal flag: O is written through the tmO tensor map (TMA stores).
 constexpr int KF_ATTN_TMA_OUT = 1 << 9;
 
@@ -485,14 +501,8 @@ __global__ void __launch_bounds__(192, MINB)
       // with max and rounding is monotonic), then P = 2^(s*scale - m) with
       // the scale folded into one FMA. Masked keys hold -inf and give P = 0.
       // Eight partial maxima / sums keep the dependency chains short.
-      if (!(all_keys && !diag)) {
-#pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const int kidx = k0 + c;
-          const bool valid = ((kw[c >> 5] >> (c & 31)) & 1u) && (kidx < S) && (!causal || kidx <= qi);
-          s[c] = valid ? s[c] : -INFINITY;
-        }
-      }
+      if (!(all_keys && !diag))
+        mask_scores<BN>(s, kw, (causal && qi + 1 < S ? qi + 1 : S) - k0);
       // Eight partial maxima, two new scores per three-input max.
       float mp[8];
 #pragma unroll
