@@ -16,7 +16,7 @@
 //               the next item as soon as the softmax warps release the
 //               single Q buffer, and streams K and V tiles of all its items
 //               through two rings;
-//   warp 1      MMA issuer: S_j into three TMEM buffers, O += P V from P in
+//   warp 1      MMA issuer: S_j into two TMEM buffers, O += P V from P in
 //               TMEM; after an item's last P V it commits o_final;
 //   warps 2-5   softmax (one thread per query row), then the item's O:
 //               TMEM -> registers -> O / l, staged in the Q buffer (idle once
@@ -575,7 +575,8 @@ __global__ void __launch_bounds__(192, MINB)
         if (__any_sync(0xffffffffu, rescale_o)) {
           // P V of the item's previous tile must have landed before O is
           // rescaled; o_done[(it-1) & 1] is at most one phase behind it
-          // (the s_full arrival just observed implies P V of tile it - 3).
+          // (the s_full arrival just observed implies P V of tile it - NSB,
+          // hence of tile it - 3).
           if (!mbar_wait(&o_done[(it - 1) & 1], static_cast<uint32_t>(((it - 1) >> 1) & 1),
                          abort_flag, KF_DEV_WAIT_TIMEOUT_SOFTMAX)) {
             ok = false;

@@ -5,11 +5,11 @@
 //   warp 0      TMA producer: Q once, then K and V tiles of BN keys through
 //               two independent smem rings, each refilled as soon as its slot
 //               frees (K once S = QK^T is done, V after O += PV);
-//   warp 1      MMA issuer and TMEM owner. TMEM holds three S buffers (BN fp32
+//   warp 1      MMA issuer and TMEM owner. TMEM holds two S buffers (BN fp32
 //               columns each) and the O accumulator (DH columns). S_j = Q K_j^T
-//               is issued as soon as O += P_{j-3} V_{j-3} has been (its buffer
-//               is then free), two softmax passes before it is needed; then
-//               O += P_{j-2} V_{j-2}, which waits for that softmax. O += P_j V_j
+//               is issued as soon as O += P_{j-2} V_{j-2} has been (its buffer
+//               is then free), one softmax pass before it is needed; then
+//               O += P_{j-1} V_{j-1}, which waits for that softmax. O += P_j V_j
 //               reads P straight from TMEM (tcgen05.mma A operand in TMEM), so
 //               P never touches shared memory;
 //   warps 2-5   softmax: one thread per query row (TMEM lane). Reads its S row,
@@ -61,9 +61,11 @@ struct FlashCfg {
   static constexpr int SMEM_BYTES = BITS_OFF + BITS_WORDS * 4 + 1024;
   // Power-of-two TMEM allocation covering the S buffers and O; with MINB CTAs
   // per SM the allocations must fit the SM's 512 columns together.
-  // S buffers in TMEM: with three, S = Q K^T runs two KV tiles ahead of the
-  // softmax, so the next S is ready when a softmax pass ends.
-  static constexpr int NSB = 3;
+  // S buffers in TMEM: with two, S = Q K^T runs one KV tile ahead of the
+  // softmax, and a softmax pass is long enough for the next S to be ready
+  // when it ends (measured: three buffers were 2-4% slower, their extra TMEM
+  // traffic and allocation bought nothing).
+  static constexpr int NSB = 2;
   static constexpr int TMEM_NEED = NSB * BN + DH;
   static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64
                                  : TMEM_NEED <= 128 ? 128 : TMEM_NEED <= 256 ? 256 : 512;
@@ -556,8 +558,9 @@ __global__ void __launch_bounds__(192, MINB)
       l_run += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       if (__any_sync(0xffffffffu, rescale_o)) {
         // O += P_{it-1} V_{it-1} must have landed before this row is rescaled.
-        // The s_full arrival just observed implies PV_{it-3} is complete (the
-        // MMA pipe completes in issue order and S_it was issued after it).
+        // The s_full arrival just observed implies PV_{it-NSB}, hence PV_{it-3},
+        // is complete (the MMA pipe completes in issue order and S_it was
+        // issued after PV_{it-NSB}).
         // o_done[(it-1) & 1] counts the products of that parity (PV_{it-3},
         // PV_{it-1}, ...), so it is at most one phase (PV_{it-1} itself)
         // behind and the parity wait is exact.
