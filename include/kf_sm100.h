@@ -72,9 +72,11 @@ int kf_set_wait_limit(int64_t cycles);
                                only when every consumer masks those rows) */
 #define KF_LN_OUT_BF16X2 8  /* write h as bf16 hi/lo planes: h_out is then a
                                uint16 [2][M][ldh] buffer (kf_gemm_bf16x3 input) */
-#define KF_LN_STATIC_PARAMS 16 /* keep, w and b were written before the kernel that
-                                  precedes this call in the stream started: they are
-                                  loaded before waiting for that kernel */
+#define KF_LN_STATIC_PARAMS 16 /* keep, w and b (and row_map) were written before the
+                                  kernel that precedes this call in the stream started:
+                                  they are loaded before waiting for that kernel */
+#define KF_LN_Y_MAPPED 32 /* kf_ln_add_mask_rows: y of row r is row row_map[r] of y */
+#define KF_LN_H_MAPPED 64 /* kf_ln_add_mask_rows: h of row r goes to row row_map[r] */
 
 /* Fused residual-add + row mask + LayerNorm over rows of width d:
  *     s = keep[r] ? x[r] + y[r] : 0          (y optional, keep optional)
@@ -87,6 +89,30 @@ int kf_set_wait_limit(int64_t cycles);
 int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64_t ldy, const uint8_t* keep,
                    const float* w, const float* b, float* s_out, int64_t lds, float* h_out,
                    int64_t ldh, int64_t M, int64_t d, float eps, int flags, void* stream);
+
+/* kf_ln_add_mask with y and / or h in a packed row order: row_map[r] (int32,
+ * M entries, e.g. from kf_pack_rows) is the row of y read for row r
+ * (KF_LN_Y_MAPPED) and the row of h written for it (KF_LN_H_MAPPED); an entry
+ * of -1 means row r has no y (s = keep ? x : 0) and writes no h. x, keep and
+ * s_out stay in the unpacked order; h's bf16 planes keep the stride M * ldh.
+ * The arithmetic of every row is that of kf_ln_add_mask. Lets the FFN GEMMs
+ * run over valid tokens only (no reference counterpart: the reference keeps
+ * the padded layout, kernelforge/optimized.py:441-446). */
+int kf_ln_add_mask_rows(const float* x, int64_t ldx, const float* y, int64_t ldy,
+                        const uint8_t* keep, const float* w, const float* b, float* s_out,
+                        int64_t lds, float* h_out, int64_t ldh, int64_t M, int64_t d, float eps,
+                        int flags, const int32_t* row_map, void* stream);
+
+/* Packed row order of the valid tokens of a [B, S] key mask (its kf_keep_bits
+ * words): row_map[b*S + s] = the rank of token (b, s) among all valid tokens
+ * in row-major order, or -1 for a padded one; row_off[0..B] the prefix sums
+ * of the rows' valid counts (row_off[B] = T); tiles[i] = i for the
+ * ceil(T / 128) 128-row tiles that hold packed rows, *tile_count that number
+ * (the live_tiles / live_count form of the GEMMs). row_map holds B*S int32,
+ * row_off B+1, tiles ceil(B*S/128). B <= 65535. Two small kernels. No
+ * reference counterpart (see kf_ln_add_mask_rows). */
+int kf_pack_rows(const uint32_t* bits, int64_t B, int64_t S, int32_t* row_map, int32_t* row_off,
+                 int32_t* tiles, int32_t* tile_count, void* stream);
 
 /* ----------------------------------------------------------- GEMM */
 

@@ -32,6 +32,10 @@ SIGNATURES = {
                               _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int,
                               _c_ptr, _c_ptr, _c_ptr]),
     "kf_live_row_tiles": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_ptr, _c_ptr]),
+    "kf_ln_add_mask_rows": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_ptr,
+                                     _c_ptr, _c_i64, _c_ptr, _c_i64, _c_i64, _c_i64, _c_float,
+                                     _c_int, _c_ptr, _c_ptr]),
+    "kf_pack_rows": (_c_int, [_c_ptr, _c_i64, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr]),
     "kf_gemm_bf16x3": (_c_int, [_c_ptr, _c_i64, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_i64,
                                 _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int,
                                 _c_ptr, _c_ptr, _c_ptr]),
@@ -83,6 +87,8 @@ KF_LN_ROUND_TF32 = 2
 KF_LN_SKIP_PADDED = 4
 KF_LN_OUT_BF16X2 = 8
 KF_LN_STATIC_PARAMS = 16
+KF_LN_Y_MAPPED = 32
+KF_LN_H_MAPPED = 64
 KF_EPI_BIAS = 0
 KF_EPI_BIAS_GELU = 1
 KF_GEMM_ROUND_TF32 = 1

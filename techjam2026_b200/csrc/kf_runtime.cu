@@ -154,6 +154,99 @@ __global__ void __launch_bounds__(1024) live_row_tiles_kernel(const uint8_t* __r
   if (tid == 0) *count = base;
 }
 
+// Packed row order of the valid tokens (kf_pack_rows), step 1 of 2: one CTA.
+// A warp counts one batch row's valid keys from its key-bit words; warp 0
+// turns each group of 32 counts into row offsets (an exclusive prefix sum
+// carried from group to group). Then the tile list of the T packed rows.
+__global__ void __launch_bounds__(1024) pack_offsets_kernel(const uint32_t* __restrict__ bits,
+                                                            int B, int S,
+                                                            int32_t* __restrict__ row_off,
+                                                            int32_t* __restrict__ tiles,
+                                                            int32_t* __restrict__ tile_count) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ int cnt[32];
+  __shared__ int run;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int words = (S + 31) >> 5;
+  if (tid == 0) run = 0;
+  __syncthreads();
+  for (int b0 = 0; b0 < B; b0 += 32) {
+    const int b = b0 + warp;
+    int c = 0;
+    if (b < B) {
+      const uint32_t* rb = bits + static_cast<int64_t>(b) * words;
+      for (int w = lane; w < words; w += 32) c += __popc(rb[w]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    }
+    if (lane == 0) cnt[warp] = c;
+    __syncthreads();
+    if (warp == 0) {
+      const int v = cnt[lane];
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      const int r = run;
+      if (b0 + lane < B) row_off[b0 + lane] = r + incl - v;
+      __syncwarp();
+      if (lane == 31) run = r + incl;
+    }
+    __syncthreads();
+  }
+  const int T = run;
+  const int n = (T + 127) / 128;
+  for (int i = tid; i < n; i += 1024) tiles[i] = i;
+  if (tid == 0) {
+    row_off[B] = T;
+    *tile_count = n;
+  }
+}
+
+// Step 2 of 2: one CTA per batch row writes its entries of the map, 1024
+// positions (32 key words, a warp each) at a time; a valid token's packed row
+// is the row's offset plus its rank among the row's valid tokens.
+__global__ void __launch_bounds__(1024) pack_map_kernel(const uint32_t* __restrict__ bits, int S,
+                                                        const int32_t* __restrict__ row_off,
+                                                        int32_t* __restrict__ row_map) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ int cnt[32], excl[32];
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int words = (S + 31) >> 5;
+  const uint32_t* rb = bits + static_cast<int64_t>(b) * words;
+  int32_t* out = row_map + static_cast<int64_t>(b) * S;
+  int base = row_off[b];
+  for (int p0 = 0; p0 < S; p0 += 1024) {
+    const int w = (p0 >> 5) + warp;
+    const uint32_t word = w < words ? rb[w] : 0u;  // bits past S are 0
+    if (lane == 0) cnt[warp] = __popc(word);
+    __syncthreads();
+    if (warp == 0) {
+      const int v = cnt[lane];
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      excl[lane] = incl - v;
+    }
+    __syncthreads();
+    const int pos = p0 + tid;
+    if (pos < S)
+      out[pos] = ((word >> lane) & 1u)
+                     ? base + excl[warp] + __popc(word & ((1u << lane) - 1u))
+                     : -1;
+    base += excl[31] + cnt[31];
+    __syncthreads();  // cnt / excl are rewritten by the next chunk
+  }
+}
+
 // dst = [2][rows][ld_dst] bf16 planes (hi, then lo) of src [rows][ld_src].
 __global__ void split_bf16x2_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
                                     int64_t ld_src, uint16_t* __restrict__ dst, int64_t ld_dst) {
@@ -418,6 +511,24 @@ extern "C" int kf_live_row_tiles(const uint8_t* keep, int64_t M, int32_t* tiles,
   return cuda_status(launch_chained(live_row_tiles_kernel, dim3(1), dim3(1024), 0,
                                     static_cast<cudaStream_t>(stream), keep, M, tiles, count),
                      "kf_live_row_tiles launch");
+}
+
+extern "C" int kf_pack_rows(const uint32_t* bits, int64_t B, int64_t S, int32_t* row_map,
+                            int32_t* row_off, int32_t* tiles, int32_t* tile_count, void* stream) {
+  if (!bits || !row_map || !row_off || !tiles || !tile_count || B <= 0 || S <= 0 ||
+      B > 65535 || B * S > INT32_MAX) {
+    set_last_error("kf_pack_rows: invalid arguments (B=%lld S=%lld)", (long long)B, (long long)S);
+    return KF_E_INVALID;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int b = static_cast<int>(B), s = static_cast<int>(S);
+  int rc = cuda_status(launch_chained(pack_offsets_kernel, dim3(1), dim3(1024), 0, st, bits, b, s,
+                                      row_off, tiles, tile_count),
+                       "kf_pack_rows launch (offsets)");
+  if (rc) return rc;
+  return cuda_status(launch_chained(pack_map_kernel, dim3(static_cast<unsigned>(b)), dim3(1024), 0,
+                                    st, bits, s, static_cast<const int32_t*>(row_off), row_map),
+                     "kf_pack_rows launch (map)");
 }
 
 extern "C" int kf_batch_order(const uint32_t* bits, int64_t B, int64_t S, int32_t* order,

@@ -33,12 +33,17 @@ __device__ __forceinline__ float warp_sum(float v) {
 // bandwidth (c4: 165.9 -> 135.2 us per norm, 0.95 of the measured copy
 // rate). Other widths keep the compiler's choice (at 64 registers NV 4
 // would spill).
-template <int NV>
+//
+// MAP (kf_ln_add_mask_rows): bit 0 = y of row r is read from row row_map[r]
+// (KF_LN_Y_MAPPED), bit 1 = h is written to it (KF_LN_H_MAPPED); an entry of
+// -1 means no y and no h for that row. Separate instantiations, so the plain
+// norm carries none of it and an h-mapped norm's loads wait on nothing.
+template <int NV, int MAP>
 __global__ void __launch_bounds__(256, (NV == 6 || NV == 8) ? 4 : 1) ln_add_mask_vec_kernel(
     const float* x, int64_t ldx, const float* y, int64_t ldy, const uint8_t* __restrict__ keep,
     const float* __restrict__ w, const float* __restrict__ b, float* s_out, int64_t lds,
     float* __restrict__ h_out, int64_t ldh, int64_t M,
-    int d, float eps, int flags) {
+    int d, float eps, int flags, const int32_t* __restrict__ row_map) {
   pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -58,8 +63,14 @@ __global__ void __launch_bounds__(256, (NV == 6 || NV == 8) ? 4 : 1) ln_add_mask
   const bool early = (flags & KF_LN_STATIC_PARAMS) != 0;
   float4 gw[NW], gb[NW];
   bool kept = true;
+  int64_t y_row = row, h_row = row;
   auto load_params = [&]() {
     kept = keep ? (__ldg(keep + row) != 0) : true;
+    if constexpr (MAP != 0) {
+      const int64_t mr = __ldg(row_map + row);
+      if constexpr (MAP & 1) y_row = mr;
+      if constexpr (MAP & 2) h_row = mr;
+    }
     if (PREFETCH_WB) {
 #pragma unroll
       for (int i = 0; i < NW; ++i) {
@@ -88,8 +99,8 @@ __global__ void __launch_bounds__(256, (NV == 6 || NV == 8) ? 4 : 1) ln_add_mask
     if (PREFETCH_WB) t[i] = v[i];
     if (c < nv4) {
       v[i] = reinterpret_cast<const float4*>(x + row * ldx)[c];
-      if (y) {
-        const float4 yy = reinterpret_cast<const float4*>(y + row * ldy)[c];
+      if (y && (!(MAP & 1) || y_row >= 0)) {
+        const float4 yy = reinterpret_cast<const float4*>(y + y_row * ldy)[c];
         if (PREFETCH_WB) {
           t[i] = yy;
         } else {
@@ -134,13 +145,15 @@ __global__ void __launch_bounds__(256, (NV == 6 || NV == 8) ? 4 : 1) ln_add_mask
   const bool zero_h = (flags & KF_LN_MASK_OUT) && !kept;
   const bool rnd = (flags & KF_LN_ROUND_TF32) != 0;
   const bool split = (flags & KF_LN_OUT_BF16X2) != 0;
-  uint16_t* h_hi = reinterpret_cast<uint16_t*>(h_out) + row * ldh;
+  uint16_t* h_hi = reinterpret_cast<uint16_t*>(h_out) + h_row * ldh;
   uint16_t* h_lo = h_hi + M * ldh;
+  const bool write_h = !(MAP & 2) || h_row >= 0;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int c = lane + 32 * i;
     if (c < nv4) {
       if (s_out) reinterpret_cast<float4*>(s_out + row * lds)[c] = v[i];
+      if (!write_h) continue;
       float4 h;
       if (zero_h) {
         h = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -161,7 +174,7 @@ __global__ void __launch_bounds__(256, (NV == 6 || NV == 8) ? 4 : 1) ln_add_mask
       if (split)
         store_split4(h_hi + 4 * c, h_lo + 4 * c, h);
       else
-        reinterpret_cast<float4*>(h_out + row * ldh)[c] = h;
+        reinterpret_cast<float4*>(h_out + h_row * ldh)[c] = h;
     }
   }
 }
@@ -171,7 +184,7 @@ __global__ void __launch_bounds__(256) ln_add_mask_scalar_kernel(
     const float* x, int64_t ldx, const float* y, int64_t ldy, const uint8_t* __restrict__ keep,
     const float* __restrict__ w, const float* __restrict__ b, float* s_out, int64_t lds,
     float* __restrict__ h_out, int64_t ldh, int64_t M,
-    int d, float eps, int flags) {
+    int d, float eps, int flags, const int32_t* __restrict__ row_map) {
   pdl_launch_dependents();
   pdl_wait();
   const int lane = threadIdx.x & 31;
@@ -179,10 +192,13 @@ __global__ void __launch_bounds__(256) ln_add_mask_scalar_kernel(
   if (row >= M) return;
   const bool kept = keep ? (keep[row] != 0) : true;  // (KF_LN_STATIC_PARAMS unused here)
   if (!kept && (flags & KF_LN_SKIP_PADDED)) return;
+  const int64_t mrow = row_map ? row_map[row] : row;
+  const int64_t y_row = !y ? -1 : ((flags & KF_LN_Y_MAPPED) ? mrow : row);
+  const int64_t h_row = (flags & KF_LN_H_MAPPED) ? mrow : row;
   auto val = [&](int c) -> float {
     if (!kept) return 0.f;
     float a = x[row * ldx + c];
-    if (y) a += y[row * ldy + c];
+    if (y_row >= 0) a += y[y_row * ldy + c];
     return a;
   };
   float sum = 0.f;
@@ -200,15 +216,16 @@ __global__ void __launch_bounds__(256) ln_add_mask_scalar_kernel(
   for (int c = lane; c < d; c += 32) {
     const float s = val(c);
     if (s_out) s_out[row * lds + c] = s;
+    if (h_row < 0) continue;
     float h = zero_h ? 0.f : (s - mean) * rstd * w[c] + b[c];
     if (rnd && !zero_h) h = round_tf32(h);
     if (flags & KF_LN_OUT_BF16X2) {
       uint16_t hi, lo;
       split_bf16(h, hi, lo);
-      reinterpret_cast<uint16_t*>(h_out)[row * ldh + c] = hi;
-      reinterpret_cast<uint16_t*>(h_out)[M * ldh + row * ldh + c] = lo;
+      reinterpret_cast<uint16_t*>(h_out)[h_row * ldh + c] = hi;
+      reinterpret_cast<uint16_t*>(h_out)[M * ldh + h_row * ldh + c] = lo;
     } else {
-      h_out[row * ldh + c] = h;
+      h_out[h_row * ldh + c] = h;
     }
   }
 }
@@ -219,10 +236,10 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 using namespace kf;
 
-extern "C" int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64_t ldy,
-                              const uint8_t* keep, const float* w, const float* b, float* s_out,
-                              int64_t lds, float* h_out, int64_t ldh, int64_t M, int64_t d,
-                              float eps, int flags, void* stream) {
+static int ln_add_mask_impl(const float* x, int64_t ldx, const float* y, int64_t ldy,
+                            const uint8_t* keep, const float* w, const float* b, float* s_out,
+                            int64_t lds, float* h_out, int64_t ldh, int64_t M, int64_t d,
+                            float eps, int flags, const int32_t* row_map, void* stream) {
   if (!x || !w || !b || !h_out || M < 0 || d <= 0 || ldx < d || ldh < d ||
       (y && ldy < d) || (s_out && lds < d) || d > (1 << 24)) {
     set_last_error("kf_ln_add_mask: invalid arguments (M=%lld d=%lld)", (long long)M,
@@ -248,9 +265,15 @@ extern "C" int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64
   cudaError_t e;
   if (vec) {
     const int nv = (di / 4 + 31) / 32;
+    const int map = !row_map ? 0
+                             : ((flags & KF_LN_Y_MAPPED) ? 1 : 0) | ((flags & KF_LN_H_MAPPED) ? 2 : 0);
+#define KF_LN_LAUNCH_MAP(NV, MAPV)                                                            \
+  launch_chained(ln_add_mask_vec_kernel<NV, MAPV>, dim3(blocks), dim3(threads), 0, st, x, ldx, y, \
+                 ldy, keep, w, b, s_out, lds, h_out, ldh, M, di, eps, flags, row_map)
 #define KF_LN_LAUNCH(NV)                                                                      \
-  e = launch_chained(ln_add_mask_vec_kernel<NV>, dim3(blocks), dim3(threads), 0, st, x, ldx, y,  \
-                     ldy, keep, w, b, s_out, lds, h_out, ldh, M, di, eps, flags)
+  e = map == 0 ? KF_LN_LAUNCH_MAP(NV, 0)                                                      \
+               : map == 1 ? KF_LN_LAUNCH_MAP(NV, 1)                                           \
+                          : map == 2 ? KF_LN_LAUNCH_MAP(NV, 2) : KF_LN_LAUNCH_MAP(NV, 3)
     if (nv <= 1)
       KF_LN_LAUNCH(1);
     else if (nv <= 2)
@@ -266,9 +289,35 @@ extern "C" int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64
     else
       KF_LN_LAUNCH(32);
 #undef KF_LN_LAUNCH
+#undef KF_LN_LAUNCH_MAP
   } else {
     e = launch_chained(ln_add_mask_scalar_kernel, dim3(blocks), dim3(threads), 0, st, x, ldx, y,
-                       ldy, keep, w, b, s_out, lds, h_out, ldh, M, di, eps, flags);
+                       ldy, keep, w, b, s_out, lds, h_out, ldh, M, di, eps, flags, row_map);
   }
   return cuda_status(e, "kf_ln_add_mask launch");
+}
+
+extern "C" int kf_ln_add_mask(const float* x, int64_t ldx, const float* y, int64_t ldy,
+                              const uint8_t* keep, const float* w, const float* b, float* s_out,
+                              int64_t lds, float* h_out, int64_t ldh, int64_t M, int64_t d,
+                              float eps, int flags, void* stream) {
+  if (flags & (KF_LN_Y_MAPPED | KF_LN_H_MAPPED)) {
+    set_last_error("kf_ln_add_mask: the row-map flags need kf_ln_add_mask_rows");
+    return KF_E_INVALID;
+  }
+  return ln_add_mask_impl(x, ldx, y, ldy, keep, w, b, s_out, lds, h_out, ldh, M, d, eps, flags,
+                          nullptr, stream);
+}
+
+extern "C" int kf_ln_add_mask_rows(const float* x, int64_t ldx, const float* y, int64_t ldy,
+                                   const uint8_t* keep, const float* w, const float* b,
+                                   float* s_out, int64_t lds, float* h_out, int64_t ldh,
+                                   int64_t M, int64_t d, float eps, int flags,
+                                   const int32_t* row_map, void* stream) {
+  if (!row_map || !(flags & (KF_LN_Y_MAPPED | KF_LN_H_MAPPED))) {
+    set_last_error("kf_ln_add_mask_rows: needs row_map and KF_LN_Y_MAPPED and/or KF_LN_H_MAPPED");
+    return KF_E_INVALID;
+  }
+  return ln_add_mask_impl(x, ldx, y, ldy, keep, w, b, s_out, lds, h_out, ldh, M, d, eps, flags,
+                          row_map, stream);
 }

@@ -117,6 +117,11 @@ class _Workspace:
         self.live_tiles = torch.zeros((M + 127) // 128, **i32)
         self.live_count = torch.zeros(1, **i32)
         self.order = torch.zeros(B, **i32)
+        # Packed row order of the valid tokens for the FFN GEMMs (kf_pack_rows).
+        self.row_map = torch.zeros(M, **i32) if plan.packed_ffn else None
+        self.row_off = torch.zeros(B + 1, **i32) if plan.packed_ffn else None
+        self.packed_tiles = torch.zeros((M + 127) // 128, **i32) if plan.packed_ffn else None
+        self.packed_count = torch.zeros(1, **i32) if plan.packed_ffn else None
         # Work list of the persistent attention (kf_attn_schedule), built once
         # per forward; zeroed so its counters start at 0.
         self.sched = (torch.zeros(int(_lib.lib().kf_attn_schedule_words(B, H, S)), **i32)
@@ -147,7 +152,8 @@ class _Workspace:
         return sum(t.numel() * t.element_size()
                    for t in (self.res, self.h, self.h2, self.qkv, self.ctx, self.y, self.ffn,
                              self.bits, self.live_tiles, self.live_count, self.order,
-                             self.sk, self.sched)
+                             self.sk, self.sched, self.row_map, self.row_off, self.packed_tiles,
+                             self.packed_count)
                    if t is not None)
 
     @staticmethod
@@ -163,8 +169,9 @@ class _Workspace:
         per_row += 4 * 3 * H * dh_store + 4 * d + 4 * d + 4 * F       # qkv, ctx, y, ffn
         words = (S + 31) // 32
         sched = 4 * (8 + 2 * B * H * ((S + 127) // 128)) if plan.attn_persistent else 0
+        packed = (4 * M + 4 * (B + 1) + 4 * ((M + 127) // 128) + 4) if plan.packed_ffn else 0
         return (M * per_row + 4 * B * words + 4 * B + 4 * ((M + 127) // 128) + 4
-                + _Workspace.sk_bytes(cfg, M, plan) + sched)
+                + _Workspace.sk_bytes(cfg, M, plan) + sched + packed)
 
 
 class FusedTransformer(LayerStack):
@@ -260,8 +267,13 @@ class FusedTransformer(LayerStack):
         # Padded rows: GEMMs compute only 128-row tiles holding a real token
         # and the (non-final) norms leave padded rows alone.
         skip_rows = keep_u8 is not None and plan.skip_padded_rows
-        lt = ws.live_tiles.data_ptr() if skip_rows else None
-        lc = ws.live_count.data_ptr() if skip_rows else None
+        lt = lt0 = ws.live_tiles.data_ptr() if skip_rows else None
+        lc = lc0 = ws.live_count.data_ptr() if skip_rows else None
+        # FFN over packed rows: a token's row in h_ffn1, ffn and FFN2's y is
+        # its rank among the batch's valid tokens (map built below).
+        pack = (keep is not None and plan.packed_ffn and split["ffn1"] and split["ffn2"])
+        rmap = ws.row_map.data_ptr() if pack else None
+        ptiles = (ws.packed_tiles.data_ptr(), ws.packed_count.data_ptr()) if pack else None
         # keep, gamma and beta are static for the forward (inputs copied and
         # weights synchronised before it starts): the norms load them before
         # waiting for the previous kernel.
@@ -302,7 +314,9 @@ class FusedTransformer(LayerStack):
                 ev1.record()
             n += 1
 
-        def gemm(kind, g, A, lda, W, bias, C, ldc, N, K, epi, flags, bn, hd_=0, hs_=0):
+        def gemm(kind, g, A, lda, W, bias, C, ldc, N, K, epi, flags, bn, hd_=0, hs_=0,
+                 tiles=None):
+            lt, lc = tiles if tiles is not None else (lt0, lc0)
             if split[g]:
                 if getattr(plan, f"sk_{g}"):
                     run(kind, L.kf_gemm_bf16x3_sk, A, lda, W.data_ptr(), K, bias.data_ptr(), C,
@@ -321,6 +335,9 @@ class FusedTransformer(LayerStack):
 
         if keep is not None:
             run("keep_bits", L.kf_keep_bits, keep, S, B, S, bits, st)
+        if pack:
+            run("keep_bits", L.kf_pack_rows, bits, B, S, rmap, ws.row_off.data_ptr(), ptiles[0],
+                ptiles[1], st)
         if skip_rows:
             run("keep_bits", L.kf_live_row_tiles, keep, M, lt, lc, st)
         sched = ws.sched.data_ptr() if plan.attn_persistent else None
@@ -356,13 +373,19 @@ class FusedTransformer(LayerStack):
                 run("attention", L.kf_flash_fwd_tf32, qkv, S * ldq, dhs, ldq,
                     qkv + 4 * H * dhs, S * ldq, dhs, ldq, qkv + 8 * H * dhs, S * ldq, dhs,
                     ldq, ctx, S * d, dh, d, bits, B, H, S, dhs, dh, dh ** -0.5, attn_flags, st)
-            # out_proj, then the residual add + mask + LN2.
+            # out_proj, then the residual add + mask + LN2 (its output at the
+            # tokens' packed rows when the FFN runs packed).
             gemm("out_proj", "out", ctx, d, lw["wo"], lw["bo"], y, d, d, d,
                  _lib.KF_EPI_BIAS, 0, plan.bn_out)
-            run("ln", L.kf_ln_add_mask, res, d, y, d, keep, lw["ln2w"].data_ptr(),
-                lw["ln2b"].data_ptr(), res, d, h_ffn1, d, M, d, lw["eps2"], f_ln2, st)
+            if pack:
+                run("ln", L.kf_ln_add_mask_rows, res, d, y, d, keep, lw["ln2w"].data_ptr(),
+                    lw["ln2b"].data_ptr(), res, d, h_ffn1, d, M, d, lw["eps2"],
+                    f_ln2 | _lib.KF_LN_H_MAPPED, rmap, st)
+            else:
+                run("ln", L.kf_ln_add_mask, res, d, y, d, keep, lw["ln2w"].data_ptr(),
+                    lw["ln2b"].data_ptr(), res, d, h_ffn1, d, M, d, lw["eps2"], f_ln2, st)
             gemm("ffn1", "ffn1", h_ffn1, d, lw["w1"], lw["b1"], ffn, F, F, d,
-                 _lib.KF_EPI_BIAS_GELU, f_ffn1_out, plan.bn_ffn1)
+                 _lib.KF_EPI_BIAS_GELU, f_ffn1_out, plan.bn_ffn1, tiles=ptiles)
             # FFN2, then the next layer's LN1 (or the final norm).
             if i == nl - 1:
                 nw, nb, ne = w.finw.data_ptr(), w.finb.data_ptr(), w.fin_eps
@@ -372,9 +395,13 @@ class FusedTransformer(LayerStack):
                 nw, nb, ne = nx["ln1w"].data_ptr(), nx["ln1b"].data_ptr(), nx["eps1"]
                 s_out, h_out, f_next = res, h_qkv, f_ln1
             gemm("ffn2", "ffn2", ffn, F, lw["w2"], lw["b2"], y, d, d, F, _lib.KF_EPI_BIAS, 0,
-                 plan.bn_ffn2)
-            run("ln", L.kf_ln_add_mask, res, d, y, d, keep, nw, nb, s_out, d, h_out, d, M, d,
-                ne, f_next, st)
+                 plan.bn_ffn2, tiles=ptiles)
+            if pack:
+                run("ln", L.kf_ln_add_mask_rows, res, d, y, d, keep, nw, nb, s_out, d, h_out, d,
+                    M, d, ne, f_next | _lib.KF_LN_Y_MAPPED, rmap, st)
+            else:
+                run("ln", L.kf_ln_add_mask, res, d, y, d, keep, nw, nb, s_out, d, h_out, d, M, d,
+                    ne, f_next, st)
         self.launches_per_forward = n
         return n
 

@@ -101,6 +101,25 @@ def test_bf16x3_gemm_rejects_unknown_flags_before_any_launch():
                                      None) == _lib.KF_E_INVALID
 
 
+def test_packed_row_entries_reject_bad_arguments_before_any_launch():
+    """kf_pack_rows and kf_ln_add_mask_rows check their arguments on the
+    host: null buffers, B outside [1, 65535], a missing row map or no map
+    flag are refused with KF_E_INVALID and no CUDA call; kf_ln_add_mask
+    refuses the map flags (they need the map)."""
+    lib = _lib.lib()
+    fake = ctypes.c_void_p(0x1000)
+    assert lib.kf_pack_rows(None, 2, 8, fake, fake, fake, fake, None) == _lib.KF_E_INVALID
+    assert lib.kf_pack_rows(fake, 0, 8, fake, fake, fake, fake, None) == _lib.KF_E_INVALID
+    assert lib.kf_pack_rows(fake, 65536, 8, fake, fake, fake, fake, None) == _lib.KF_E_INVALID
+    assert lib.kf_pack_rows(fake, 2, 8, fake, None, fake, fake, None) == _lib.KF_E_INVALID
+    ln = lambda fn, flags, rmap: fn(fake, 8, fake, 8, None, fake, fake, None, 0, fake, 8, 4, 8,
+                                    1e-5, flags, *(() if rmap is False else (rmap,)), None)
+    assert ln(lib.kf_ln_add_mask_rows, _lib.KF_LN_Y_MAPPED, None) == _lib.KF_E_INVALID
+    assert ln(lib.kf_ln_add_mask_rows, 0, fake) == _lib.KF_E_INVALID
+    assert b"row_map" in lib.kf_last_error()
+    assert ln(lib.kf_ln_add_mask, _lib.KF_LN_H_MAPPED, False) == _lib.KF_E_INVALID
+
+
 def test_noalloc_entry_rejects_bad_attention_arguments_before_any_launch():
     """kf_flash_fwd_tf32_keep_noalloc runs every check of the attention call
     before it queues the key-bit packer: an unsupported head_dim, an odd

@@ -1177,3 +1177,103 @@ def test_flash_sched_without_mask_and_long_rows():
         _attn_call(q, k, v, o, bits, _lib.KF_ATTN_CAUSAL, attn_schedule(bits, B, H, S))
         torch.cuda.synchronize()
         assert torch.equal(o, ref)
+
+
+def _pack_reference(keep):
+    """row_map, row_off and the packed tile count of a [B, S] keep mask."""
+    B, S = keep.shape
+    flat = keep.reshape(-1).bool()
+    rank = torch.cumsum(flat.to(torch.int64), 0) - 1
+    row_map = torch.where(flat, rank, torch.full_like(rank, -1)).to(torch.int32)
+    counts = keep.bool().sum(1).to(torch.int64)
+    row_off = torch.cat([torch.zeros(1, dtype=torch.int64, device=keep.device),
+                         torch.cumsum(counts, 0)]).to(torch.int32)
+    return row_map, row_off, (int(counts.sum()) + 127) // 128
+
+
+@pytest.mark.parametrize("B,S", [(1, 1), (3, 5), (8, 512), (64, 2048), (5, 3000), (2, 65536),
+                                 (40, 33)])
+@pytest.mark.parametrize("kind", ["prefix", "random", "empty_rows"])
+def test_pack_rows_matches_its_definition(B, S, kind):
+    """kf_pack_rows: each valid token's rank among all valid tokens in
+    row-major order, -1 for padding, the rows' offsets and the tile list of
+    the packed rows, for prefix masks, arbitrary masks and empty rows."""
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    torch.manual_seed(B * 7 + S)
+    if kind == "prefix":
+        lens = torch.randint(0, S + 1, (B,))
+        keep = (torch.arange(S)[None, :] < lens[:, None])
+    else:
+        keep = torch.rand(B, S) > 0.4
+        if kind == "empty_rows":
+            keep[::2] = False
+    keep = keep.to(torch.uint8).cuda()
+    bits = _bits_of(keep)
+    M = B * S
+    row_map = torch.full((M,), 7, dtype=torch.int32, device="cuda")
+    row_off = torch.full((B + 1,), 7, dtype=torch.int32, device="cuda")
+    tiles = torch.full(((M + 127) // 128,), -7, dtype=torch.int32, device="cuda")
+    count = torch.full((1,), -7, dtype=torch.int32, device="cuda")
+    _lib.check(L.kf_pack_rows(bits.data_ptr(), B, S, row_map.data_ptr(), row_off.data_ptr(),
+                              tiles.data_ptr(), count.data_ptr(), _lib.stream_ptr()), "pack")
+    torch.cuda.synchronize()
+    want_map, want_off, n = _pack_reference(keep)
+    assert torch.equal(row_map, want_map)
+    assert torch.equal(row_off, want_off)
+    assert count.item() == n
+    assert torch.equal(tiles[:n].cpu(), torch.arange(n, dtype=torch.int32))
+
+
+@pytest.mark.parametrize("M,d", [(300, 768), (517, 512), (1024, 1024), (200, 40)])
+@pytest.mark.parametrize("mode", ["h_planes", "y_mask_out", "both_fp32"])
+def test_ln_rows_map_matches_unmapped(M, d, mode):
+    """kf_ln_add_mask_rows equals kf_ln_add_mask bit for bit on every row:
+    its y read from, and / or its h written to, the row's packed position
+    (rows mapped to -1 have no y and write no h)."""
+    from techjam2026_b200 import _lib
+    L = _lib.lib()
+    torch.manual_seed(M + d)
+    x = torch.randn(M, d, device="cuda")
+    y = torch.randn(M, d, device="cuda")
+    g, b = torch.randn(d, device="cuda"), torch.randn(d, device="cuda")
+    keep = (torch.rand(M, device="cuda") > 0.3).to(torch.uint8)
+    row_map, _, _ = _pack_reference(keep[None, :])
+    T = int(keep.sum())
+    valid = keep.bool()
+    mapped = row_map[valid].long()
+    planes = mode == "h_planes"
+    flags = {"h_planes": _lib.KF_LN_OUT_BF16X2 | _lib.KF_LN_SKIP_PADDED,
+             "y_mask_out": _lib.KF_LN_MASK_OUT,
+             "both_fp32": _lib.KF_LN_SKIP_PADDED}[mode]
+    mflags = {"h_planes": _lib.KF_LN_H_MAPPED, "y_mask_out": _lib.KF_LN_Y_MAPPED,
+              "both_fp32": _lib.KF_LN_Y_MAPPED | _lib.KF_LN_H_MAPPED}[mode]
+
+    def new_h():
+        return (torch.full((2, M, d), 3, dtype=torch.int16, device="cuda") if planes
+                else torch.full((M, d), 3.0, device="cuda"))
+    s_a, h_a = x.clone(), new_h()
+    _lib.check(L.kf_ln_add_mask(s_a.data_ptr(), d, y.data_ptr(), d, keep.data_ptr(), g.data_ptr(),
+                                b.data_ptr(), s_a.data_ptr(), d, h_a.data_ptr(), d, M, d, 1e-5,
+                                flags, _lib.stream_ptr()), "ln")
+    # y in packed order for the mapped call
+    yp = torch.full((M, d), float("nan"), device="cuda")
+    if mflags & _lib.KF_LN_Y_MAPPED:
+        yp[mapped] = y[valid]
+    else:
+        yp = y
+    s_b, h_b = x.clone(), new_h()
+    _lib.check(L.kf_ln_add_mask_rows(s_b.data_ptr(), d, yp.data_ptr(), d, keep.data_ptr(),
+                                     g.data_ptr(), b.data_ptr(), s_b.data_ptr(), d, h_b.data_ptr(),
+                                     d, M, d, 1e-5, flags | mflags, row_map.data_ptr(),
+                                     _lib.stream_ptr()), "ln rows")
+    torch.cuda.synchronize()
+    assert torch.equal(s_a, s_b)
+    if mflags & _lib.KF_LN_H_MAPPED:
+        got = h_b[:, mapped] if planes else h_b[mapped]
+        want = h_a[:, valid] if planes else h_a[valid]
+        assert torch.equal(got, want)
+        rest = h_b[:, T:] if planes else h_b[T:]
+        assert torch.all(rest == 3)
+    else:
+        assert torch.equal(h_a, h_b)
