@@ -308,10 +308,10 @@ int kf_flash_fwd_tf32_sched(const float* q, int64_t q_sb, int64_t q_sh, int64_t 
 /* Capacity of the library's static key-bit scratch: 1 MiB per device. */
 #define KF_NOALLOC_KEEP_WORDS_MAX 262144
 
-/* kf_flash_fwd_tf32 for callers that cannot allocate device memory: code
- * running inside a global-mode stream capture (cudaMalloc is illegal there),
- * host functions enqueued with cudaLaunchHostFunc (no CUDA calls allowed) and
- * hosts whose device memory is a fixed arena they cannot grow. It takes the
+/* kf_flash_fwd_tf32 for callers that cannot allocate device memory: serving
+ * processes whose GPU memory is all in a fixed arena they cannot grow,
+ * latency-bound paths that cannot take the device-wide synchronisation of
+ * cudaMalloc/cudaFree, and FFI callers with no device allocator. It takes the
  * uint8 keep mask [B, S] (row stride ld_keep, required) instead of a
  * kf_keep_bits workspace and packs the key bits into a static device array of
  * the library (KF_NOALLOC_KEEP_WORDS_MAX words, held on every device that

@@ -2,12 +2,12 @@
 //
 // kf_flash_fwd_tf32 reads the packed key bits from a workspace the caller
 // allocates (kf_keep_bits_words(B, S) words). Some callers cannot allocate:
-//   * code running while a stream is captured in cudaStreamCaptureModeGlobal,
-//     where cudaMalloc is an illegal call that invalidates the capture;
-//   * host functions enqueued with cudaLaunchHostFunc, which may make no CUDA
-//     calls at all;
-//   * hosts whose device memory belongs to a fixed arena or pool they cannot
-//     grow (and FFI callers that have no device allocator of their own).
+//   * serving processes that hand nearly all of a GPU's memory to a fixed
+//     arena or pool at start-up, where one more cudaMalloc fails or splits
+//     the arena;
+//   * latency-bound paths that cannot take the device-wide synchronisation
+//     cudaMalloc and cudaFree may imply;
+//   * FFI callers (ctypes, cgo, JNI) that own no device allocator at all.
 // kf_flash_fwd_tf32_keep_noalloc takes the uint8 keep mask instead and packs
 // the bits into a static device array of this library, then runs the same
 // two kernels through the existing entry points (kf_keep_bits,

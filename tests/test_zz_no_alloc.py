@@ -1,6 +1,7 @@
 """kf_flash_fwd_tf32_keep_noalloc: the attention forward for callers that
-cannot allocate device memory (inside a global-mode stream capture, in a
-cudaLaunchHostFunc callback, or with a fixed device arena). It packs the key
+cannot allocate device memory (a serving process whose GPU memory is all in a
+fixed arena, a latency-bound path that cannot take cudaMalloc's device-wide
+synchronisation, an FFI caller with no device allocator). It packs the key
 bits into the library's static device scratch instead of a caller workspace.
 
 Checked through the C ABI against the existing entry points
